@@ -1,0 +1,400 @@
+#!/usr/bin/env python
+"""Benchmark: memboost quantize throughput on B200 (FP16 GB/s ingested).
+
+One step = quantize the Llama-7B MLP-shaped pair (11008x4096 and 4096x11008
+fp16, N(0, 0.02^2) with 0.05% Student-t(3) outliers, lognormal(0, 1.5)
+hessian_diag, ratio_4bit 0.1) -- synthetic, seeded, generated on the CPU.
+At N GPUs every rank quantizes its own copy (weak scaling, no collective on
+the data path); rank 0 prints one JSON line.
+
+  value      device-resident throughput: inputs already in HBM, the
+             QuantizePlan path (launch both matrices, one sync, CSR extract)
+  e2e        the public memboost_b200.quantize() call per matrix with host
+             buffers: pinned H2D copy of the weights and hessian, quantize,
+             D2H of every output tensor, inside the timed region
+  roofline   algorithmic bytes of one quantize call (3.0 B per weight plus
+             hessian, 2nd-order, CSR and precision bytes) / its CUDA-event
+             duration on the launching stream, against MEASURED_PEAKS.json
+  cpu_baseline  the CPU oracle (C++ restatement of the reference algorithm)
+             on all host cores, on the same matrices
+
+--impl reference times the reference algorithm on the host cores (the
+oracle port) for the same workload and, when the reference's own extension
+is built in oracle/_ref, its CUDA kernels on this GPU.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "FP16 GB/s quantized (Llama-7B MLP pair 11008x4096 + 4096x11008)"
+UNIT = "GB/s"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--e2e-steps", type=int, default=5)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def dist_setup():
+    import torch
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if ws > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return ws, rank, local
+
+
+def barrier(ws):
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(ws, x: float) -> float:
+    if ws == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+class ClockSampler:
+    """nvidia-smi samples of this GPU's clocks during the timed region."""
+
+    FIELDS = ("clocks.sm", "clocks.max.sm", "power.draw", "clocks_event_reasons.active",
+              "clocks_event_reasons.hw_slowdown", "clocks_event_reasons.hw_thermal_slowdown",
+              "clocks_event_reasons.sw_thermal_slowdown", "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        import torch
+        try:
+            self.index = "GPU-" + str(torch.cuda.get_device_properties(device_index).uuid)
+        except Exception:
+            self.index = str(device_index)
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), "--query-gpu=" + ",".join(self.FIELDS),
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        rows = []
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) == len(self.FIELDS):
+                rows.append(parts)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({n for r in rows for n, v in zip(names, r[4:8]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "power_w_max": max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
+                if any(r[2].replace(".", "").isdigit() for r in rows) else None,
+                "samples": len(rows), "reasons": reasons}
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        d = json.load(open(path))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def algorithmic_bytes(M: int, K: int, nnz: int, selecting: bool) -> int:
+    """Compulsory HBM bytes of one quantize call: W read once (2 B/weight),
+    packed 2-bit (4 B) and 4-bit (8 B) words, fp16 scale, int8 zero and uint8
+    2nd-order code per (row, group) -- 3.0 B per weight -- plus hessian
+    (4 B/column), 2nd-order scale+zero (3 B/chunk), CSR (6 B/outlier +
+    4 B/row) and group precision (1 B/group)."""
+    ng = (K + 15) // 16
+    ng2 = (M * ng + 255) // 256
+    return (2 * M * K + M * ng * (4 + 8 + 2 + 1 + 1) + (4 * K if selecting else 0) + 3 * ng2
+            + 6 * nnz + 4 * (M + 1) + ng)
+
+
+def cpu_baseline(cases, min_seconds=10.0):
+    from oracle import oracle
+    oracle.build()
+    n, t0 = 0, time.perf_counter()
+    nbytes = 0
+    while True:
+        for c in cases:
+            oracle.quantize(c.weights.numpy(), c.ratio_4bit, c.hessian_diag.numpy(), nthreads=0)
+            nbytes += 2 * c.weights.numel()
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds or n >= 50:
+            break
+    return {"value": round(nbytes / el / 1e9, 4), "unit": UNIT, "cores": os.cpu_count(),
+            "kind": "port",
+            "sample": f"oracle/mb_oracle.cpp on {os.cpu_count()} host threads, {n} x the "
+                      f"full pair ({'+'.join(c.name for c in cases)}), {el:.1f} s"}
+
+
+def run_ours(args, ws, rank, local):
+    import torch
+
+    import memboost_b200 as mb
+    from memboost_b200 import _C, workloads
+
+    dev = torch.device("cuda", local)
+    cases = workloads.mlp_7b()
+    W = [c.weights.to(dev) for c in cases]
+    H = [c.hessian_diag.to(dev) for c in cases]
+    plans = [_C.QuantizePlan(*w.shape, dev) for w in W]
+    fp16_bytes = sum(2 * w.numel() for w in W)
+    nnz_seen = []
+
+    def step(ev=None):
+        for i, (p, w, h, c) in enumerate(zip(plans, W, H, cases)):
+            if ev is not None:
+                ev[i][0].record()
+            p.launch(w, c.ratio_4bit, h)
+            if ev is not None:
+                ev[i][1].record()
+        res = [p.finish() for p in plans]
+        nnz_seen.append([int(r[8].numel()) for r in res])
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    per_call = [[] for _ in plans]
+    events = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in plans]
+              for _ in range(args.steps)]
+    barrier(ws)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for k in range(args.steps):
+            step(events[k])
+        t1.record()
+        torch.cuda.synchronize()
+    barrier(ws)
+    ms_local = t0.elapsed_time(t1)
+    ms = max_over_ranks(ws, ms_local)
+    for k in range(args.steps):
+        for i in range(len(plans)):
+            per_call[i].append(events[k][i][0].elapsed_time(events[k][i][1]))
+    value = fp16_bytes * args.steps * ws / (ms / 1e3) / 1e9
+
+    # roofline of the quantize call (all its kernels, one stream)
+    peak, peak_kind = peaks()
+    nnz = nnz_seen[-1]
+    alg = [algorithmic_bytes(*w.shape, n, True) for w, n in zip(W, nnz)]
+    dur = [statistics.mean(x) for x in per_call]
+    achieved = sum(alg) / (sum(dur) / 1e3) / 1e9
+    launches_per_step = sum(6 + (1 if n > 0 else 0) for n in nnz)
+
+    # e2e: public API, host buffers, copies in the timed region
+    e2e = None
+    if args.e2e_steps > 0:
+        hw = [c.weights.pin_memory() for c in cases]
+        hh = [c.hessian_diag.pin_memory() for c in cases]
+        h2d = sum(t.numel() * t.element_size() for t in hw + hh)
+        d2h_holder = {}
+
+        def e2e_step():
+            outs = []
+            for wh, hhh, c in zip(hw, hh, cases):
+                wd = wh.to(dev, non_blocking=True)
+                hd = hhh.to(dev, non_blocking=True)
+                qt = mb.quantize(wd, c.ratio_4bit, hd)
+                sd = {k: v.to("cpu", non_blocking=True) for k, v in qt.state_dict().items()
+                      if isinstance(v, torch.Tensor) and v.is_cuda}
+                outs.append(sd)
+            torch.cuda.synchronize()
+            d2h_holder["bytes"] = sum(v.numel() * v.element_size() for sd in outs
+                                      for v in sd.values())
+
+        for _ in range(2):
+            e2e_step()
+        barrier(ws)
+        torch.cuda.synchronize()
+        a = time.perf_counter()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize()
+        ems = max_over_ranks(ws, e0.elapsed_time(e1))
+        e2e = {"value": round(fp16_bytes * args.e2e_steps * ws / (ems / 1e3) / 1e9, 3),
+               "unit": UNIT, "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h_holder["bytes"], "steps": args.e2e_steps,
+               "ms_per_step": round(ems / args.e2e_steps, 3),
+               "path": "memboost_b200.quantize() per matrix (C ABI), pinned host buffers"}
+        _ = a
+
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": ws,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16->u8/i32",
+        "data": "synthetic (seeded N(0,0.02^2) + Student-t(3) outliers, lognormal hessian)",
+        "config": {"workload": "mlp_7b pair: 11008x4096 + 4096x11008 fp16, ratio_4bit 0.1, "
+                               "hessian_diag lognormal(0,1.5), 16-col groups",
+                   "per_rank_fp16_bytes": fp16_bytes,
+                   "l2": "per-step inputs 180 MB > 126 MB L2; not flushed",
+                   "parallelism": f"{ws} independent ranks (weak scaling)"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "peak_kind": peak_kind, "traffic": None,
+                     "kernel": "quantize call (stats+select+params+second_order+encode+rowscan)",
+                     "algorithmic_bytes_per_call": alg,
+                     "call_ms": [round(d, 4) for d in dur]},
+        "gpu_launches": launches_per_step * args.steps,
+        "nnz": nnz,
+        "clocks": clk.summary(),
+    }
+    if e2e:
+        line["e2e"] = e2e
+    return line, cases
+
+
+def run_reference_arm(args, ws, rank, local):
+    """Reference algorithm on the host cores (oracle port) + the reference's
+    own CUDA kernels on this GPU when built in oracle/_ref."""
+    import torch
+
+    from memboost_b200 import workloads
+    from oracle import oracle
+
+    oracle.build()
+    cases = workloads.mlp_7b()
+    fp16 = sum(2 * c.weights.numel() for c in cases)
+    wn = [c.weights.numpy() for c in cases]
+    hn = [c.hessian_diag.numpy() for c in cases]
+    t_one = time.perf_counter()
+    for w, h, c in zip(wn, hn, cases):
+        oracle.quantize(w, c.ratio_4bit, h, nthreads=0)
+    t_one = time.perf_counter() - t_one
+    # bounded sample per step: whole pair if a step is short, else row slices
+    frac = min(1.0, 6.0 / max(t_one, 1e-6))
+    rows = [max(256, int(w.shape[0] * frac)) for w in wn]
+    sample = [np.ascontiguousarray(w[:r]) for w, r in zip(wn, rows)] if frac < 1 else wn
+    step_bytes = sum(2 * s.size for s in sample)
+    for _ in range(args.warmup):
+        for s, h, c in zip(sample, hn, cases):
+            oracle.quantize(s, c.ratio_4bit, h, nthreads=0)
+    a = time.perf_counter()
+    for _ in range(args.steps):
+        for s, h, c in zip(sample, hn, cases):
+            oracle.quantize(s, c.ratio_4bit, h, nthreads=0)
+    el = time.perf_counter() - a
+    value = step_bytes * args.steps / el / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT,
+        "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(el / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp16->u8/i32", "data": "synthetic",
+        "config": {"workload": "mlp_7b pair: 11008x4096 + 4096x11008 fp16, ratio_4bit 0.1",
+                   "per_step_sample_rows": rows},
+        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": os.cpu_count(),
+                         "kind": "port",
+                         "sample": f"oracle/mb_oracle.cpp (reference algorithm) on "
+                                   f"{os.cpu_count()} host threads, rows {rows} of the pair"},
+        "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    # the reference's own CUDA kernels, built from its sources, on this GPU
+    try:
+        from oracle import build_ref
+        ref = build_ref.load()
+        dev = torch.device("cuda", local)
+        W = [c.weights.to(dev) for c in cases]
+        H = [c.hessian_diag.to(dev) for c in cases]
+        for _ in range(3):
+            for w, h, c in zip(W, H, cases):
+                ref.quantize(w, c.ratio_4bit, h)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n = max(3, min(args.steps, 10))
+        e0.record()
+        for _ in range(n):
+            for w, h, c in zip(W, H, cases):
+                ref.quantize(w, c.ratio_4bit, h)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        line["reference_cuda_b200"] = {
+            "value": round(fp16 * n / (ms / 1e3) / 1e9, 3), "unit": UNIT,
+            "ms_per_step": round(ms / n, 3),
+            "what": "reference core/*.cu compiled for sm_100a (oracle/build_ref.py), "
+                    "_C.quantize on the same pair, CUDA events, device-resident inputs"}
+    except Exception as e:  # not built here
+        line["reference_cuda_b200"] = {"unavailable": str(e)[:200]}
+    return line
+
+
+def main():
+    args = parse()
+    ws, rank, local = dist_setup()
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(run_reference_arm(args, ws, rank, local)), flush=True)
+        return
+    line, cases = run_ours(args, ws, rank, local)
+    if rank == 0:
+        if ws == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(cases)
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

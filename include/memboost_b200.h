@@ -1,0 +1,128 @@
+/*
+ * memboost_b200 -- C ABI of the B200-native (sm_100a) memboost quantization
+ * hot path.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream; no
+ * torch types cross this boundary.  All work is enqueued on `stream` (may be
+ * NULL for the legacy default stream); entry points return without a device
+ * synchronisation unless stated otherwise.  The caller owns every buffer.
+ *
+ * Each function names the reference interface it replaces (paths are inside
+ * the reference project: core/torch_ops.h, core/bindings.cpp,
+ * core/torch_ops.cu).  Data layouts are the reference's QuantizedTensor
+ * layout (memboost/formats.py:20-42):
+ *   ng  = ceil(K / 16)            1st-order groups per row
+ *   ng2 = ceil(M * ng / 256)      2nd-order groups
+ *   packed_2bit       int32 [M, ng]     element j of a group at bits [2j, 2j+2)
+ *   packed_4bit       int32 [M, 2*ng]   word 2g = cols 0-7, 2g+1 = cols 8-15,
+ *                                       element j at bits [4j, 4j+4)
+ *   scales_1st        fp16  [M, ng]
+ *   zeros_1st         int8  [M, ng]
+ *   scales_2nd        fp16  [ng2]
+ *   zeros_2nd         int8  [ng2]
+ *   scales_1st_quant  uint8 [M, ng]
+ *   group_precision   uint8 [ng]        0 = 2-bit, 1 = 4-bit
+ *   outlier_values    fp16  [nnz]       CSR, ascending column within a row
+ *   outlier_col_indices int32 [nnz]
+ *   outlier_row_ptrs  int32 [M + 1]
+ */
+#ifndef MEMBOOST_B200_H_
+#define MEMBOOST_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* mb_stream_t; /* == cudaStream_t */
+
+typedef enum {
+  MB_OK = 0,
+  MB_ERR_INVALID_ARGUMENT = 1, /* a TORCH_CHECK of the reference would fire */
+  MB_ERR_CUDA = 2,             /* a CUDA runtime call or launch failed */
+  MB_ERR_WORKSPACE = 3,        /* workspace missing or too small */
+  MB_ERR_DEVICE_STATUS = 4     /* a kernel reported an error status */
+} mb_status;
+
+/* Text of the last error raised on the calling host thread ("" if none). */
+const char* mb_last_error(void);
+
+/* Library version string ("memboost_b200 <version> sm_100a"). */
+const char* mb_version(void);
+
+/* ---------------------------------------------------------------------------
+ * quantize -- replaces memboost::quantize_op (core/torch_ops.h:18-22,
+ * core/torch_ops.cu:105-264; bound as _C.quantize in core/bindings.cpp:25-29).
+ *
+ * Two calls, because the CSR outputs are sized by the outlier count:
+ *   1. mb_quantize() writes every output except outlier_values /
+ *      outlier_col_indices, writes outlier_row_ptrs [M+1] and the outlier
+ *      count to *nnz_device (int32, device memory).
+ *   2. When nnz > 0 the caller allocates the CSR arrays and calls
+ *      mb_quantize_extract_outliers() with the same weights and workspace.
+ * ratio_4bit, hessian_diag: as the reference -- sensitivity-based 4-bit
+ * selection runs only when hessian_diag != NULL, hessian_numel > 0 and
+ * ratio_4bit > 0; hessian_diag must then hold >= K fp32 values.
+ * The workspace (device memory, any contents) must hold
+ * mb_quantize_workspace_size(M, K) bytes and stay untouched between the two
+ * calls.  Scratch use: per-group statistics, sensitivities, selection,
+ * per-group parameters, 2nd-order tables and per-row outlier counts.
+ * ------------------------------------------------------------------------- */
+size_t mb_quantize_workspace_size(int64_t M, int64_t K);
+
+mb_status mb_quantize(const void* weights_fp16, int64_t M, int64_t K, double ratio_4bit,
+                      const float* hessian_diag, int64_t hessian_numel,
+                      int32_t* packed_2bit, int32_t* packed_4bit, void* scales_1st_fp16,
+                      int8_t* zeros_1st, void* scales_2nd_fp16, int8_t* zeros_2nd,
+                      uint8_t* scales_1st_quant, uint8_t* group_precision,
+                      int32_t* outlier_row_ptrs, int32_t* nnz_device, void* workspace,
+                      size_t workspace_bytes, mb_stream_t stream);
+
+/* Phase 2 of quantize -- core/torch_ops.cu:231-248 (extract_outliers). */
+mb_status mb_quantize_extract_outliers(const void* weights_fp16, int64_t M, int64_t K,
+                                       const int32_t* outlier_row_ptrs,
+                                       void* outlier_values_fp16,
+                                       int32_t* outlier_col_indices, const void* workspace,
+                                       size_t workspace_bytes, mb_stream_t stream);
+
+/* Host-side flags of the last mb_quantize on `workspace` (synchronises the
+ * stream).  Bit 0: the 4-bit selection met a tie of equal sensitivities at
+ * the selection boundary and broke it by lowest group index (the reference
+ * breaks such ties by std::sort's unspecified order). */
+mb_status mb_quantize_flags(const void* workspace, size_t workspace_bytes, int64_t M, int64_t K,
+                            uint32_t* flags, mb_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * dequantize -- replaces memboost::dequantize_op (core/torch_ops.h:24-29,
+ * core/torch_ops.cu:267-301; bound as _C.dequantize, core/bindings.cpp:31-38).
+ * out[r, c] = fp16(float(scales_1st[r, g]) * (q - zeros_1st[r, g])), no
+ * outlier add-back.
+ * ------------------------------------------------------------------------- */
+mb_status mb_dequantize(const int32_t* packed_2bit, const int32_t* packed_4bit,
+                        const void* scales_1st_fp16, const int8_t* zeros_1st,
+                        const uint8_t* group_precision, int64_t M, int64_t K, void* out_fp16,
+                        mb_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * pack / unpack -- replace memboost::pack_2bit_op, unpack_2bit_op,
+ * pack_4bit_op, unpack_4bit_op (core/torch_ops.h:10-15,
+ * core/torch_ops.cu:20-102; bound in core/bindings.cpp:9-22).
+ * Device buffers.  pack: n_values % 16 == 0 (2-bit) or % 8 == 0 (4-bit).
+ * unpack: num_elements <= 16 * n_words (2-bit) or 8 * n_words (4-bit).
+ * ------------------------------------------------------------------------- */
+mb_status mb_pack_2bit(const uint8_t* values, int64_t n_values, int32_t* packed,
+                       mb_stream_t stream);
+mb_status mb_unpack_2bit(const int32_t* packed, int64_t n_words, int64_t num_elements,
+                         uint8_t* values, mb_stream_t stream);
+mb_status mb_pack_4bit(const uint8_t* values, int64_t n_values, int32_t* packed,
+                       mb_stream_t stream);
+mb_status mb_unpack_4bit(const int32_t* packed, int64_t n_words, int64_t num_elements,
+                         uint8_t* values, mb_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MEMBOOST_B200_H_ */

@@ -1,0 +1,300 @@
+"""ctypes binding of libmemboost_b200.so -- the replacement for the
+reference's pybind11 module ``memboost._C`` (core/bindings.cpp:6-39).
+
+The six functions here take and return torch tensors with the reference's
+names, argument meaning, output devices and error messages
+(core/torch_ops.cu:20-301); underneath, each calls the C ABI of
+include/memboost_b200.h on torch's current CUDA stream of the input's device.
+There is no CPU implementation: if the library is missing the import fails,
+and the ops require CUDA tensors (pack/unpack copy CPU inputs to the current
+CUDA device first, and return CPU tensors as the reference does).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+
+_LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libmemboost_b200.so")
+
+if not os.path.exists(_LIB_PATH):
+    raise ImportError(
+        f"memboost_b200: native library {_LIB_PATH} is missing; build it with "
+        "`python -m memboost_b200.build` (there is no CPU fallback)")
+
+_lib = ctypes.CDLL(_LIB_PATH)
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_lib.mb_last_error.restype = ctypes.c_char_p
+_lib.mb_version.restype = ctypes.c_char_p
+_lib.mb_quantize_workspace_size.restype = ctypes.c_size_t
+_lib.mb_quantize_workspace_size.argtypes = [_I64, _I64]
+_lib.mb_quantize.restype = ctypes.c_int
+_lib.mb_quantize.argtypes = [_P, _I64, _I64, ctypes.c_double, _P, _I64,
+                             _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P]
+_lib.mb_quantize_extract_outliers.restype = ctypes.c_int
+_lib.mb_quantize_extract_outliers.argtypes = [_P, _I64, _I64, _P, _P, _P, _P, ctypes.c_size_t, _P]
+_lib.mb_quantize_flags.restype = ctypes.c_int
+_lib.mb_quantize_flags.argtypes = [_P, ctypes.c_size_t, _I64, _I64,
+                                   ctypes.POINTER(ctypes.c_uint32), _P]
+_lib.mb_dequantize.restype = ctypes.c_int
+_lib.mb_dequantize.argtypes = [_P, _P, _P, _P, _P, _I64, _I64, _P, _P]
+for _n in ("mb_pack_2bit", "mb_pack_4bit"):
+    getattr(_lib, _n).restype = ctypes.c_int
+    getattr(_lib, _n).argtypes = [_P, _I64, _P, _P]
+for _n in ("mb_unpack_2bit", "mb_unpack_4bit"):
+    getattr(_lib, _n).restype = ctypes.c_int
+    getattr(_lib, _n).argtypes = [_P, _I64, _I64, _P, _P]
+
+GROUP_SIZE_1ST = 16
+GROUP_SIZE_2ND = 256
+LIB_PATH = _LIB_PATH
+
+# mb_quantize_flags bit 0: a tie of equal sensitivities straddled the 4-bit
+# selection boundary (broken by lowest group index).
+FLAG_SELECTION_TIE = 1
+
+
+def version() -> str:
+    return _lib.mb_version().decode()
+
+
+def _check(status: int) -> None:
+    if status != 0:
+        raise RuntimeError(_lib.mb_last_error().decode() or f"memboost_b200 error {status}")
+
+
+def _ptr(t: torch.Tensor | None):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(device: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _to_cuda(t: torch.Tensor) -> torch.Tensor:
+    if t.is_cuda:
+        return t.contiguous()
+    if not torch.cuda.is_available():
+        raise RuntimeError("memboost_b200 requires a CUDA device")
+    return t.contiguous().to(torch.device("cuda", torch.cuda.current_device()))
+
+
+# ---- pack / unpack (core/torch_ops.cu:20-102) ----
+
+def _pack(values: torch.Tensor, per: int, fn) -> torch.Tensor:
+    if values.dtype != torch.uint8:
+        raise RuntimeError("values must be uint8")
+    if values.dim() != 1:
+        raise RuntimeError("values must be 1D")
+    if values.size(0) % per != 0:
+        raise RuntimeError(f"length must be multiple of {per}")
+    n = values.size(0)
+    if n == 0:
+        return torch.zeros(0, dtype=torch.int32)
+    v = _to_cuda(values)
+    with torch.cuda.device(v.device):
+        out = torch.empty(n // per, dtype=torch.int32, device=v.device)
+        _check(fn(_ptr(v), n, _ptr(out), _stream(v.device)))
+    return out.cpu()
+
+
+def _unpack(packed: torch.Tensor, num_elements: int, per: int, fn) -> torch.Tensor:
+    if packed.dtype != torch.int32:
+        raise RuntimeError("packed must be int32")
+    if packed.dim() != 1:
+        raise RuntimeError("packed must be 1D")
+    num_elements = int(num_elements)
+    if num_elements > packed.size(0) * per:
+        raise RuntimeError("num_elements too large")
+    if num_elements < 0:
+        raise RuntimeError("num_elements must be non-negative")
+    if num_elements == 0:
+        return torch.zeros(0, dtype=torch.uint8)
+    p = _to_cuda(packed)
+    with torch.cuda.device(p.device):
+        out = torch.empty(num_elements, dtype=torch.uint8, device=p.device)
+        _check(fn(_ptr(p), p.size(0), num_elements, _ptr(out), _stream(p.device)))
+    return out.cpu()
+
+
+def pack_2bit(values: torch.Tensor) -> torch.Tensor:
+    return _pack(values, 16, _lib.mb_pack_2bit)
+
+
+def unpack_2bit(packed: torch.Tensor, num_elements: int) -> torch.Tensor:
+    return _unpack(packed, num_elements, 16, _lib.mb_unpack_2bit)
+
+
+def pack_4bit(values: torch.Tensor) -> torch.Tensor:
+    return _pack(values, 8, _lib.mb_pack_4bit)
+
+
+def unpack_4bit(packed: torch.Tensor, num_elements: int) -> torch.Tensor:
+    return _unpack(packed, num_elements, 8, _lib.mb_unpack_4bit)
+
+
+# ---- quantize (core/torch_ops.cu:105-264) ----
+
+class QuantizeWorkspace:
+    """Device scratch for mb_quantize, reusable across calls of one shape."""
+
+    def __init__(self, M: int, K: int, device: torch.device):
+        self.M, self.K = M, K
+        self.nbytes = int(_lib.mb_quantize_workspace_size(M, K))
+        self.buf = torch.empty(self.nbytes, dtype=torch.uint8, device=device)
+        self.nnz = torch.empty(1, dtype=torch.int32, device=device)
+
+    def flags(self) -> int:
+        f = ctypes.c_uint32(0)
+        _check(_lib.mb_quantize_flags(_ptr(self.buf), self.nbytes, self.M, self.K,
+                                      ctypes.byref(f), _stream(self.buf.device)))
+        return int(f.value)
+
+
+def quantize(weights: torch.Tensor, ratio_4bit: float = 0.1,
+             hessian_diag: torch.Tensor | None = None,
+             workspace: QuantizeWorkspace | None = None) -> list:
+    """Returns the reference's 11-tensor list (core/torch_ops.cu:251-263)."""
+    if weights.dtype != torch.float16:
+        raise RuntimeError("weights must be float16")
+    if weights.dim() != 2:
+        raise RuntimeError("weights must be 2D [M, K]")
+    if not weights.is_cuda:
+        raise RuntimeError("weights must be on CUDA")
+    weights = weights.contiguous()
+    M, K = int(weights.size(0)), int(weights.size(1))
+    if M == 0 or K == 0:
+        raise RuntimeError("weights must be non-empty")
+    dev = weights.device
+    ratio_4bit = float(ratio_4bit)
+    h = None
+    if hessian_diag is not None and hessian_diag.numel() > 0 and ratio_4bit > 0.0:
+        if hessian_diag.dtype != torch.float32:
+            raise RuntimeError("hessian_diag must be float32")
+        if not hessian_diag.is_cuda:
+            raise RuntimeError("hessian_diag must be on CUDA")
+        if hessian_diag.device != dev:
+            raise RuntimeError("hessian_diag must be on the same device as weights")
+        if hessian_diag.numel() < K:
+            raise RuntimeError("hessian_diag must hold at least K values")
+        h = hessian_diag.contiguous().reshape(-1)
+    ng = (K + GROUP_SIZE_1ST - 1) // GROUP_SIZE_1ST
+    ng2 = (M * ng + GROUP_SIZE_2ND - 1) // GROUP_SIZE_2ND
+    with torch.cuda.device(dev):
+        if workspace is None or workspace.M != M or workspace.K != K or workspace.buf.device != dev:
+            workspace = QuantizeWorkspace(M, K, dev)
+        packed_2bit = torch.empty((M, ng), dtype=torch.int32, device=dev)
+        packed_4bit = torch.empty((M, 2 * ng), dtype=torch.int32, device=dev)
+        scales_1st = torch.empty((M, ng), dtype=torch.float16, device=dev)
+        zeros_1st = torch.empty((M, ng), dtype=torch.int8, device=dev)
+        scales_2nd = torch.empty((ng2,), dtype=torch.float16, device=dev)
+        zeros_2nd = torch.empty((ng2,), dtype=torch.int8, device=dev)
+        scales_1st_quant = torch.empty((M, ng), dtype=torch.uint8, device=dev)
+        group_precision = torch.empty((ng,), dtype=torch.uint8, device=dev)
+        row_ptrs = torch.empty((M + 1,), dtype=torch.int32, device=dev)
+        s = _stream(dev)
+        _check(_lib.mb_quantize(
+            _ptr(weights), M, K, ratio_4bit, _ptr(h), 0 if h is None else h.numel(),
+            _ptr(packed_2bit), _ptr(packed_4bit), _ptr(scales_1st), _ptr(zeros_1st),
+            _ptr(scales_2nd), _ptr(zeros_2nd), _ptr(scales_1st_quant), _ptr(group_precision),
+            _ptr(row_ptrs), _ptr(workspace.nnz), _ptr(workspace.buf), workspace.nbytes, s))
+        nnz = int(workspace.nnz.item())
+        if nnz > 0:
+            outlier_values = torch.empty((nnz,), dtype=torch.float16, device=dev)
+            outlier_col_indices = torch.empty((nnz,), dtype=torch.int32, device=dev)
+            _check(_lib.mb_quantize_extract_outliers(
+                _ptr(weights), M, K, _ptr(row_ptrs), _ptr(outlier_values),
+                _ptr(outlier_col_indices), _ptr(workspace.buf), workspace.nbytes, s))
+        else:
+            outlier_values = torch.empty((0,), dtype=torch.float16, device=dev)
+            outlier_col_indices = torch.empty((0,), dtype=torch.int32, device=dev)
+    return [packed_2bit, packed_4bit, scales_1st, zeros_1st, scales_2nd, zeros_2nd,
+            scales_1st_quant, group_precision, outlier_values, outlier_col_indices, row_ptrs]
+
+
+# ---- dequantize (core/torch_ops.cu:267-301) ----
+
+def dequantize(packed_2bit: torch.Tensor, packed_4bit: torch.Tensor, scales_1st: torch.Tensor,
+               zeros_1st: torch.Tensor, group_precision: torch.Tensor, M: int, K: int,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    if not packed_2bit.is_cuda:
+        raise RuntimeError("packed_2bit must be on CUDA")
+    if packed_2bit.dtype != torch.int32:
+        raise RuntimeError("packed_2bit must be int32")
+    M, K = int(M), int(K)
+    if M <= 0 or K <= 0:
+        raise RuntimeError("M and K must be positive")
+    dev = packed_2bit.device
+    ng = (K + GROUP_SIZE_1ST - 1) // GROUP_SIZE_1ST
+    expect = ((packed_2bit, torch.int32, M * ng, "packed_2bit"),
+              (packed_4bit, torch.int32, 2 * M * ng, "packed_4bit"),
+              (scales_1st, torch.float16, M * ng, "scales_1st"),
+              (zeros_1st, torch.int8, M * ng, "zeros_1st"),
+              (group_precision, torch.uint8, ng, "group_precision"))
+    for t, dt, n, name in expect:
+        if t.device != dev:
+            raise RuntimeError(f"{name} must be on the same CUDA device as packed_2bit")
+        if t.dtype != dt:
+            raise RuntimeError(f"{name} must be {str(dt).replace('torch.', '')}")
+        if t.numel() < n:
+            raise RuntimeError(f"{name} too small for M={M}, K={K}")
+    with torch.cuda.device(dev):
+        args = [t.contiguous() for t, *_ in expect]
+        if out is None:
+            out = torch.empty((M, K), dtype=torch.float16, device=dev)
+        _check(_lib.mb_dequantize(*[_ptr(a) for a in args], M, K, _ptr(out), _stream(dev)))
+    return out
+
+
+class QuantizePlan:
+    """Preallocated outputs and workspace for repeatedly quantizing [M, K]
+    matrices on one device (whole-model loops, benchmarks).
+
+    ``launch`` enqueues phase 1 (every output except the CSR arrays) on the
+    current stream without synchronising; ``finish`` reads the outlier count
+    (one stream synchronisation) and extracts the CSR arrays.  Launching
+    several plans before finishing any keeps the GPU busy across matrices.
+    The tensors returned by ``finish`` alias the plan's buffers until the
+    next ``launch``.
+    """
+
+    def __init__(self, M: int, K: int, device=None):
+        device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        self.M, self.K, self.device = M, K, device
+        ng = (K + GROUP_SIZE_1ST - 1) // GROUP_SIZE_1ST
+        ng2 = (M * ng + GROUP_SIZE_2ND - 1) // GROUP_SIZE_2ND
+        e = lambda shape, dt: torch.empty(shape, dtype=dt, device=device)  # noqa: E731
+        self.ws = QuantizeWorkspace(M, K, device)
+        self.out = [e((M, ng), torch.int32), e((M, 2 * ng), torch.int32), e((M, ng), torch.float16),
+                    e((M, ng), torch.int8), e((ng2,), torch.float16), e((ng2,), torch.int8),
+                    e((M, ng), torch.uint8), e((ng,), torch.uint8)]
+        self.row_ptrs = e((M + 1,), torch.int32)
+        self._w = None
+
+    def launch(self, weights: torch.Tensor, ratio_4bit: float = 0.1,
+               hessian_diag: torch.Tensor | None = None) -> None:
+        assert weights.dtype == torch.float16 and weights.is_contiguous()
+        assert tuple(weights.shape) == (self.M, self.K) and weights.device == self.device
+        h = hessian_diag if (hessian_diag is not None and hessian_diag.numel() > 0
+                             and ratio_4bit > 0) else None
+        o = self.out
+        _check(_lib.mb_quantize(
+            _ptr(weights), self.M, self.K, float(ratio_4bit), _ptr(h),
+            0 if h is None else h.numel(), _ptr(o[0]), _ptr(o[1]), _ptr(o[2]), _ptr(o[3]),
+            _ptr(o[4]), _ptr(o[5]), _ptr(o[6]), _ptr(o[7]), _ptr(self.row_ptrs),
+            _ptr(self.ws.nnz), _ptr(self.ws.buf), self.ws.nbytes, _stream(self.device)))
+        self._w = weights
+
+    def finish(self) -> list:
+        nnz = int(self.ws.nnz.item())
+        dev = self.device
+        vals = torch.empty((nnz,), dtype=torch.float16, device=dev)
+        cols = torch.empty((nnz,), dtype=torch.int32, device=dev)
+        if nnz > 0:
+            _check(_lib.mb_quantize_extract_outliers(
+                _ptr(self._w), self.M, self.K, _ptr(self.row_ptrs), _ptr(vals), _ptr(cols),
+                _ptr(self.ws.buf), self.ws.nbytes, _stream(dev)))
+        return [*self.out, vals, cols, self.row_ptrs]

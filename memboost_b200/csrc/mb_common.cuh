@@ -1,0 +1,66 @@
+// Shared helpers for the memboost_b200 sm_100a kernels and their C-ABI
+// wrappers: error reporting, launch checks and small device utilities.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include "memboost_b200.h"
+
+namespace mb {
+
+constexpr int kGroup1 = 16;   // 1st-order group width (columns)
+constexpr int kGroup2 = 256;  // 2nd-order group length (flattened scales)
+
+// Records `msg` as the calling thread's last error and returns `st`.
+mb_status set_error(mb_status st, const std::string& msg);
+void clear_error();
+
+__host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+__host__ __device__ inline int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
+__host__ __device__ inline int64_t max64(int64_t a, int64_t b) { return a > b ? a : b; }
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+#define MB_CUDA_TRY(expr)                                                             \
+  do {                                                                                \
+    cudaError_t _e = (expr);                                                          \
+    if (_e != cudaSuccess)                                                            \
+      return ::mb::set_error(MB_ERR_CUDA, std::string("CUDA error: ") +               \
+                                              cudaGetErrorString(_e) + " at " #expr); \
+  } while (0)
+
+#define MB_LAUNCH_CHECK(name)                                                            \
+  do {                                                                                   \
+    cudaError_t _e = cudaGetLastError();                                                 \
+    if (_e != cudaSuccess)                                                               \
+      return ::mb::set_error(MB_ERR_CUDA, std::string("CUDA error: ") +                  \
+                                              cudaGetErrorString(_e) + " launching " name); \
+  } while (0)
+
+#define MB_REQUIRE(cond, msg)                                                  \
+  do {                                                                         \
+    if (!(cond)) return ::mb::set_error(MB_ERR_INVALID_ARGUMENT, (msg));       \
+  } while (0)
+
+// ---- device helpers ----
+
+__device__ __forceinline__ float warp_min(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fminf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// float -> int32 with the semantics of a C cast compiled for the GPU
+// (cvt.rzi.s32.f32: truncate, saturate, NaN -> 0).
+__device__ __forceinline__ int f2i_rz(float x) { return __float2int_rz(x); }
+
+}  // namespace mb

@@ -1,0 +1,102 @@
+"""Seeded parity cases shared by the GPU parity tests and the golden-fixture
+generator (tests/golden/make_golden.py).  Each case is (name, weights fp16
+[M, K] numpy, ratio_4bit, hessian_diag fp32 numpy or None)."""
+from __future__ import annotations
+
+import numpy as np
+
+from memboost_b200 import workloads
+
+
+def _np_case(mc):
+    return mc.weights.numpy(), mc.ratio_4bit, mc.hessian_diag.numpy()
+
+
+def fma_probe(seed: int = 0, M: int = 32, n_groups: int = 6) -> np.ndarray:
+    """A matrix whose outlier set differs between the two candidate
+    evaluations of the reference's outlier test (quantize.cu:192-194):
+    |w - scale*(q-zero)| with the product rounded first, or fused into the
+    subtraction.  Each 16-column group is all-positive (zero point clamped to
+    0), holds its min and max, and is filled with fp16 values whose error sits
+    on the threshold so that the two evaluations disagree."""
+    F = np.float32
+    allw = np.arange(65536, dtype=np.uint16).view(np.float16).astype(np.float32)
+    allw = allw[np.isfinite(allw)]
+    rng = np.random.default_rng(seed)
+    W = np.zeros((M, 16 * n_groups), np.float16)
+    g = 0
+    while g < n_groups:
+        gmin = F(np.float16(rng.uniform(0.001, 0.3)))
+        gmax = F(np.float16(gmin + rng.uniform(0.001, 0.3)))
+        if not gmax > gmin:
+            continue
+        scale = F(F(gmax - gmin) / F(3))
+        thr = F(F(0.4) * F(gmax - gmin))
+        w = allw[(allw >= gmin) & (allw <= gmax)]
+        with np.errstate(invalid="ignore"):
+            a = (w - gmin).astype(F) / scale
+        q = np.clip(np.floor(a.astype(np.float64) + 0.5), 0, 3).astype(F)  # roundf for a >= 0
+        sep = np.abs((w - (scale * q).astype(F)).astype(F))
+        fused = np.abs((w.astype(np.float64) - np.float64(scale) * q.astype(np.float64)).astype(F))
+        d = (sep > thr) != (fused > thr)
+        if not d.any():
+            continue
+        cand = w[d]
+        blk = rng.choice(cand, size=(M, 16)).astype(np.float16)
+        blk[0, 0] = np.float16(gmin)
+        blk[1, 0] = np.float16(gmax)
+        W[:, 16 * g:16 * (g + 1)] = blk
+        g += 1
+    return W
+
+
+def small_cases():
+    """Small cases covering the reference's tests and the edge cases."""
+    out = []
+    rng = np.random.default_rng(123)
+    # reference tests/test_ops.py: 64x64 randn, pure 2-bit and 0.2 without hessian
+    w = rng.standard_normal((64, 64)).astype(np.float16)
+    out.append(("ops_64x64_r0", w, 0.0, None))
+    out.append(("ops_64x64_r02_nohess", w, 0.2, None))
+    # reference tests/test_gemm.py shapes: 256x256 randn and 100x80
+    out.append(("gemm_256", rng.standard_normal((256, 256)).astype(np.float16), 0.0, None))
+    out.append(("gemm_100x80", rng.standard_normal((100, 80)).astype(np.float16), 0.0, None))
+    # native self-test shape: 128x128 U(-0.5, 0.5), all 2-bit
+    out.append(("native_128", rng.uniform(-0.5, 0.5, (128, 128)).astype(np.float16), 0.0, None))
+    for (M, K, kind, seed, ratio) in [
+        (1, 16, "normal", 1, 0.25), (3, 80, "normal", 2, 0.25), (17, 100, "normal", 3, 0.25),
+        (17, 4104, "normal", 4, 0.1), (256, 256, "normal", 5, 0.1), (257, 272, "ones", 6, 0.1),
+        (100, 96, "shifted", 7, 0.25), (100, 96, "shifted", 8, 1.0), (33, 48, "const", 9, 0.25),
+        (64, 192, "ties", 10, 0.25), (64, 4104, "tiny", 11, 0.25), (300, 1040, "shifted", 12, 0.1),
+        (129, 688, "normal", 13, 0.1), (77, 136, "normal", 14, 1.5), (5, 33, "shifted", 15, 0.5),
+    ]:
+        mc = workloads.small_case(M, K, seed, kind)
+        wn, _, hn = _np_case(mc)
+        out.append((f"{kind}_{M}x{K}_s{seed}_r{ratio}", wn, ratio, hn))
+    out.append(("fma_probe", fma_probe(0), 0.0, None))
+    out.append(("fma_probe_4bit", fma_probe(1), 1.0, np.ones(96, np.float32)))
+    # hessian given but empty, and ratio 0 with hessian: no selection
+    out.append(("empty_hess", rng.standard_normal((40, 64)).astype(np.float16), 0.3,
+                np.zeros(0, np.float32)))
+    out.append(("ratio0_hess", rng.standard_normal((40, 64)).astype(np.float16), 0.0,
+                np.ones(64, np.float32)))
+    return out
+
+
+OUTPUT_FIELDS = ("packed_2bit", "packed_4bit", "scales_1st", "zeros_1st", "scales_2nd",
+                 "zeros_2nd", "scales_1st_quant", "group_precision", "outlier_values",
+                 "outlier_col_indices", "outlier_row_ptrs")
+
+
+def as_bits(a: np.ndarray) -> np.ndarray:
+    """fp16 arrays compared by bit pattern."""
+    return a.view(np.uint16) if a.dtype == np.float16 else a
+
+
+def diff_fields(a: dict, b: dict, fields=OUTPUT_FIELDS) -> list[str]:
+    bad = []
+    for f in fields:
+        x, y = np.asarray(a[f]), np.asarray(b[f])
+        if x.shape != y.shape or x.dtype != y.dtype or not np.array_equal(as_bits(x), as_bits(y)):
+            bad.append(f)
+    return bad

@@ -1,0 +1,78 @@
+"""Bit-exact parity at the benchmark shapes against the reference's own
+kernels (oracle/_ref) on the same seeded inputs: every one of the 11 outputs,
+and dequantize."""
+import numpy as np
+import pytest
+import torch
+
+from cases import OUTPUT_FIELDS, diff_fields
+from memboost_b200 import workloads
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(fn, *a):
+    out = fn(*a)
+    torch.cuda.synchronize()
+    return {f: t for f, t in zip(OUTPUT_FIELDS, out)}
+
+
+def _same(a, b):
+    bad = []
+    for f in OUTPUT_FIELDS:
+        x, y = a[f], b[f]
+        if x.dtype == torch.float16:
+            x, y = x.view(torch.int16), y.view(torch.int16)
+        if x.shape != y.shape or not torch.equal(x, y):
+            bad.append(f)
+    return bad
+
+
+def _check(case, ref_module):
+    from memboost_b200 import _C
+    w = case.weights.cuda()
+    h = case.hessian_diag.cuda()
+    got = _run(_C.quantize, w, case.ratio_4bit, h)
+    want = _run(ref_module.quantize, w, case.ratio_4bit, h)
+    assert _same(got, want) == [], case.name
+    # the 4-bit count is int(ratio * ng)
+    ng = (w.shape[1] + 15) // 16
+    assert int(got["group_precision"].sum()) == int(case.ratio_4bit * ng)
+    deq = _C.dequantize(got["packed_2bit"], got["packed_4bit"], got["scales_1st"],
+                        got["zeros_1st"], got["group_precision"], *w.shape)
+    deq_ref = ref_module.dequantize(got["packed_2bit"], got["packed_4bit"], got["scales_1st"],
+                                    got["zeros_1st"], got["group_precision"], *w.shape)
+    assert torch.equal(deq.view(torch.int16), deq_ref.view(torch.int16))
+
+
+def test_single_4096(ref_module):
+    _check(workloads.single_4096(), ref_module)
+
+
+@pytest.mark.parametrize("i", [0, 1])
+def test_mlp_7b(ref_module, i):
+    _check(workloads.mlp_7b()[i], ref_module)
+
+
+def test_mlp_70b_up(ref_module):
+    _check(workloads.mlp_70b()[0], ref_module)
+
+
+def test_llama7b_layer0(ref_module):
+    for name, M, K in workloads.llama7b_shapes(1):
+        _check(workloads.llama7b_matrix(name, M, K, seed=hash(name) % 1000), ref_module)
+
+
+def test_workspace_reuse_and_streams(mb):
+    """Same results with a reused workspace and on a side stream."""
+    from memboost_b200 import _C
+    case = workloads.mlp_matrix(1024, 2048, seed=3)
+    w, h = case.weights.cuda(), case.hessian_diag.cuda()
+    a = _run(_C.quantize, w, 0.1, h)
+    ws = _C.QuantizeWorkspace(1024, 2048, w.device)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        b = _run(_C.quantize, w, 0.1, h, ws)
+        c = _run(_C.quantize, w, 0.1, h, ws)
+    s.synchronize()
+    assert _same(a, b) == [] and _same(a, c) == []
