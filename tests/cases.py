@@ -83,6 +83,18 @@ def small_cases():
     return out
 
 
+def reference_defined(w, ratio, h) -> bool:
+    """False where the reference implementation has undefined behaviour and
+    must not be run: with a hessian, ratio_4bit > 0 and int(ratio * ng) > ng
+    its host top-k loop reads past the end of its index vector
+    (core/torch_ops.cu:172-177; it crashed the reference process here).  This
+    implementation and the oracle clamp the count to ng instead."""
+    K = w.shape[1]
+    ng = (K + 15) // 16
+    selecting = h is not None and np.asarray(h).size > 0 and ratio > 0
+    return not (selecting and int(ratio * ng) > ng)
+
+
 OUTPUT_FIELDS = ("packed_2bit", "packed_4bit", "scales_1st", "zeros_1st", "scales_2nd",
                  "zeros_2nd", "scales_1st_quant", "group_precision", "outlier_values",
                  "outlier_col_indices", "outlier_row_ptrs")

@@ -12,7 +12,7 @@ GOLDEN = sorted(glob.glob(os.path.join(os.path.dirname(__file__), "golden", "*.n
 
 
 def test_fixtures_present():
-    assert len(GOLDEN) >= 20, "golden fixtures missing (tests/golden/make_golden.py)"
+    assert len(GOLDEN) >= 22, "golden fixtures missing (tests/golden/make_golden.py)"
 
 
 @pytest.mark.parametrize("path", GOLDEN, ids=[os.path.basename(p)[:-4] for p in GOLDEN])

@@ -59,8 +59,8 @@ def test_mlp_70b_up(ref_module):
 
 
 def test_llama7b_layer0(ref_module):
-    for name, M, K in workloads.llama7b_shapes(1):
-        _check(workloads.llama7b_matrix(name, M, K, seed=hash(name) % 1000), ref_module)
+    for i, (name, M, K) in enumerate(workloads.llama7b_shapes(1)):
+        _check(workloads.llama7b_matrix(name, M, K, seed=100 + i), ref_module)
 
 
 def test_workspace_reuse_and_streams(mb):
@@ -76,3 +76,24 @@ def test_workspace_reuse_and_streams(mb):
         c = _run(_C.quantize, w, 0.1, h, ws)
     s.synchronize()
     assert _same(a, b) == [] and _same(a, c) == []
+
+
+def test_misaligned_weights_view(mb):
+    """A weights view starting 2 bytes into its storage takes the scalar
+    load path and gives the same results."""
+    from memboost_b200 import _C
+    case = workloads.mlp_matrix(96, 1024, seed=4)
+    flat = torch.empty(96 * 1024 + 8, dtype=torch.float16, device="cuda")
+    w_mis = flat[1:1 + 96 * 1024].view(96, 1024)
+    w_mis.copy_(case.weights.cuda())
+    assert w_mis.data_ptr() % 16 != 0
+    h = case.hessian_diag.cuda()
+    a = _run(_C.quantize, w_mis, 0.25, h)
+    b = _run(_C.quantize, case.weights.cuda(), 0.25, h)
+    assert _same(a, b) == []
+    out = torch.empty(96 * 1024 + 8, dtype=torch.float16, device="cuda")[1:1 + 96 * 1024].view(96, 1024)
+    d1 = _C.dequantize(a["packed_2bit"], a["packed_4bit"], a["scales_1st"], a["zeros_1st"],
+                       a["group_precision"], 96, 1024, out)
+    d2 = _C.dequantize(a["packed_2bit"], a["packed_4bit"], a["scales_1st"], a["zeros_1st"],
+                       a["group_precision"], 96, 1024)
+    assert torch.equal(d1.view(torch.int16), d2.view(torch.int16))

@@ -5,7 +5,7 @@ import numpy as np
 import pytest
 import torch
 
-from cases import OUTPUT_FIELDS, diff_fields, small_cases
+from cases import OUTPUT_FIELDS, diff_fields, reference_defined, small_cases
 
 pytestmark = pytest.mark.gpu
 
@@ -45,6 +45,8 @@ def test_quantize_matches_oracle(case, oracle):
 @pytest.mark.parametrize("case", CASES, ids=IDS)
 def test_quantize_matches_reference_kernels(case, ref_module):
     name, w, ratio, h = case
+    if not reference_defined(w, ratio, h):
+        pytest.skip("reference behaviour undefined for ratio * ng > ng")
     got = run_product(w, ratio, h)
     want = run_reference(ref_module, w, ratio, h)
     assert diff_fields(got, want) == []
@@ -53,6 +55,8 @@ def test_quantize_matches_reference_kernels(case, ref_module):
 @pytest.mark.parametrize("case", CASES, ids=IDS)
 def test_oracle_pinned_to_reference_kernels(case, ref_module, oracle):
     name, w, ratio, h = case
+    if not reference_defined(w, ratio, h):
+        pytest.skip("reference behaviour undefined for ratio * ng > ng")
     want = run_reference(ref_module, w, ratio, h)
     assert diff_fields(oracle.quantize(w, ratio, h), want) == []
 
