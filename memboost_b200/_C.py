@@ -21,7 +21,7 @@ _LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libmemboos
 if not os.path.exists(_LIB_PATH):
     raise ImportError(
         f"memboost_b200: native library {_LIB_PATH} is missing; build it with "
-        "`python -m memboost_b200.build` (there is no CPU fallback)")
+        "`python memboost_b200/build.py` (there is no CPU fallback)")
 
 _lib = ctypes.CDLL(_LIB_PATH)
 

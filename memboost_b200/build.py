@@ -6,7 +6,8 @@ shared library with a statically linked CUDA runtime.  The library exports
 exactly the C ABI declared in include/memboost_b200.h.  nvcc cross-compiles,
 so this runs on machines without a GPU.
 
-Usage: python -m memboost_b200.build [--force] [-v]
+Usage: python memboost_b200/build.py [--force] [-v]
+(run by path: importing the package needs the library this builds)
 """
 from __future__ import annotations
 
