@@ -95,6 +95,37 @@ mb_status mb_quantize_flags(const void* workspace, size_t workspace_bytes, int64
                             uint32_t* flags, mb_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * quantize without allocation -- no counterpart in the reference.
+ *
+ * For callers that cannot provide or allocate device memory for the
+ * workspace: a C/C++ host linking only this library whose device memory is
+ * owned entirely by its own fixed arena, or a latency path that must never
+ * reach cudaMalloc/cudaFree (they can synchronise the device).  The scratch
+ * is one static device array of MB_NOALLOC_SCRATCH_BYTES per GPU, held for
+ * as long as the library is loaded; matrices whose workspace
+ * (mb_quantize_workspace_size) exceeds it are rejected.
+ *
+ * Runs both phases of mb_quantize: same inputs and outputs, plus the CSR
+ * arrays with room for outlier_capacity outliers.  Synchronises `stream`
+ * once to read the outlier count into *nnz_host; if it exceeds the
+ * capacity, MB_ERR_INVALID_ARGUMENT is returned and every output except the
+ * CSR values/columns is valid.  All calls share the array: calls whose GPU
+ * work overlaps race and corrupt each other -- order them.  The first call
+ * on a device looks up the array's device address; make it before any
+ * stream capture.
+ * ------------------------------------------------------------------------- */
+#define MB_NOALLOC_SCRATCH_BYTES (4u << 20) /* 4 MiB */
+
+mb_status mb_quantize_noalloc(const void* weights_fp16, int64_t M, int64_t K, double ratio_4bit,
+                              const float* hessian_diag, int64_t hessian_numel,
+                              int32_t* packed_2bit, int32_t* packed_4bit, void* scales_1st_fp16,
+                              int8_t* zeros_1st, void* scales_2nd_fp16, int8_t* zeros_2nd,
+                              uint8_t* scales_1st_quant, uint8_t* group_precision,
+                              int32_t* outlier_row_ptrs, int32_t* nnz_device,
+                              void* outlier_values_fp16, int32_t* outlier_col_indices,
+                              int64_t outlier_capacity, int64_t* nnz_host, mb_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * dequantize -- replaces memboost::dequantize_op (core/torch_ops.h:24-29,
  * core/torch_ops.cu:267-301; bound as _C.dequantize, core/bindings.cpp:31-38).
  * out[r, c] = fp16(float(scales_1st[r, g]) * (q - zeros_1st[r, g])), no
