@@ -28,7 +28,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -85,62 +84,60 @@ def max_over_ranks(ws, x: float) -> float:
 
 
 class ClockSampler:
-    """nvidia-smi samples of this GPU's clocks during the timed region."""
+    """Samples this GPU's SM clock and throttle reasons through NVML every
+    ~2 ms while the timed region runs (read-only queries)."""
 
-    FIELDS = ("clocks.sm", "clocks.max.sm", "power.draw", "clocks_event_reasons.active",
-              "clocks_event_reasons.hw_slowdown", "clocks_event_reasons.hw_thermal_slowdown",
-              "clocks_event_reasons.sw_thermal_slowdown", "clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "sw_power_cap": 0x4}
 
     def __init__(self, device_index: int):
-        import torch
+        self.samples = []
+        self._stop = threading.Event()
+        self.handle = None
         try:
-            self.index = "GPU-" + str(torch.cuda.get_device_properties(device_index).uuid)
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            uuid = "GPU-" + str(torch.cuda.get_device_properties(device_index).uuid)
+            self.nvml = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByUUID(uuid)
         except Exception:
-            self.index = str(device_index)
-        self.proc = None
-        self.lines = []
+            self.handle = None
+
+    def _run(self):
+        nv = self.nvml
+        while not self._stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
+                mx = nv.nvmlDeviceGetMaxClockInfo(self.handle, nv.NVML_CLOCK_SM)
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                pw = nv.nvmlDeviceGetPowerUsage(self.handle) / 1000.0
+                self.samples.append((sm, mx, rs, pw))
+            except Exception:
+                pass
+            time.sleep(0.002)
 
     def __enter__(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index), "--query-gpu=" + ",".join(self.FIELDS),
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+        if self.handle is not None:
+            self.t = threading.Thread(target=self._run, daemon=True)
             self.t.start()
-        except OSError:
-            self.proc = None
+            time.sleep(0.01)
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        if self.handle is not None:
+            self._stop.set()
+            self.t.join(timeout=2)
 
     def summary(self) -> dict:
-        rows = []
-        for ln in self.lines:
-            parts = [x.strip() for x in ln.split(",")]
-            if len(parts) == len(self.FIELDS):
-                rows.append(parts)
-        if not rows:
+        if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
-        mx = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        reasons = sorted({n for r in rows for n, v in zip(names, r[4:8]) if v.lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None,
-                "power_w_max": max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
-                if any(r[2].replace(".", "").isdigit() for r in rows) else None,
-                "samples": len(rows), "reasons": reasons}
+        reasons = sorted({n for (_, _, r, _) in self.samples for n, bit in self.REASONS.items()
+                          if r & bit})
+        return {"sm_mhz": statistics.median(s[0] for s in self.samples),
+                "sm_max_mhz": max(s[1] for s in self.samples),
+                "power_w_max": round(max(s[3] for s in self.samples), 1),
+                "samples": len(self.samples), "source": "NVML, 2 ms", "reasons": reasons}
 
 
 def peaks():

@@ -64,3 +64,44 @@ __device__ __forceinline__ float warp_max(float v) {
 __device__ __forceinline__ int f2i_rz(float x) { return __float2int_rz(x); }
 
 }  // namespace mb
+
+namespace mb {
+
+// ---- packed fp32 pairs (sm_100 f32x2 arithmetic, round-to-nearest) ----
+// A pair lives in one 64-bit register: element 0 in the low half.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+// w * w of an fp16 value as an fp32 (exact: the product has <= 22 bits)
+__device__ __forceinline__ float f16_square(uint16_t h) {
+  float d;
+  asm("fma.rn.f32.f16 %0, %1, %1, %2;" : "=f"(d) : "h"(h), "f"(0.0f));
+  return d;
+}
+
+}  // namespace mb
