@@ -152,6 +152,48 @@ mb_status mb_pack_4bit(const uint8_t* values, int64_t n_values, int32_t* packed,
 mb_status mb_unpack_4bit(const int32_t* packed, int64_t n_words, int64_t num_elements,
                          uint8_t* values, mb_stream_t stream);
 
+/* ---------------------------------------------------------------------------
+ * GPTQ calibration (models/llama.py; the reference does these steps with
+ * torch inside its layer loop, so there is no native interface to replace).
+ * ------------------------------------------------------------------------- */
+
+/* Hessian -- replaces the forward-hook accumulation H_acc.add_(x.T @ x)
+ * (models/llama.py:523-528) and the normalisation H.div_(total_tokens)
+ * (models/llama.py:547-551):
+ *   H = alpha * X^T X            (accumulate == 0)
+ *   H = H + alpha * X^T X        (accumulate != 0)
+ * X: [N, K] row-major fp16 (x_is_bf16 == 0) or bf16, 16-byte aligned, K a
+ * multiple of 8.  H: [K, K] fp32 row-major, 16-byte aligned; both triangles
+ * are written.  Products of 16-bit inputs are exact in fp32; the sums run on
+ * the tensor cores in fp32 in an order of their own, so H matches an fp32
+ * GEMM to rounding, not bit for bit.  status_device (optional, device uint32)
+ * gets bit 0 set if a pipeline wait ran out (the output is then invalid). */
+mb_status mb_hessian(const void* X, int64_t N, int64_t K, int x_is_bf16, float alpha,
+                     int accumulate, float* H, uint32_t* status_device, mb_stream_t stream);
+
+/* How gptq_quantize's (w - gmin) / sc (a tensor divided by a Python float,
+ * models/llama.py:278) is evaluated: PyTorch computes the IEEE quotient for
+ * CPU tensors and multiplies by the fp32 reciprocal of the scalar for CUDA
+ * tensors. */
+#define MB_GPTQ_DIV_TRUE 0
+#define MB_GPTQ_DIV_RECIPROCAL 1
+
+/* Workspace bytes of mb_gptq_quantize (per-group parameters). */
+size_t mb_gptq_workspace_size(int64_t M, int64_t K);
+
+/* gptq_quantize -- replaces models/llama.py:234-294: per-group min/max of W
+ * (L = 16 levels where group_precision[g] == 1, else 4), then per 128-column
+ * block and column the rounding, Err = (w - q) / Hinv_cho[c, c] and the
+ * intra-block update W_block[:, j+1:] -= Err * Hinv_cho[c, j+1:], all in the
+ * reference's fp32 operation order: Q is bit-identical to the reference run
+ * on the same device kind (scalar_division).  W, Q: [M, K] fp32 row-major,
+ * 16-byte aligned, not aliased; K a multiple of 16; hinv_cho: [K, K] fp32
+ * (upper Cholesky factor of H^-1, models/llama.py:177-203); blocksize 128. */
+mb_status mb_gptq_quantize(const float* W, int64_t M, int64_t K, const float* hinv_cho,
+                           const uint8_t* group_precision, int blocksize, int scalar_division,
+                           float* Q, void* workspace, size_t workspace_bytes,
+                           mb_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -48,8 +48,22 @@ for _n in ("mb_unpack_2bit", "mb_unpack_4bit"):
     getattr(_lib, _n).restype = ctypes.c_int
     getattr(_lib, _n).argtypes = [_P, _I64, _I64, _P, _P]
 
+_lib.mb_hessian.restype = ctypes.c_int
+_lib.mb_hessian.argtypes = [_P, _I64, _I64, ctypes.c_int, ctypes.c_float, ctypes.c_int, _P, _P, _P]
+_lib.mb_gptq_workspace_size.restype = ctypes.c_size_t
+_lib.mb_gptq_workspace_size.argtypes = [_I64, _I64]
+_lib.mb_gptq_quantize.restype = ctypes.c_int
+_lib.mb_gptq_quantize.argtypes = [_P, _I64, _I64, _P, _P, ctypes.c_int, ctypes.c_int, _P, _P,
+                                  ctypes.c_size_t, _P]
+
 GROUP_SIZE_1ST = 16
 GROUP_SIZE_2ND = 256
+
+# mb_gptq_quantize's evaluation of (w - gmin) / sc: the IEEE quotient
+# (PyTorch on CPU tensors) or a product with the fp32 reciprocal (PyTorch on
+# CUDA tensors).
+GPTQ_DIV_TRUE = 0
+GPTQ_DIV_RECIPROCAL = 1
 LIB_PATH = _LIB_PATH
 
 # mb_quantize_flags bit 0: a tie of equal sensitivities straddled the 4-bit
@@ -298,3 +312,65 @@ class QuantizePlan:
                 _ptr(self._w), self.M, self.K, _ptr(self.row_ptrs), _ptr(vals), _ptr(cols),
                 _ptr(self.ws.buf), self.ws.nbytes, _stream(dev)))
         return [*self.out, vals, cols, self.row_ptrs]
+
+
+# ---- GPTQ calibration (models/llama.py) ----
+
+def hessian(x: torch.Tensor, alpha: float = 1.0, out: torch.Tensor | None = None,
+            accumulate: bool = False, status: torch.Tensor | None = None) -> torch.Tensor:
+    """out = alpha * x^T x, or out += alpha * x^T x with ``accumulate``.
+
+    x: [N, K] fp16 or bf16 CUDA tensor (K a multiple of 8), computed by the
+    tcgen05 kernel with fp32 accumulation; out: [K, K] fp32.  ``status``
+    (int32 [1], zeroed by the caller) receives bit 0 if a pipeline wait in the
+    kernel ran out."""
+    if x.dim() != 2:
+        raise RuntimeError("x must be 2D [tokens, features]")
+    if x.dtype not in (torch.float16, torch.bfloat16):
+        raise RuntimeError("x must be float16 or bfloat16")
+    if not x.is_cuda:
+        raise RuntimeError("x must be on CUDA")
+    x = x.contiguous()
+    N, K = int(x.size(0)), int(x.size(1))
+    dev = x.device
+    with torch.cuda.device(dev):
+        if out is None:
+            if accumulate:
+                raise RuntimeError("accumulate needs an output tensor")
+            out = torch.empty((K, K), dtype=torch.float32, device=dev)
+        if out.dtype != torch.float32 or tuple(out.shape) != (K, K) or not out.is_contiguous() \
+                or out.device != dev:
+            raise RuntimeError("out must be a contiguous float32 [K, K] tensor on x's device")
+        if N == 0:
+            if not accumulate:
+                out.zero_()
+            return out
+        _check(_lib.mb_hessian(_ptr(x), N, K, int(x.dtype == torch.bfloat16), float(alpha),
+                               int(bool(accumulate)), _ptr(out), _ptr(status), _stream(dev)))
+    return out
+
+
+def gptq_quantize(W: torch.Tensor, Hinv_cho: torch.Tensor, group_precision: torch.Tensor,
+                  blocksize: int = 128, scalar_division: int = GPTQ_DIV_RECIPROCAL,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """gptq_quantize of models/llama.py:234-294 on the GPU (fp32 [M, K])."""
+    if W.dim() != 2 or W.dtype != torch.float32 or not W.is_cuda:
+        raise RuntimeError("W must be a 2D float32 CUDA tensor")
+    W = W.contiguous()
+    M, K = int(W.size(0)), int(W.size(1))
+    dev = W.device
+    if tuple(Hinv_cho.shape) != (K, K) or Hinv_cho.dtype != torch.float32 \
+            or Hinv_cho.device != dev:
+        raise RuntimeError("Hinv_cho must be float32 [K, K] on W's device")
+    gp = group_precision.to(device=dev, dtype=torch.uint8).contiguous()
+    if gp.numel() != K // GROUP_SIZE_1ST:
+        raise RuntimeError("group_precision must hold K // 16 entries")
+    with torch.cuda.device(dev):
+        hc = Hinv_cho.contiguous()
+        if out is None:
+            out = torch.empty_like(W)
+        ws = torch.empty(int(_lib.mb_gptq_workspace_size(M, K)), dtype=torch.uint8, device=dev)
+        _check(_lib.mb_gptq_quantize(_ptr(W), M, K, _ptr(hc), _ptr(gp), int(blocksize),
+                                     int(scalar_division), _ptr(out), _ptr(ws), ws.numel(),
+                                     _stream(dev)))
+    return out

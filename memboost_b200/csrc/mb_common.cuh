@@ -5,6 +5,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 #include <cstdio>
 #include <string>
@@ -40,6 +41,21 @@ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
       return ::mb::set_error(MB_ERR_CUDA, std::string("CUDA error: ") +                  \
                                               cudaGetErrorString(_e) + " launching " name); \
   } while (0)
+
+// Raises `func`'s dynamic shared-memory limit to `bytes` once per device
+// (the attribute belongs to the device context); `done` is one bit per
+// device ordinal, owned by the caller (one per kernel instantiation).
+template <typename F>
+inline cudaError_t set_smem_limit_once(F* func, int bytes, std::atomic<uint64_t>& done) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = dev < 64 ? (1ull << dev) : 0ull;
+  if (bit != 0 && (done.load(std::memory_order_acquire) & bit) != 0) return cudaSuccess;
+  e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && bit != 0) done.fetch_or(bit, std::memory_order_release);
+  return e;
+}
 
 #define MB_REQUIRE(cond, msg)                                                  \
   do {                                                                         \

@@ -95,4 +95,10 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 bool make_tensor_map_2d_f16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
                             uint32_t box_rows, uint32_t box_cols);
 
+// Row-major [rows, cols] matrix of a 16-bit type (fp16 or bf16), box
+// [box_rows, box_cols] with the 128-byte swizzle (box_cols * 2 must be 128),
+// out-of-bounds elements read as zero.
+bool make_tensor_map_2d_16bit_sw128(CUtensorMap* map, const void* base, bool bf16, uint64_t rows,
+                                    uint64_t cols, uint32_t box_rows, uint32_t box_cols);
+
 }  // namespace mb

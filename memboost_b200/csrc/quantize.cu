@@ -1140,12 +1140,8 @@ template <int NW, bool kSens, bool kTma>
 mb_status launch_stats(const CUtensorMap& tmap, const StatsArgs& a, size_t smem,
                        cudaStream_t stream) {
   auto kern = stats_kernel<NW, kSens, kTma>;
-  static bool attr_set = false;  // once per instantiation
-  if (!attr_set) {
-    MB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     96 * 1024));
-    attr_set = true;
-  }
+  static std::atomic<uint64_t> attr_done{0};  // per instantiation, one bit per device
+  MB_CUDA_TRY(set_smem_limit_once(kern, 96 * 1024, attr_done));
   kern<<<(unsigned)a.ng, NW * 32, smem, stream>>>(tmap, a);
   MB_LAUNCH_CHECK("stats_kernel");
   return MB_OK;

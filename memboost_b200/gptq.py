@@ -1,0 +1,188 @@
+"""GPTQ calibration feeding memboost's mixed 2/4-bit format, on B200.
+
+The GPTQ steps of the reference's ``models/llama.py`` with the same names and
+argument meaning:
+
+* ``hessian`` / ``HessianAccumulator`` -- H = X^T X accumulated in fp32 and
+  divided by the token count (llama.py:523-528, 547-551), on the tcgen05
+  tensor-core kernel of ``csrc/hessian.cu``;
+* ``gptq_inverse`` -- damping, Cholesky, inverse, upper Cholesky of H^-1
+  (llama.py:177-203), torch.linalg as in the reference;
+* ``compute_group_precision`` -- torch sensitivity sum + top-k
+  (llama.py:209-231), the reference's own tensor expression;
+* ``gptq_quantize`` -- the blockwise error-propagating rounding
+  (llama.py:234-294) on the kernel of ``csrc/gptq.cu``, bit-identical to the
+  reference;
+* ``make_quantized_linear`` / ``QuantizedLinear`` -- GPTQ then
+  ``memboost.quantize`` with the forced hessian that makes it select the same
+  4-bit groups (llama.py:331-371, 91-105);
+* ``quantize_layer`` -- the per-layer sequence of llama.py:530-617 (4
+  Hessians, 4 inverses, 7 GPTQ + quantize calls) on given calibration inputs.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import _C
+from .formats import GROUP_SIZE_1ST, QuantizedTensor
+from .ops import dequantize, quantize
+
+GROUP_SIZE = GROUP_SIZE_1ST
+GPTQ_DIV_TRUE = _C.GPTQ_DIV_TRUE
+GPTQ_DIV_RECIPROCAL = _C.GPTQ_DIV_RECIPROCAL
+
+
+def hessian(x: torch.Tensor, alpha: float = 1.0, out: torch.Tensor | None = None,
+            accumulate: bool = False, status: torch.Tensor | None = None) -> torch.Tensor:
+    """alpha * x^T x (or out += alpha * x^T x) for x [tokens, K] fp16/bf16."""
+    return _C.hessian(x, alpha=alpha, out=out, accumulate=accumulate, status=status)
+
+
+class HessianAccumulator:
+    """Running H = sum of x^T x over calibration batches, then H / tokens.
+
+    ``add`` is the reference's forward hook (llama.py:523-528: x viewed as
+    [-1, K], H += x^T x in fp32); ``finalize`` its normalisation
+    (llama.py:547-551: H.div_(total_tokens))."""
+
+    def __init__(self, K: int, device=None):
+        device = torch.device("cuda", torch.cuda.current_device()) if device is None \
+            else torch.device(device)
+        self.K = K
+        self.H = torch.zeros((K, K), dtype=torch.float32, device=device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=device)
+        self.tokens = 0
+
+    def add(self, x: torch.Tensor) -> None:
+        x = x.detach().reshape(-1, x.shape[-1])
+        if x.shape[1] != self.K:
+            raise RuntimeError(f"expected {self.K} features, got {x.shape[1]}")
+        hessian(x, out=self.H, accumulate=True, status=self.status)
+        self.tokens += int(x.shape[0])
+
+    def finalize(self, total_tokens: int | None = None) -> torch.Tensor:
+        if int(self.status.item()) != 0:
+            raise RuntimeError("hessian kernel reported a pipeline timeout")
+        self.H.div_(self.tokens if total_tokens is None else total_tokens)
+        return self.H
+
+
+def gptq_inverse(H: torch.Tensor):
+    """(h_diag, Hinv_cho) of llama.py:177-203; damps H in place as the
+    reference does: damp = max(0.01 * max|diag H|, 1e-6) added to the
+    diagonal, diagonal entries below 1e-8 set to 1, then Cholesky inverse,
+    h_diag = diag(H^-1), and the upper Cholesky factor of H^-1 + 1e-8 I."""
+    d = H.diagonal()
+    damp = max((0.01 * d.abs().max()).item(), 1e-6)
+    d.add_(damp)
+    dead = d < 1e-8
+    if dead.any():
+        d[dead] = 1.0
+    Hinv = torch.cholesky_inverse(torch.linalg.cholesky(H))
+    h_diag = Hinv.diag().clone()
+    Hinv.diagonal().add_(1e-8)
+    return h_diag, torch.linalg.cholesky(Hinv, upper=True)
+
+
+def compute_group_precision(W: torch.Tensor, h_diag: torch.Tensor, ratio_4bit: float):
+    """uint8 [K // 16]: 1 for the int(ratio * groups) groups of largest
+    sum_{rows, cols in group} w^2 / clamp(h_diag, 1e-8) (llama.py:209-231,
+    the same torch expression, so the same sums and top-k)."""
+    M, K = W.shape
+    ng = K // GROUP_SIZE
+    inv_h = 1.0 / h_diag.clamp(min=1e-8)
+    sens = (W.pow(2) * inv_h.unsqueeze(0)).view(M, ng, GROUP_SIZE).sum(dim=(0, 2))
+    n4 = int(ratio_4bit * ng)
+    gp = torch.zeros(ng, dtype=torch.uint8, device=W.device)
+    if n4 > 0:
+        gp[sens.topk(n4).indices] = 1
+    return gp
+
+
+def gptq_quantize(W: torch.Tensor, Hinv_cho: torch.Tensor, group_precision: torch.Tensor,
+                  blocksize: int = 128, scalar_division: int | None = None) -> torch.Tensor:
+    """Q of llama.py:234-294 (fp32 [M, K]), bit-identical to the reference.
+
+    ``scalar_division`` picks which run of the reference to reproduce:
+    GPTQ_DIV_RECIPROCAL (default) -- tensors on a CUDA device, where PyTorch
+    divides by the Python-float scale as a multiplication by its fp32
+    reciprocal; GPTQ_DIV_TRUE -- tensors on the CPU (IEEE quotient)."""
+    if scalar_division is None:
+        scalar_division = GPTQ_DIV_RECIPROCAL
+    return _C.gptq_quantize(W, Hinv_cho, group_precision, blocksize=blocksize,
+                            scalar_division=scalar_division)
+
+
+def forced_hessian_diag(group_precision: torch.Tensor, K: int, device=None) -> torch.Tensor:
+    """The hessian_diag of llama.py:356-364 that makes memboost's selection
+    pick exactly the groups marked in ``group_precision``: 1e-10 on 4-bit
+    groups, 1e10 on 2-bit groups, 1.0 past the last whole group."""
+    device = group_precision.device if device is None else device
+    h = torch.ones(K, dtype=torch.float32, device=device)
+    ng = K // GROUP_SIZE
+    four = group_precision[:ng].to(device=device).repeat_interleave(GROUP_SIZE) == 1
+    h[:ng * GROUP_SIZE] = torch.where(four, torch.tensor(1e-10, device=device),
+                                      torch.tensor(1e10, device=device))
+    return h
+
+
+class QuantizedLinear(nn.Module):
+    """Linear layer over a memboost QuantizedTensor (llama.py:91-105):
+    forward = F.linear(x.half(), dequantize(q_weight))."""
+
+    def __init__(self, in_features: int, out_features: int):
+        super().__init__()
+        self.in_features = in_features
+        self.out_features = out_features
+        self.q_weight: QuantizedTensor | None = None
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return F.linear(x.to(torch.float16), dequantize(self.q_weight))
+
+
+def make_quantized_linear(W_fp32: torch.Tensor, h_diag: torch.Tensor, Hinv_cho: torch.Tensor,
+                          ratio_4bit: float, blocksize: int = 128) -> QuantizedLinear:
+    """GPTQ + memboost quantize of one weight matrix (llama.py:331-371)."""
+    M, K = W_fp32.shape
+    if ratio_4bit <= 0:
+        gp = torch.zeros(K // GROUP_SIZE, dtype=torch.uint8, device=W_fp32.device)
+        Q = gptq_quantize(W_fp32, Hinv_cho, gp, blocksize=blocksize)
+        qt = quantize(Q.to(torch.float16).contiguous(), ratio_4bit=0.0)
+    else:
+        gp = compute_group_precision(W_fp32, h_diag, ratio_4bit)
+        Q = gptq_quantize(W_fp32, Hinv_cho, gp, blocksize=blocksize)
+        qt = quantize(Q.to(torch.float16).contiguous(), ratio_4bit=ratio_4bit,
+                      hessian_diag=forced_hessian_diag(gp, K))
+    ql = QuantizedLinear(K, M)
+    ql.q_weight = qt
+    return ql
+
+
+# weight name -> which calibration input (Hessian) it shares (llama.py:555-593)
+LAYER_INPUTS = {
+    "self_attn.q_proj": "attn", "self_attn.k_proj": "attn", "self_attn.v_proj": "attn",
+    "self_attn.o_proj": "o", "mlp.gate_proj": "mlp", "mlp.up_proj": "mlp",
+    "mlp.down_proj": "down",
+}
+
+
+def quantize_layer(weights: dict, inputs: dict, ratio_4bit: float = 0.1,
+                   blocksize: int = 128) -> dict:
+    """One transformer layer's GPTQ (llama.py:530-617): the four Hessians
+    from the calibration inputs (``inputs``: "attn", "o", "mlp", "down" ->
+    [tokens, K] fp16/bf16), their inverses, then GPTQ + quantize of the seven
+    fp32 weight matrices (``weights``: names of ``LAYER_INPUTS``).  Returns
+    name -> QuantizedTensor."""
+    inv = {}
+    for key, x in inputs.items():
+        acc = HessianAccumulator(x.shape[-1], x.device)
+        acc.add(x)
+        inv[key] = gptq_inverse(acc.finalize())
+    out = {}
+    for name, W in weights.items():
+        h_diag, hinv_cho = inv[LAYER_INPUTS[name]]
+        out[name] = make_quantized_linear(W, h_diag, hinv_cho, ratio_4bit,
+                                          blocksize=blocksize).q_weight
+    return out

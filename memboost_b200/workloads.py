@@ -16,6 +16,11 @@ same bytes.
                    per matrix; ratio 0.1
   mlp_70b          28672x8192 and 8192x28672 ~ N(0, 0.015^2); 0.2% x10
                    outliers; lognormal(0, 2.0) hessian; ratio 0.25
+  gptq_layer       one Llama-7B layer's GPTQ: calibration activations of
+                   128 x 2048 tokens (bf16, Student-t(4) / sqrt(4096), 1% of
+                   channels x20) for the attention (K=4096), o_proj (4096),
+                   MLP (4096) and down_proj (11008) inputs; fp32 weights
+                   ~ N(0, 0.02^2) of the seven projection shapes; ratio 0.1
 """
 from __future__ import annotations
 
@@ -133,3 +138,51 @@ def small_case(M: int, K: int, seed: int, kind: str = "normal") -> MatrixCase:
     elif kind != "normal":
         raise ValueError(kind)
     return MatrixCase(f"{kind}_{M}x{K}", w.half(), h.float(), 0.25)
+
+
+def calibration_activations(N: int, K: int, seed: int, device=None,
+                            dtype: torch.dtype = torch.bfloat16,
+                            channel_frac: float = 0.01, channel_scale: float = 20.0
+                            ) -> torch.Tensor:
+    """[N, K] calibration inputs: Student-t(4) / sqrt(4096), with a seeded
+    ``channel_frac`` of the K channels scaled by ``channel_scale`` (the
+    outlier channels of LLM activations).  Student-t(4) is drawn as
+    Z / sqrt(chi2_4 / 4) from five normals, so it is cheap on any device;
+    ``device`` defaults to the CPU (bytes identical for a given seed)."""
+    device = torch.device("cpu") if device is None else torch.device(device)
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    z = torch.randn((N, K), generator=g, device=device)
+    chi2 = torch.zeros((N, K), device=device)
+    for _ in range(4):
+        chi2.addcmul_(n := torch.randn((N, K), generator=g, device=device), n)
+    x = z.div_(chi2.div_(4.0).sqrt_()).div_(64.0)
+    gc = torch.Generator()
+    gc.manual_seed(seed + 7919)
+    n_ch = max(1, int(round(channel_frac * K)))
+    ch = torch.randperm(K, generator=gc)[:n_ch].to(device)
+    x[:, ch] *= channel_scale
+    return x.to(dtype)
+
+
+GPTQ_LAYER_SHAPES = {  # name -> (M, K) of a Llama-2-7B layer
+    "self_attn.q_proj": (4096, 4096), "self_attn.k_proj": (4096, 4096),
+    "self_attn.v_proj": (4096, 4096), "self_attn.o_proj": (4096, 4096),
+    "mlp.gate_proj": (11008, 4096), "mlp.up_proj": (11008, 4096),
+    "mlp.down_proj": (4096, 11008),
+}
+GPTQ_INPUT_FEATURES = {"attn": 4096, "o": 4096, "mlp": 4096, "down": 11008}
+
+
+def gptq_layer(seed: int = 11, tokens: int = 128 * 2048, device=None, scale: int = 1):
+    """(weights, inputs) of one synthetic Llama-7B layer for GPTQ.  ``scale``
+    divides every dimension (shapes stay multiples of 128 for scale <= 8)."""
+    device = torch.device("cpu") if device is None else torch.device(device)
+    weights = {}
+    for i, (name, (M, K)) in enumerate(GPTQ_LAYER_SHAPES.items()):
+        g = torch.Generator(device=device)
+        g.manual_seed(seed * 100 + i)
+        weights[name] = torch.randn((M // scale, K // scale), generator=g, device=device) * 0.02
+    inputs = {key: calibration_activations(tokens // scale, K // scale, seed * 1000 + j, device)
+              for j, (key, K) in enumerate(GPTQ_INPUT_FEATURES.items())}
+    return weights, inputs

@@ -379,6 +379,73 @@ void mbo_unpack_4bit(const int32_t* p, int64_t n_words, int64_t num_elements, ui
   }
 }
 
+// gptq_quantize -- models/llama.py:234-294 (torch fp32 tensor arithmetic
+// with Python-float scalars), operation by operation:
+//   :252-263  gmin/gmax = W[:, 16g:16g+16].min()/.max() (.item(): NaN
+//             propagates), group_min[g] = gmin (fp32), group_scale[g] =
+//             (gmax - gmin) / (L - 1) in double stored as fp32, 0.0 unless
+//             gmax > gmin; L = 16 where gp[g] == 1 else 4
+//   :265-268  blocks of `blocksize` columns; W_block = a copy of the
+//             original W block (no column of a block is written before it
+//             is copied), Err per column
+//   :277-281  sc > 0: q_int = ((w - gmin) / sc).round().clamp(0, L - 1),
+//             zero = round(-gmin / sc) (Python: double, half-even),
+//             q = sc * (q_int - zero); else q = gmin
+//   :283      Err = (w - q) / Hinv_cho[col, col]
+//   :286-289  W_block[:, j+1:] -= Err[:, j] * Hinv_cho[col, j+1:block_end]
+// (w - gmin) / sc divides a tensor by a Python float: PyTorch evaluates that
+// as the IEEE quotient on CPU tensors (div_mode 0) and as a multiplication by
+// the fp32 reciprocal 1.0f / sc on CUDA tensors (div_mode 1).  Rows are
+// independent; they are split over host threads.
+void mbo_gptq_quantize(const float* W, int64_t M, int64_t K, const float* Hc, const uint8_t* gp,
+                       int64_t blocksize, int div_mode, float* Q, int nthreads) {
+  const int64_t ng = K / 16;
+  std::vector<float> gmin(ng), sc(ng), rsc(ng), zero_f(ng), lmax(ng);
+  for (int64_t g = 0; g < ng; ++g) {
+    float mn = INFINITY, mx = -INFINITY;
+    bool nan = false;
+    for (int64_t r = 0; r < M; ++r)
+      for (int64_t c = 16 * g; c < 16 * g + 16; ++c) {
+        const float v = W[r * K + c];
+        if (std::isnan(v)) nan = true;
+        mn = std::min(mn, v);
+        mx = std::max(mx, v);
+      }
+    if (nan) mn = mx = NAN;
+    const int L = gp[g] == 1 ? 16 : 4;
+    const double d = ((double)mx > (double)mn) ? ((double)mx - (double)mn) / (double)(L - 1) : 0.0;
+    gmin[g] = mn;
+    sc[g] = (float)d;
+    rsc[g] = sc[g] > 0.0f ? 1.0f / sc[g] : 0.0f;
+    zero_f[g] = sc[g] > 0.0f ? (float)std::nearbyint(-(double)mn / (double)sc[g]) : 0.0f;
+    lmax[g] = (float)(L - 1);
+  }
+  parallel_for(M, nthreads, [&](int64_t r) {
+    std::vector<float> wb((size_t)blocksize);
+    for (int64_t bs = 0; bs < K; bs += blocksize) {
+      const int64_t be = std::min(bs + blocksize, K);
+      const int64_t n = be - bs;
+      for (int64_t c = 0; c < n; ++c) wb[c] = W[r * K + bs + c];
+      for (int64_t j = 0; j < n; ++j) {
+        const int64_t col = bs + j, g = col / 16;
+        const float x = wb[j];
+        float q;
+        if (sc[g] > 0.0f) {
+          const float dlt = x - gmin[g];
+          float qi = std::nearbyint(div_mode == 1 ? dlt * rsc[g] : dlt / sc[g]);
+          if (!std::isnan(qi)) qi = std::min(std::max(qi, 0.0f), lmax[g]);
+          q = sc[g] * (qi - zero_f[g]);
+        } else {
+          q = gmin[g];
+        }
+        const float err = (x - q) / Hc[col * K + col];
+        Q[r * K + col] = q;
+        for (int64_t c = j + 1; c < n; ++c) wb[c] = wb[c] - err * Hc[col * K + bs + c];
+      }
+    }
+  });
+}
+
 // Conversion helpers exported for the tests.
 float mbo_f16_to_f32(uint16_t h) { return f16_to_f32(h); }
 uint16_t mbo_f32_to_f16(float f) { return f32_to_f16_rn(f); }

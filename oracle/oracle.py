@@ -57,6 +57,7 @@ def lib():
             getattr(L, n).argtypes = [P, I64, P]
         for n in ("mbo_unpack_2bit", "mbo_unpack_4bit"):
             getattr(L, n).argtypes = [P, I64, I64, P]
+        L.mbo_gptq_quantize.argtypes = [P, I64, I64, P, P, I64, ctypes.c_int, P, ctypes.c_int]
         L.mbo_f16_to_f32.restype = ctypes.c_float
         L.mbo_f16_to_f32.argtypes = [ctypes.c_uint16]
         L.mbo_f32_to_f16.restype = ctypes.c_uint16
@@ -203,3 +204,25 @@ def f32_to_f16_bits(x: float) -> int:
 
 def f16_bits_to_f32(b: int) -> float:
     return float(lib().mbo_f16_to_f32(int(b)))
+
+
+# (w - gmin) / sc in gptq_quantize (models/llama.py:278): PyTorch's IEEE
+# quotient on CPU tensors, multiplication by the fp32 reciprocal on CUDA.
+GPTQ_DIV_TRUE = 0
+GPTQ_DIV_RECIPROCAL = 1
+
+
+def gptq_quantize(W: np.ndarray, hinv_cho: np.ndarray, group_precision: np.ndarray,
+                  blocksize: int = 128, div_mode: int = GPTQ_DIV_TRUE,
+                  nthreads: int = 0) -> np.ndarray:
+    """gptq_quantize of models/llama.py:234-294 on fp32 numpy arrays."""
+    W = np.ascontiguousarray(W, dtype=np.float32)
+    M, K = W.shape
+    assert K % GROUP_SIZE_1ST == 0
+    Hc = np.ascontiguousarray(hinv_cho, dtype=np.float32)
+    assert Hc.shape == (K, K)
+    gp = np.ascontiguousarray(group_precision, dtype=np.uint8)
+    assert gp.shape == (K // GROUP_SIZE_1ST,)
+    Q = np.empty_like(W)
+    lib().mbo_gptq_quantize(_p(W), M, K, _p(Hc), _p(gp), blocksize, div_mode, _p(Q), nthreads)
+    return Q

@@ -112,3 +112,38 @@ def diff_fields(a: dict, b: dict, fields=OUTPUT_FIELDS) -> list[str]:
         if x.shape != y.shape or x.dtype != y.dtype or not np.array_equal(as_bits(x), as_bits(y)):
             bad.append(f)
     return bad
+
+
+def gptq_division_probe(M: int = 8, ng: int = 16, seed: int = 0):
+    """(W, hinv_cho, group_precision) on which the two evaluations of
+    gptq_quantize's (w - gmin) / sc (models/llama.py:278) give different
+    codes: every group has min 0 and a max chosen so that sc's reciprocal is
+    inexact, and its other entries sit within a few ulps of the (k + 0.5) * sc
+    rounding boundaries where rint(w / sc) != rint(w * fl(1 / sc)).
+    hinv_cho = I keeps the columns independent (every update adds err * 0)."""
+    f = np.float32
+    rng = np.random.default_rng(seed)
+    K = 16 * ng
+    W = np.zeros((M, K), f)
+    gp = (np.arange(ng) % 2).astype(np.uint8)
+    for g in range(ng):
+        L = 16 if gp[g] else 4
+        while True:
+            gmax = f(rng.uniform(0.01, 0.1))
+            sc = f(np.float64(gmax) / (L - 1))
+            r = f(f(1) / sc)
+            hits = []
+            for k in range(L - 1):
+                w = f((k + 0.5) * np.float64(sc))
+                for _ in range(4):
+                    w = np.nextafter(w, f(-1), dtype=f)
+                for _ in range(9):
+                    if 0 < w < gmax and np.rint(f(w / sc)) != np.rint(f(w * r)):
+                        hits.append(w)
+                    w = np.nextafter(w, f(1), dtype=f)
+            if len(hits) >= 2:
+                break
+        block = rng.choice(np.array(hits, f), size=(M, 16))
+        block[0, 0], block[0, 1] = f(0), gmax
+        W[:, 16 * g:16 * g + 16] = block
+    return W, np.eye(K, dtype=f), gp
