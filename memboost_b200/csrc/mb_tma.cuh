@@ -84,6 +84,13 @@ __device__ __forceinline__ void grid_dependency_wait() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
+// Programmatic dependent launch: the next grid in the stream may begin
+// launching (it still waits for this grid's completion in
+// grid_dependency_wait before reading what this grid writes).
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---- host ----
 
 // cuTensorMapEncodeTiled from the driver, without linking libcuda.

@@ -52,7 +52,10 @@ constexpr int kStatsThreads = 32 * kTileGroups;   // 256
 constexpr int kSteps = kChunkRows / 32;
 constexpr int kBoxBytes = kChunkRows * 128;       // one 64-column TMA box (16 KB)
 constexpr int kTileBytes = 2 * kBoxBytes;         // 32 KB
-constexpr int kStatsSmem = kTileBytes + 1024;     // + alignment slack
+constexpr int kStages = 3;     // stats tile ring per CTA (two CTAs per SM)
+constexpr int kEncStages = 2;  // encode tile ring (its staging buffers take the rest)
+constexpr int kStatsSmem = kStages * kTileBytes + 1024;   // + alignment slack
+constexpr int kEncSmem = kEncStages * kTileBytes + 1024;
 
 // exact sums of pending groups
 constexpr int kMaxItems = 8;             // program items per (group, chunk)
@@ -89,7 +92,9 @@ struct __align__(16) Header {
   uint32_t n_pend;         // pending groups after them (ascending)
   uint32_t need;           // how many pending groups are 4-bit
   uint32_t ticket_exact;   // pending groups whose exact sum is assembled
-  uint32_t pad[7];
+  uint32_t tile_stats;     // next stats tile
+  uint32_t tile_encode;    // next encode tile
+  uint32_t pad[5];
 };
 static_assert(sizeof(Header) == 64, "Header must stay 64 bytes");
 
@@ -122,17 +127,20 @@ ChunkLayout chunk_layout(int64_t M, int64_t ng) {
 struct Workspace {
   Header* hdr;
   uint32_t* ct_count;   // [nct] stats tiles finished per column tile (zeroed with hdr)
-  double* cpred;        // [ng * nrc] chunk prediction sums
+  float* ccol;          // [ng * nrc * 16] per-column sums of w*w over the chunk
+  double* cpred;        // [ng * nrc] chunk prediction sums (from ccol and 1/h)
   float2* cminmax;      // [ng * nrc] chunk min / max
-  uint32_t* cflag;      // [ng * nrc] chunk NaN / inf bits
   double* gpred;        // [ng] predicted sensitivity
   double* gmom;         // [ng] sum over chunks of terms * inclusive prediction
   uint32_t* gflag;      // [ng] kGrp* bits
+  uint2* gkey;          // [ng] sortable lower / upper bound of the sensitivity
   uint32_t* gticket;    // [ng] exact-sum chunk programs finished (pending groups)
   int4* items;          // [ng * nrc * kMaxItems] chunk programs (pending groups)
   uint32_t* icount;     // [ng * nrc] item count | NaN / inf / overflow bits
   float* gmin;
   float* gmax;
+  uint32_t* gscale;     // [ng] fp16 scale_1st of the 2-bit (low) and 4-bit (high) params
+  uint8_t* greg;        // [ng] bit 0 / 1: the 2-bit / 4-bit params are regular
   float* sens;          // [ng] exact sums (pending groups)
   GroupParams* params;  // [2 * ng]: 2g = 2-bit, 2g + 1 = 4-bit
   float4* chunk_tab;    // [ntab_full + 1]: (min, fp32 scale2, fp16 bits of scale2, zero2)
@@ -152,17 +160,20 @@ size_t workspace_layout(int64_t M, int64_t K, char* base, Workspace* ws) {
   };
   const int64_t nct = ceil_div(K, kTileCols), nrc = ceil_div(M, kChunkRows), nrec = ng * nrc;
   char* p_hdr = take(sizeof(Header) + sizeof(uint32_t) * nct);  // zeroed per call
+  char* p_cc = take(sizeof(float) * 16 * nrec);
   char* p_cp = take(sizeof(double) * nrec);
   char* p_mm = take(sizeof(float2) * nrec);
-  char* p_cf = take(sizeof(uint32_t) * nrec);
   char* p_gp = take(sizeof(double) * ng);
   char* p_gm = take(sizeof(double) * ng);
   char* p_gf = take(sizeof(uint32_t) * ng);
+  char* p_gk = take(sizeof(uint2) * ng);
   char* p_gt = take(sizeof(uint32_t) * ng);
   char* p_it = take(sizeof(int4) * kMaxItems * nrec);
   char* p_ic = take(sizeof(uint32_t) * nrec);
   char* p_gmin = take(sizeof(float) * ng);
   char* p_gmax = take(sizeof(float) * ng);
+  char* p_gsc = take(sizeof(uint32_t) * ng);
+  char* p_grg = take(ng);
   char* p_sens = take(sizeof(float) * ng);
   char* p_par = take(sizeof(GroupParams) * 2 * ng);
   char* p_ch = take(sizeof(float4) * (cl.ntab_full + 1));
@@ -172,17 +183,20 @@ size_t workspace_layout(int64_t M, int64_t K, char* base, Workspace* ws) {
   if (ws) {
     ws->hdr = reinterpret_cast<Header*>(p_hdr);
     ws->ct_count = reinterpret_cast<uint32_t*>(p_hdr + sizeof(Header));
+    ws->ccol = reinterpret_cast<float*>(p_cc);
     ws->cpred = reinterpret_cast<double*>(p_cp);
     ws->cminmax = reinterpret_cast<float2*>(p_mm);
-    ws->cflag = reinterpret_cast<uint32_t*>(p_cf);
     ws->gpred = reinterpret_cast<double*>(p_gp);
     ws->gmom = reinterpret_cast<double*>(p_gm);
     ws->gflag = reinterpret_cast<uint32_t*>(p_gf);
+    ws->gkey = reinterpret_cast<uint2*>(p_gk);
     ws->gticket = reinterpret_cast<uint32_t*>(p_gt);
     ws->items = reinterpret_cast<int4*>(p_it);
     ws->icount = reinterpret_cast<uint32_t*>(p_ic);
     ws->gmin = reinterpret_cast<float*>(p_gmin);
     ws->gmax = reinterpret_cast<float*>(p_gmax);
+    ws->gscale = reinterpret_cast<uint32_t*>(p_gsc);
+    ws->greg = reinterpret_cast<uint8_t*>(p_grg);
     ws->sens = reinterpret_cast<float*>(p_sens);
     ws->params = reinterpret_cast<GroupParams*>(p_par);
     ws->chunk_tab = reinterpret_cast<float4*>(p_ch);
@@ -332,10 +346,21 @@ __device__ void group_scalars(float gmin, float gmax, int L, GroupParams& p) {
 }
 
 // Parameters of group g for both precisions (one warp): lanes 0-2 find the
-// 2-bit thresholds, lanes 3-17 the 4-bit ones.
-__device__ void group_params_warp(GroupParams* params, int64_t g, float mn, float mx, int lane) {
+// 2-bit thresholds, lanes 3-17 the 4-bit ones.  Also the compact copies of
+// the two fp16 scales and regular flags.
+__device__ void group_params_warp(GroupParams* params, uint32_t* gscale, uint8_t* greg, int64_t g,
+                                  float mn, float mx, int lane) {
   GroupParams* p2 = params + 2 * g;
   GroupParams* p4 = p2 + 1;
+  {
+    GroupParams q2, q4;
+    group_scalars(mn, mx, 4, q2);
+    group_scalars(mn, mx, 16, q4);
+    if (lane == 0) {
+      gscale[g] = (uint32_t)q2.scale_h | ((uint32_t)q4.scale_h << 16);
+      greg[g] = (uint8_t)((q2.flags & kFlagRegular) | ((q4.flags & kFlagRegular) << 1));
+    }
+  }
   if (lane < 18) {
     const bool four = lane >= 3;
     const int L = four ? 16 : 4;
@@ -734,8 +759,6 @@ struct QArgs {
   uint8_t* sq;
   int32_t* row_ptrs;
   int32_t* nnz;
-  int enc_nbx;  // encode grid: slot blocks (x) per row block
-  int enc_nby;  // row blocks
 };
 
 // Replay runs [a, b) of group g's chunk rc exactly, starting from s.  Runs go
@@ -964,6 +987,40 @@ __device__ __forceinline__ void sync_nt() {
     __syncthreads();
 }
 
+// One radix step (one warp): among the 256 bins (highest first) find the
+// bin holding the s2[1]-th largest key; extend the prefix s2[0] with it and
+// leave in s2[1] how many keys of that bin are still needed.
+__device__ __forceinline__ void radix_pick(const uint32_t* hist, uint32_t* s2, uint32_t prefix,
+                                           int shift, int lane) {
+  uint32_t c[8], tot = 0;  // lane l owns bins 8l .. 8l+7
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    c[j] = hist[lane * 8 + j];
+    tot += c[j];
+  }
+  uint32_t suf = tot;  // keys in lanes >= lane
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_down_sync(0xffffffffu, suf, o);
+    if (lane + o < 32) suf += y;
+  }
+  const uint32_t need = s2[1];
+  const uint32_t above = suf - tot;
+  const bool here = above < need && suf >= need;
+  const unsigned bal = __ballot_sync(0xffffffffu, here);
+  const int L = __ffs(bal) - 1;
+  if (lane == L) {
+    uint32_t acc = above;
+    int b = 7;
+    for (; b > 0; --b) {
+      if (acc + c[b] >= need) break;
+      acc += c[b];
+    }
+    s2[0] = prefix | ((uint32_t)(lane * 8 + b) << shift);
+    s2[1] = need - acc;
+  }
+}
+
 // k-th largest (1-based, 1 <= k <= n) of n 32-bit keys key(i), by 4 passes
 // of 8 bits; returns the key and, in *need_eq, how many keys equal to it the
 // k largest include.  All NT threads call it with the same arguments.
@@ -985,36 +1042,7 @@ __device__ uint32_t kth_largest(int n, int k, KeyF key, uint32_t* hist, uint32_t
       if ((kk & mask) == prefix) atomicAdd(&hist[(kk >> shift) & 255u], 1u);
     }
     sync_nt<NT>();
-    if (warp == 0) {
-      // suffix sums over bins, highest bin first; lane l owns bins 8l..8l+7
-      uint32_t c[8], tot = 0;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        c[j] = hist[lane * 8 + j];
-        tot += c[j];
-      }
-      uint32_t suf = tot;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t y = __shfl_down_sync(0xffffffffu, suf, o);
-        if (lane + o < 32) suf += y;
-      }
-      const uint32_t need = s2[1];
-      const uint32_t above = suf - tot;
-      const bool here = above < need && suf >= need;
-      const unsigned bal = __ballot_sync(0xffffffffu, here);
-      const int L = __ffs(bal) - 1;
-      if (lane == L) {
-        uint32_t acc = above;
-        int b = 7;
-        for (; b > 0; --b) {
-          if (acc + c[b] >= need) break;
-          acc += c[b];
-        }
-        s2[0] = prefix | ((uint32_t)(lane * 8 + b) << shift);
-        s2[1] = need - acc;
-      }
-    }
+    if (warp == 0) radix_pick(hist, s2, prefix, shift, lane);
     mask |= 0xFFu << shift;
     sync_nt<NT>();
   }
@@ -1024,96 +1052,135 @@ __device__ uint32_t kth_largest(int n, int k, KeyF key, uint32_t* hist, uint32_t
   return T;
 }
 
+// Two order statistics at once over the same indices: the ka-th largest of
+// keys a(i) and the kb-th largest of keys b(i) (the passes share the syncs).
+template <int NT, typename KeyA, typename KeyB>
+__device__ void kth_largest2(int n, int ka, KeyA a, int kb, KeyB b, uint32_t* hist /*512*/,
+                             uint32_t* s4, uint32_t& Ta, uint32_t& Tb) {
+  const int tid = threadIdx.x % NT, lane = threadIdx.x & 31, warp = tid >> 5;
+  if (tid == 0) {
+    s4[0] = 0;
+    s4[1] = (uint32_t)ka;
+    s4[2] = 0;
+    s4[3] = (uint32_t)kb;
+  }
+  uint32_t mask = 0;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = tid; i < 512; i += NT) hist[i] = 0;
+    sync_nt<NT>();
+    const uint32_t pa = s4[0], pb = s4[2];
+    for (int i = tid; i < n; i += NT) {
+      const uint32_t x = a(i), y = b(i);
+      if ((x & mask) == pa) atomicAdd(&hist[(x >> shift) & 255u], 1u);
+      if ((y & mask) == pb) atomicAdd(&hist[256 + ((y >> shift) & 255u)], 1u);
+    }
+    sync_nt<NT>();
+    if (warp == 0) radix_pick(hist, s4, pa, shift, lane);
+    if (warp == (NT > 32 ? 1 : 0)) radix_pick(hist + 256, s4 + 2, pb, shift, lane);
+    mask |= 0xFFu << shift;
+    sync_nt<NT>();
+  }
+  Ta = s4[0];
+  Tb = s4[2];
+  sync_nt<NT>();
+}
+
 // Sortable key of a non-negative float or NaN (NaN above +inf, as the bit
 // patterns of the reference's comparisons would order them).
 __device__ __forceinline__ uint32_t sens_key(float s) {
   return isnan(s) ? 0xFFFFFFFFu : __float_as_uint(s);
 }
 
-// 2nd-order tables, group order and any_irregular once every group's
-// precision is in ws.prec (quantize.cu:245-272 over the flattened [M, ng]
-// scales; scales_1st[r, g] depends only on g, so full chunks repeat with
-// period ng / gcd(ng, 256)).  Also writes the group_precision output.
-// With rebuild_order false (the selection completed after encode started)
-// `order` and the decided / pending counts stay as they are.
+// 2nd-order tables, any_irregular and the group_precision output once every
+// group's precision is in ws.prec (quantize.cu:245-272 over the flattened
+// [M, ng] scales).  scales_1st[r, g] depends only on g, so full chunks repeat
+// with period ng / gcd(ng, 256), and a chunk starting at flat index s0 holds
+// the groups s0 mod ng, s0 mod ng + 1, ... cyclically.  With rebuild_order
+// (used when nothing stays pending) the decided / pending counts are reset;
+// otherwise (the selection completed after encode started) `order` and the
+// counts stay as they are.
 template <int NT>
 __device__ void finalize_tables(const QArgs& a, float* s1, size_t s1_bytes, uint32_t* s_wsum,
                                 int* s_irr, bool rebuild_order) {
   const int ng = a.ng;
   const int tid = threadIdx.x % NT, lane = threadIdx.x & 31, warp = tid >> 5;
   constexpr int NWARP = NT / 32;
+  (void)s_wsum;
   if (tid == 0) *s_irr = 0;
   sync_nt<NT>();
   const bool s1_in_smem = (size_t)ng * sizeof(float) <= s1_bytes;
+  auto scale_from = [&](int g, uint8_t pr) -> float {
+    const uint32_t sh2 = __ldcg(a.ws.gscale + g);
+    return __half2float(__ushort_as_half((uint16_t)(pr ? (sh2 >> 16) : (sh2 & 0xFFFFu))));
+  };
   int irr = 0;
   for (int g = tid; g < ng; g += NT) {
     const uint8_t pr = a.ws.prec[g];
     a.gp[g] = pr;
-    const GroupParams& p = a.ws.params[2 * g + pr];
-    if (s1_in_smem) s1[g] = __half2float(__ushort_as_half((uint16_t)p.scale_h));
-    irr |= !(p.flags & kFlagRegular);
+    if (s1_in_smem) s1[g] = scale_from(g, pr);
+    irr |= !((a.ws.greg[g] >> pr) & 1);
   }
-  if (irr) atomicOr(s_irr, 1);
+  if (__any_sync(0xffffffffu, irr) && lane == 0) atomicOr(s_irr, 1);
   sync_nt<NT>();
   auto scale_of = [&](int g) -> float {
-    return s1_in_smem ? s1[g]
-                      : __half2float(__ushort_as_half(
-                            (uint16_t)a.ws.params[2 * g + a.ws.prec[g]].scale_h));
+    return s1_in_smem ? s1[g] : scale_from(g, a.ws.prec[g]);
   };
   const ChunkLayout& cl = a.cl;
   const int nchunks = cl.ntab_full + cl.has_partial;
-  for (int ci = warp; ci < nchunks; ci += NWARP) {
-    const int64_t cidx = ci < cl.ntab_full ? ci : cl.nfull;  // the partial chunk is the last
-    const int64_t s0 = cidx * kGroup2, s1e = min64(s0 + kGroup2, cl.total);
-    float mn = 1e10f, mx = -1e10f;
-    for (int64_t i = s0 + lane; i < s1e; i += 32) {
-      const float v = scale_of((int)(i % ng));
-      mn = fminf(mn, v);
-      mx = fmaxf(mx, v);
+  // block minima / maxima of 32 consecutive groups (in the scratch after s1)
+  const int nblk = (ng + 31) / 32;
+  const bool blk_in_smem =
+      s1_in_smem && (size_t)(ng + 2 * nblk) * sizeof(float) <= s1_bytes && NT > 32;
+  float* bmin = s1 + ng;
+  float* bmax = bmin + nblk;
+  if (blk_in_smem) {
+    for (int b = warp; b < nblk; b += NWARP) {
+      const int g = b * 32 + lane;
+      const float v = g < ng ? s1[g] : 1e10f;
+      const float mnv = warp_min(v), mxv = warp_max(g < ng ? v : -1e10f);
+      if (lane == 0) {
+        bmin[b] = mnv;
+        bmax[b] = mxv;
+      }
     }
-    mn = warp_min(mn);
-    mx = warp_max(mx);
-    if (lane == 0) {
-      float sc2 = __fdiv_rn(__fsub_rn(mx, mn), 15.0f);
-      if (sc2 < 1e-10f) sc2 = 1e-10f;
-      const int z2 = f2i_rz(roundf(__fdiv_rn(-mn, sc2)));
-      const int slot = ci < cl.ntab_full ? ci : cl.ntab_full;
-      a.ws.chunk_tab[slot] =
-          make_float4(mn, sc2, __int_as_float((int)__half_as_ushort(__float2half_rn(sc2))),
-                      __int_as_float((int)(int8_t)z2));
-    }
+    sync_nt<NT>();
   }
-  // group order for encode: 2-bit groups first, then 4-bit, each ascending,
-  // so that a warp of encode threads shares one precision
-  if (rebuild_order) {
-    const int per = (ng + NT - 1) / NT;
-    const int i0 = min(ng, tid * per), i1 = min(ng, i0 + per);
-    uint32_t n2 = 0;
-    for (int i = i0; i < i1; ++i) n2 += (a.ws.prec[i] == 0);
-    uint32_t incl = n2;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += y;
+  // min / max of scales over groups [g0, g0 + n) cyclically
+  auto range_minmax = [&](int g0, int n, float& mn, float& mx) {
+    int g = g0, left = n;
+    while (left > 0) {
+      if (g >= ng) g -= ng;
+      if (blk_in_smem && (g & 31) == 0 && left >= 32 && g + 32 <= ng) {
+        mn = fminf(mn, bmin[g >> 5]);
+        mx = fmaxf(mx, bmax[g >> 5]);
+        g += 32;
+        left -= 32;
+      } else {
+        const float v = scale_of(g);
+        mn = fminf(mn, v);
+        mx = fmaxf(mx, v);
+        ++g;
+        --left;
+      }
     }
-    sync_nt<NT>();
-    if (lane == 31) s_wsum[warp] = incl;
-    sync_nt<NT>();
-    uint32_t off = 0, total2 = 0;
-#pragma unroll
-    for (int w = 0; w < NWARP; ++w) {
-      if (w < warp) off += s_wsum[w];
-      total2 += s_wsum[w];
+  };
+  for (int ci = tid; ci < nchunks; ci += NT) {
+    const int64_t cidx = ci < cl.ntab_full ? ci : cl.nfull;  // the partial chunk is the last
+    const int64_t s0 = cidx * kGroup2;
+    const int n = (int)min64(kGroup2, cl.total - s0);
+    float mn = 1e10f, mx = -1e10f;
+    if (n >= ng) {  // every group at least once
+      range_minmax(0, ng, mn, mx);
+    } else {
+      range_minmax((int)(s0 % ng), n, mn, mx);
     }
-    uint32_t pos2 = off + incl - n2;
-    uint32_t pos4 = total2 + (uint32_t)i0 - pos2;
-    for (int i = i0; i < i1; ++i) {
-      if (a.ws.prec[i] == 0)
-        a.ws.order[pos2++] = i;
-      else
-        a.ws.order[pos4++] = i;
-    }
-    if (tid == 0) a.ws.hdr->n2 = total2;
+    float sc2 = __fdiv_rn(__fsub_rn(mx, mn), 15.0f);
+    if (sc2 < 1e-10f) sc2 = 1e-10f;
+    const int z2 = f2i_rz(roundf(__fdiv_rn(-mn, sc2)));
+    const int slot = ci < cl.ntab_full ? ci : cl.ntab_full;
+    a.ws.chunk_tab[slot] =
+        make_float4(mn, sc2, __int_as_float((int)__half_as_ushort(__float2half_rn(sc2))),
+                    __int_as_float((int)(int8_t)z2));
   }
   sync_nt<NT>();
   if (tid == 0) {
@@ -1125,33 +1192,21 @@ __device__ void finalize_tables(const QArgs& a, float* s1, size_t s1_bytes, uint
   }
 }
 
-// Interval of group g's fp32 serial sum as sortable keys (lo rounded down,
-// hi rounded up).  NaN / inf groups are exact.
-__device__ __forceinline__ void sens_interval(const QArgs& a, int g, uint32_t& klo,
-                                              uint32_t& khi) {
-  const uint32_t f = __ldcg(a.ws.gflag + g);
-  if (f & kGrpNaN) {
-    klo = khi = 0xFFFFFFFFu;
-    return;
-  }
-  if (f & kGrpInf) {
-    klo = khi = 0x7F800000u;
-    return;
-  }
-  const double n = 16.0 * (double)a.M;
+// Interval of a group's fp32 serial sum as sortable keys (lo rounded down,
+// hi rounded up) from its flags, prediction P and moment (M rows of 16
+// terms).  NaN / inf groups are exact.
+__device__ __forceinline__ uint2 sens_interval_of(uint32_t f, double P, double mom, int64_t M) {
+  if (f & kGrpNaN) return make_uint2(0xFFFFFFFFu, 0xFFFFFFFFu);
+  if (f & kGrpInf) return make_uint2(0x7F800000u, 0x7F800000u);
+  const double n = 16.0 * (double)M;
   const double dcr = n * kEps24;
-  if ((f & kGrpLoose) || dcr >= 0.5) {
-    klo = 0u;
-    khi = 0x7F800000u;
-    return;
-  }
-  const double P = __ldcg(a.ws.gpred + g), mom = __ldcg(a.ws.gmom + g);
-  const double eps = 24.0 * kEps24;
+  if ((f & kGrpLoose) || dcr >= 0.5) return make_uint2(0u, 0x7F800000u);
+  const double eps = 32.0 * kEps24;
   const double D = dcr / (1.0 - dcr);
   const double E = kEps24 * (1.0 + eps) * (1.0 + D) * mom * (1.0 + 1e-6) + n * 0x1p-148;
   const double lo = fmax(P * (1.0 - eps) - E, 0.0), hi = P * (1.0 + eps) + E;
-  klo = __float_as_uint(__double2float_rd(lo));
-  khi = __float_as_uint(__double2float_ru(hi));  // +inf past FLT_MAX
+  return make_uint2(__float_as_uint(__double2float_rd(lo)),
+                    __float_as_uint(__double2float_ru(hi)));  // +inf past FLT_MAX
 }
 
 // The selection from the intervals (the last stats CTA; NT threads).  Group g
@@ -1165,36 +1220,27 @@ __device__ void select_from_intervals(const QArgs& a, uint8_t* scratch, size_t s
   const int ng = a.ng, n4 = a.n4;
   const int tid = threadIdx.x % NT, lane = threadIdx.x & 31, warp = tid >> 5;
   constexpr int NWARP = NT / 32;
-  __shared__ uint32_t hist[256];
-  __shared__ uint32_t s2[2];
+  __shared__ uint32_t hist[512];
+  __shared__ uint32_t s4[4];
   __shared__ uint32_t s_wsum[NWARP];
   __shared__ uint32_t s_cnt[2];
   __shared__ int s_irr;
-  uint32_t* klo = reinterpret_cast<uint32_t*>(scratch);
-  uint32_t* khi = klo + ng;
+  uint2* keys = reinterpret_cast<uint2*>(scratch);
   const bool keys_in_smem = (size_t)ng * 8 <= scratch_bytes;
-  auto lo_of = [&](int g) -> uint32_t {
-    if (keys_in_smem) return klo[g];
-    uint32_t l, h;
-    sens_interval(a, g, l, h);
-    return l;
-  };
-  auto hi_of = [&](int g) -> uint32_t {
-    if (keys_in_smem) return khi[g];
-    uint32_t l, h;
-    sens_interval(a, g, l, h);
-    return h;
-  };
+  auto lo_of = [&](int g) -> uint32_t { return keys_in_smem ? keys[g].x : __ldcg(a.ws.gkey + g).x; };
+  auto hi_of = [&](int g) -> uint32_t { return keys_in_smem ? keys[g].y : __ldcg(a.ws.gkey + g).y; };
   int pending = 0;
   if (a.select && n4 > 0) {
     if (keys_in_smem)
-      for (int g = tid; g < ng; g += NT) sens_interval(a, g, klo[g], khi[g]);
+      for (int g = tid; g < ng; g += NT) keys[g] = __ldcg(a.ws.gkey + g);
     if (tid == 0) s_cnt[0] = s_cnt[1] = 0;
     sync_nt<NT>();
-    uint32_t eq;
-    const uint32_t Alo = kth_largest<NT>(ng, n4, lo_of, hist, s2, &eq);
     const bool all_in = n4 >= ng;
-    const uint32_t Bhi = all_in ? 0u : kth_largest<NT>(ng, n4 + 1, hi_of, hist, s2, &eq);
+    uint32_t Alo = 0, Bhi = 0;
+    if (all_in)
+      kth_largest2<NT>(ng, n4, lo_of, n4, hi_of, hist, s4, Alo, Bhi);
+    else
+      kth_largest2<NT>(ng, n4, lo_of, n4 + 1, hi_of, hist, s4, Alo, Bhi);
     uint32_t c_in = 0, c_pend = 0;
     for (int g = tid; g < ng; g += NT) {
       const uint32_t l = lo_of(g), h = hi_of(g);
@@ -1275,180 +1321,329 @@ __device__ void select_from_intervals(const QArgs& a, uint8_t* scratch, size_t s
 }
 
 // ---------------------------------------------------------------------------
-// stats kernel: one CTA per 128 x 128 tile (row chunks of a column tile are
-// consecutive blocks), one warp per group.
+// stats kernel: persistent CTAs over the 128 x 128 tiles (row chunks of a
+// column tile are consecutive tile indices), two tile buffers so the next
+// tile's TMA load overlaps the current tile's work, one warp per group.
 // ---------------------------------------------------------------------------
+
+// w*w of the two fp16 values of `w`, accumulated into a0 / a1 in fp32 (the
+// squares are exact in fp32; one rounding per add).
+__device__ __forceinline__ void sq_acc2(uint32_t w, float& a0, float& a1) {
+  asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\t"
+      "fma.rn.f32.f16 %0, l, l, %0;\n\tfma.rn.f32.f16 %1, h, h, %1;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "r"(w));
+}
+
+// Issue the TMA loads of tile `t` (two 64-column boxes) into `dst`.
+__device__ __forceinline__ void tile_load(const CUtensorMap* tmap, uint64_t* bar, uint8_t* dst,
+                                          int64_t t, int nct) {
+  const int rc = (int)(t / nct), ct = (int)(t % nct);
+  mbar_arrive_expect_tx(bar, kTileBytes);
+  tma_load_2d(dst, tmap, bar, ct * kTileCols, rc * kChunkRows);
+  tma_load_2d(dst + kBoxBytes, tmap, bar, ct * kTileCols + 64, rc * kChunkRows);
+}
+
+// The same swizzled tile layout from plain loads (inputs TMA cannot take);
+// `fill` outside the matrix.
+__device__ __forceinline__ void tile_fill(const __half* W, int64_t M, int64_t K, uint8_t* dst,
+                                          int64_t t, int nct, uint16_t fill) {
+  const int rc = (int)(t / nct), ct = (int)(t % nct);
+  for (int e = threadIdx.x; e < kChunkRows * kTileCols; e += blockDim.x) {
+    const int r = e / kTileCols, c = e % kTileCols;
+    const int64_t gr = (int64_t)rc * kChunkRows + r, gc = (int64_t)ct * kTileCols + c;
+    const uint16_t v = (gr < M && gc < K) ? __half_as_ushort(W[gr * K + gc]) : fill;
+    const int half = c >> 6, cc = c & 63;
+    *reinterpret_cast<uint16_t*>(dst + half * kBoxBytes + r * 128 +
+                                 (((cc >> 3) ^ (r & 7)) << 4) + (cc & 7) * 2) = v;
+  }
+}
+
+// The last CTA of a column tile: totals, flags, min / max and parameters of
+// its groups (one warp per group).
 template <bool kSens>
-__global__ void __launch_bounds__(kStatsThreads)
-    stats_kernel(const __grid_constant__ CUtensorMap tmap, const QArgs A, int use_tma) {
-  extern __shared__ uint8_t dsm_raw[];
-  uint8_t* buf = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) &
-                                            ~(uintptr_t)1023);
-  __shared__ uint64_t full_bar;
-  __shared__ GroupDiv s_div[kTileGroups];
-  __shared__ int s_flag;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int64_t M = A.M, K = A.K;
-  const int nct = A.nct, nrc = A.nrc;
-  const int rc = (int)(blockIdx.x % (unsigned)nrc), ct = (int)(blockIdx.x / (unsigned)nrc);
-  const int64_t row0 = (int64_t)rc * kChunkRows;
-
-  if (use_tma) {
-    if (tid == 0) {
-      mbar_init(&full_bar, 1);
-      fence_mbar_init();
-      mbar_arrive_expect_tx(&full_bar, kTileBytes);
-      tma_load_2d(buf, &tmap, &full_bar, ct * kTileCols, (int)row0);
-      tma_load_2d(buf + kBoxBytes, &tmap, &full_bar, ct * kTileCols + 64, (int)row0);
-    }
-  } else {
-    // the same swizzled layout from plain loads; NaN outside the matrix
-    for (int e = tid; e < kChunkRows * kTileCols; e += kStatsThreads) {
-      const int r = e / kTileCols, c = e % kTileCols;
-      const int64_t gr = row0 + r, gc = (int64_t)ct * kTileCols + c;
-      const uint16_t v =
-          (gr < M && gc < K) ? __half_as_ushort(A.W[gr * K + gc]) : (uint16_t)0x7E00;
-      const int half = c >> 6, cc = c & 63;
-      *reinterpret_cast<uint16_t*>(buf + half * kBoxBytes + r * 128 +
-                                   (((cc >> 3) ^ (r & 7)) << 4) + (cc & 7) * 2) = v;
-    }
-  }
-  const int gi = warp;
-  const int64_t g = (int64_t)ct * kTileGroups + gi;
-  const int64_t c0 = g * kGroup1;
-  bool loose = false;
-  if (kSens && g < A.ng) loose = !load_group_div(A.hess, c0, K, lane, &s_div[gi]);
-  bool ok = true;
-  if (use_tma && tid == 0) ok = mbar_wait(&full_bar, 0);
-  if (__syncthreads_or(!ok)) {
-    if (tid == 0) {
-      atomicOr(&A.ws.hdr->status, kStatusTimeout);
-      (void)mbar_wait(&full_bar, 0);  // bounded: the loads must land before exit
-    }
-  }
-  __syncthreads();
-
-  if (g < A.ng) {
-    const int gs = (int)min64(kGroup1, K - c0);
-    const uint32_t cmask = gs >= 16 ? 0xFFFFu : ((1u << gs) - 1u);
-    const bool edge = (row0 + kChunkRows > M) || gs < kGroup1;
-    const size_t rec = (size_t)g * nrc + rc;
-    __half2 hmn = __float2half2_rn(INFINITY), hmx = __float2half2_rn(-INFINITY);
-    const __half2 hnan = __float2half2_rn(NAN);
-    double csum = 0.0;
-    bool any_nan = false, any_inf = false;
+__device__ __noinline__ void ct_assemble(const QArgs& A, int ct, int warp, int lane) {
+  const int64_t M = A.M;
+  const int nrc = A.nrc;
+  const int64_t g = (int64_t)ct * kTileGroups + warp;
+  if (g >= A.ng) return;
+  float mn = INFINITY, mx = -INFINITY;
+  bool any_nan = false, any_inf = false, loose = false;
+  double carry = 0.0, mom = 0.0;
+  for (int j0 = 0; j0 < nrc; j0 += 96) {
+    // up to three chunks per lane in flight
+    float2 mm[3];
+    float4 cc[3][4];
 #pragma unroll
-    for (int s = 0; s < kSteps; ++s) {
-      const int r = s * 32 + lane;
-      const bool rvalid = row0 + r < M;
-      const Row16 v = tile_run(buf, gi, r);
-      const uint32_t vmask = rvalid ? cmask : 0u;
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        __half2 w2 = as_h2(row_word(v, k));
-        if (edge) {
-          const bool v0 = (vmask >> (2 * k)) & 1u, v1 = (vmask >> (2 * k + 1)) & 1u;
-          w2 = __halves2half2(v0 ? __low2half(w2) : __low2half(hnan),
-                              v1 ? __high2half(w2) : __high2half(hnan));
-        }
-        hmn = __hmin2(hmn, w2);
-        hmx = __hmax2(hmx, w2);
-      }
-      if (kSens) {
-        uint64_t X2[8];
-        run_squares(v, vmask, X2);
-        const float p = run_pred(X2, s_div[gi].R2);
-        any_nan |= isnan(p);
-        any_inf |= isinf(p);
-        csum += isfinite(p) ? (double)p : 0.0;
-      }
-    }
-    float mn = fminf(__half2float(__low2half(hmn)), __half2float(__high2half(hmn)));
-    float mx = fmaxf(__half2float(__low2half(hmx)), __half2float(__high2half(hmx)));
-    mn = warp_min(mn);
-    mx = warp_max(mx);
-    if (kSens) {
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) csum += __shfl_xor_sync(0xffffffffu, csum, o);
-      const uint32_t fl = (__any_sync(0xffffffffu, any_nan) ? kGrpNaN : 0u) |
-                          (__any_sync(0xffffffffu, any_inf) ? kGrpInf : 0u) |
-                          (loose ? kGrpLoose : 0u);
-      if (lane == 0) {
-        A.ws.cpred[rec] = csum;
-        A.ws.cflag[rec] = fl;
-      }
-    }
-    if (lane == 0) A.ws.cminmax[rec] = make_float2(mn, mx);
-  }
-  // zero this tile's share of the per-row outlier counts
-  if (ct == 0)
-    for (int r = tid; r < kChunkRows; r += kStatsThreads)
-      if (row0 + r < M) A.ws.row_counts[row0 + r] = 0;
-
-  // ---- last tile of the column tile: its groups' totals and parameters ----
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) s_flag = atomicAdd(&A.ws.ct_count[ct], 1u) == (unsigned)nrc - 1u;
-  __syncthreads();
-  if (!s_flag) return;
-  __threadfence();
-  if (g < A.ng) {
-    float mn = INFINITY, mx = -INFINITY;
-    uint32_t flags = 0;
-    double carry = 0.0, mom = 0.0;
-    for (int j0 = 0; j0 < nrc; j0 += 32) {
-      const int j = j0 + lane;
+    for (int u = 0; u < 3; ++u) {
+      const int j = j0 + 32 * u + lane;
       const size_t rec = (size_t)g * nrc + j;
-      double v = 0.0;
+      mm[u] = make_float2(INFINITY, -INFINITY);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) cc[u][q] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (j < nrc) {
-        const float2 m = __ldcg(A.ws.cminmax + rec);
-        mn = fminf(mn, m.x);
-        mx = fmaxf(mx, m.y);
+        mm[u] = __ldcg(A.ws.cminmax + rec);
         if (kSens) {
-          v = __ldcg(A.ws.cpred + rec);
-          flags |= __ldcg(A.ws.cflag + rec);
+          const float4* src = reinterpret_cast<const float4*>(A.ws.ccol + rec * 16);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) cc[u][q] = __ldcg(src + q);
         }
       }
+    }
+    // RN(1/h) of the group's 16 columns (1 where the reference does not divide)
+    float rc16[16];
+    if (kSens) {
+      const int64_t c0 = g * kGroup1;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        float r = 1.0f;
+        if (c0 + c < A.K) {
+          const float h = __ldg(A.hess + c0 + c);
+          if (h > 1e-8f) {
+            r = __frcp_rn(h);
+            loose |= !(h >= 0x1p-60f && h <= 0x1p60f);
+          }
+        }
+        rc16[c] = r;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 3; ++u) {
+      const int j = j0 + 32 * u + lane;
+      mn = fminf(mn, mm[u].x);
+      mx = fmaxf(mx, mm[u].y);
       if (kSens) {
+        double v = 0.0;
+        if (j < nrc) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float cv[4] = {cc[u][q].x, cc[u][q].y, cc[u][q].z, cc[u][q].w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              any_nan |= isnan(cv[e]);
+              any_inf |= isinf(cv[e]);
+              if (isfinite(cv[e])) v += (double)cv[e] * (double)rc16[4 * q + e];
+            }
+          }
+          A.ws.cpred[(size_t)g * nrc + j] = v;
+        }
         double incl = v;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
           const double y = __shfl_up_sync(0xffffffffu, incl, o);
           if (lane >= o) incl += y;
         }
-        const double terms = 16.0 * (double)min64(kChunkRows, M - (int64_t)j * kChunkRows);
-        if (j < nrc) mom += terms * (carry + incl);
+        const double terms =
+            j < nrc ? 16.0 * (double)min64(kChunkRows, M - (int64_t)j * kChunkRows) : 0.0;
+        mom += terms * (carry + incl);
         carry += __shfl_sync(0xffffffffu, incl, 31);
       }
     }
-    mn = warp_min(mn);
-    mx = warp_max(mx);
-    // the reference starts from +-1e10f and ignores NaN: clamp the exact min / max
-    mn = fminf(1e10f, mn);
-    mx = fmaxf(-1e10f, mx);
-    if (kSens) {
+  }
+  mn = warp_min(mn);
+  mx = warp_max(mx);
+  // the reference starts from +-1e10f and ignores NaN: clamp the exact min / max
+  mn = fminf(1e10f, mn);
+  mx = fmaxf(-1e10f, mx);
+  if (kSens) {
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) mom += __shfl_xor_sync(0xffffffffu, mom, o);
-      flags = __reduce_or_sync(0xffffffffu, flags);
-    }
+    for (int o = 16; o > 0; o >>= 1) mom += __shfl_xor_sync(0xffffffffu, mom, o);
+    const uint32_t flags = (__any_sync(0xffffffffu, any_nan) ? kGrpNaN : 0u) |
+                           (__any_sync(0xffffffffu, any_inf) ? kGrpInf : 0u) |
+                           (__any_sync(0xffffffffu, loose) ? kGrpLoose : 0u);
     if (lane == 0) {
-      A.ws.gmin[g] = mn;
-      A.ws.gmax[g] = mx;
+      A.ws.gpred[g] = carry;
+      A.ws.gmom[g] = mom;
+      A.ws.gflag[g] = flags;
+      A.ws.gkey[g] = sens_interval_of(flags, carry, mom, M);
+    }
+  }
+  if (lane == 0) {
+    A.ws.gmin[g] = mn;
+    A.ws.gmax[g] = mx;
+  }
+  group_params_warp(A.ws.params, A.ws.gscale, A.ws.greg, g, mn, mx, lane);
+}
+
+__device__ __noinline__ void select_all(const QArgs& A, uint8_t* scratch) {
+  select_from_intervals<kStatsThreads>(A, scratch, kTileBytes);
+}
+
+// Tile ring of a persistent CTA: kStages tile buffers fed by TMA; CTA b takes
+// tiles b, b + grid, b + 2 grid, ... (tile t covers row chunk t / nct and
+// column tile t % nct, so tiles in flight together span whole rows of W).  Thread 0 refills a stage as soon as the CTA is
+// done with it, so kStages - 1 loads stay in flight while the warps work.
+template <int S>
+struct TileRing {
+  uint64_t full[S];
+  int64_t tile[S];
+  uint32_t parity_pending;  // bit s: a load into stage s was issued and not waited for
+};
+
+// Load tile t (if it exists) into stage s; thread 0.
+template <int S>
+__device__ __forceinline__ void ring_issue(TileRing<S>& R, int s, const CUtensorMap* tmap,
+                                           uint8_t* dsm, int64_t t, int64_t ntiles, int nct,
+                                           bool use_tma) {
+  R.tile[s] = t;
+  if (use_tma && t < ntiles) {
+    fence_proxy_async_smem();
+    tile_load(tmap, &R.full[s], dsm + (size_t)s * kTileBytes, t, nct);
+    R.parity_pending |= 1u << s;
+  }
+}
+
+// Wait (thread 0) for the load of iteration i; false on timeout.
+template <int S>
+__device__ __forceinline__ bool ring_wait(TileRing<S>& R, int s, int i) {
+  const bool ok = mbar_wait(&R.full[s], (uint32_t)((i / S) & 1));
+  if (ok) R.parity_pending &= ~(1u << s);
+  return ok;
+}
+
+// Before exit (thread 0): loads still in flight must land.
+template <int S>
+__device__ __forceinline__ void ring_drain(TileRing<S>& R, int i_next) {
+  for (int k = 0; k < S; ++k) {
+    const int i = i_next + k, s = i % S;
+    if (R.parity_pending & (1u << s)) (void)mbar_wait(&R.full[s], (uint32_t)((i / S) & 1));
+  }
+}
+
+// stats: persistent CTAs streaming the tiles, one warp per group of the
+// current tile: per (group, row chunk) min / max and the per-column sums of
+// w*w (the sensitivity prediction before the division by h).
+template <bool kSens>
+__global__ void __launch_bounds__(kStatsThreads, 2)
+    stats_kernel(const __grid_constant__ CUtensorMap tmap, const QArgs A, int use_tma) {
+  extern __shared__ uint8_t dsm_raw[];
+  uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) &
+                                            ~(uintptr_t)1023);
+  __shared__ TileRing<kStages> R;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t M = A.M, K = A.K;
+  const int nrc = A.nrc, nct = A.nct;
+  const int64_t ntiles = (int64_t)nct * nrc;
+  if (tid == 0) {
+    R.parity_pending = 0;
+    for (int s = 0; s < kStages; ++s) mbar_init(&R.full[s], 1);
+    fence_mbar_init();
+    for (int s = 0; s < kStages; ++s)
+      ring_issue(R, s, &tmap, dsm, blockIdx.x + (int64_t)s * gridDim.x, ntiles, nct, use_tma);
+  }
+  __syncthreads();
+  bool failed = false;
+  int i = 0;
+  for (;; ++i) {
+    const int st = i % kStages;
+    const int64_t t = R.tile[st];
+    if (t >= ntiles) break;
+    uint8_t* buf = dsm + (size_t)st * kTileBytes;
+    const int rc = (int)(t / nct), ct = (int)(t % nct);
+    const int64_t row0 = (int64_t)rc * kChunkRows;
+    const int gi = warp;
+    const int64_t g = (int64_t)ct * kTileGroups + gi;
+    const int64_t c0 = g * kGroup1;
+    if (use_tma) {
+      bool ok = true;
+      if (tid == 0) ok = ring_wait(R, st, i);
+      failed |= __syncthreads_or(!ok) != 0;
+    } else {
+      tile_fill(A.W, M, K, buf, t, nct, 0x7E00);
+      __syncthreads();
+    }
+    if (g < A.ng) {
+      const int gs = (int)min64(kGroup1, K - c0);
+      const uint32_t cmask = gs >= 16 ? 0xFFFFu : ((1u << gs) - 1u);
+      const bool edge = (row0 + kChunkRows > M) || gs < kGroup1;
+      const size_t rec = (size_t)g * nrc + rc;
+      __half2 hmn = __float2half2_rn(INFINITY), hmx = __float2half2_rn(-INFINITY);
+      float acc[16];
+#pragma unroll
+      for (int c = 0; c < 16; ++c) acc[c] = 0.0f;
+#pragma unroll
+      for (int s = 0; s < kSteps; ++s) {
+        const int r = s * 32 + lane;
+        const Row16 v = tile_run(buf, gi, r);
+        const uint32_t vmask = row0 + r < M ? cmask : 0u;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t w = row_word(v, k);
+          uint32_t wm = w, ws = w;
+          if (edge) {  // outside the matrix: NaN for min / max (ignored), 0 for sums
+            const uint32_t keep = (((vmask >> (2 * k)) & 1u) ? 0x0000FFFFu : 0u) |
+                                  (((vmask >> (2 * k + 1)) & 1u) ? 0xFFFF0000u : 0u);
+            ws = w & keep;
+            wm = ws | (0x7E007E00u & ~keep);
+          }
+          hmn = __hmin2(hmn, as_h2(wm));
+          hmx = __hmax2(hmx, as_h2(wm));
+          if (kSens) sq_acc2(ws, acc[2 * k], acc[2 * k + 1]);
+        }
+      }
+      float mn = fminf(__half2float(__low2half(hmn)), __half2float(__high2half(hmn)));
+      float mx = fmaxf(__half2float(__low2half(hmx)), __half2float(__high2half(hmx)));
+      mn = warp_min(mn);
+      mx = warp_max(mx);
+      if (lane == 0) A.ws.cminmax[rec] = make_float2(mn, mx);
       if (kSens) {
-        A.ws.gpred[g] = carry;
-        A.ws.gmom[g] = mom;
-        A.ws.gflag[g] = flags;
+        // per-column sums over the chunk's rows by a transposing butterfly:
+        // each step halves the columns a lane holds; lane l ends with column
+        // 8 b4 + 4 b3 + 2 b2 + b1 (bits of l)
+        float a8[8], a4[4], a2[2];
+        const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4, b1 = lane & 2;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          a8[j] = __fadd_rn(b4 ? acc[8 + j] : acc[j],
+                            __shfl_xor_sync(0xffffffffu, b4 ? acc[j] : acc[8 + j], 16));
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          a4[j] = __fadd_rn(b3 ? a8[4 + j] : a8[j],
+                            __shfl_xor_sync(0xffffffffu, b3 ? a8[j] : a8[4 + j], 8));
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+          a2[j] = __fadd_rn(b2 ? a4[2 + j] : a4[j],
+                            __shfl_xor_sync(0xffffffffu, b2 ? a4[j] : a4[2 + j], 4));
+        float a1 = __fadd_rn(b1 ? a2[1] : a2[0], __shfl_xor_sync(0xffffffffu, b1 ? a2[0] : a2[1], 2));
+        a1 = __fadd_rn(a1, __shfl_xor_sync(0xffffffffu, a1, 1));
+        const int col = (b4 ? 8 : 0) + (b3 ? 4 : 0) + (b2 ? 2 : 0) + (b1 ? 1 : 0);
+        if (!(lane & 1)) A.ws.ccol[rec * 16 + col] = a1;
       }
     }
-    group_params_warp(A.ws.params, g, mn, mx, lane);
+    // zero this tile's share of the per-row outlier counts
+    if (ct == 0)
+      for (int r = tid; r < kChunkRows; r += kStatsThreads)
+        if (row0 + r < M) A.ws.row_counts[row0 + r] = 0;
+    __syncthreads();  // the stage is free
+    if (tid == 0)
+      ring_issue(R, st, &tmap, dsm, t + (int64_t)kStages * gridDim.x, ntiles, nct, use_tma);
   }
+  grid_launch_dependents();
+  if (tid == 0) {
+    if (failed) atomicOr(&A.ws.hdr->status, kStatusTimeout);
+    ring_drain(R, i);
+  }
+}
+
+// assemble: one CTA per column tile, one warp per group: totals, flags,
+// min / max and parameters from the chunk records; the last CTA selects.
+template <bool kSens>
+__global__ void __launch_bounds__(kStatsThreads) assemble_kernel(const QArgs A) {
+  extern __shared__ uint8_t dsm_raw[];
+  uint8_t* scratch = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 15) &
+                                                ~(uintptr_t)15);
+  __shared__ int s_flag;
+  grid_launch_dependents();  // exact / encode may start loading W
+  grid_dependency_wait();    // the chunk records are complete
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  ct_assemble<kSens>(A, blockIdx.x, warp, lane);
   __threadfence();
   __syncthreads();
-  if (tid == 0) s_flag = atomicAdd(&A.ws.hdr->ticket_ct, 1u) == (unsigned)nct - 1u;
+  if (tid == 0) s_flag = atomicAdd(&A.ws.hdr->ticket_ct, 1u) == gridDim.x - 1u;
   __syncthreads();
   if (!s_flag) return;
   __threadfence();
-  select_from_intervals<kStatsThreads>(A, buf, kTileBytes);
+  select_all(A, scratch);
 }
 
 // ---------------------------------------------------------------------------
@@ -1462,95 +1657,199 @@ __device__ __forceinline__ bool is_outlier(float x, float scale, int zero, float
   return err > thr;
 }
 
+// Codes of one run (16 values of one row) of a group: the 2-bit word (wa) or
+// the two 4-bit words (wa, wb), and the number of outliers.  Regular groups
+// compare against the code thresholds (packed half2: each comparison adds 1
+// to a 1024 + code accumulator, whose low mantissa bits are the code);
+// others evaluate the reference formula per element (quantize.cu:178-240).
+struct EncGroup {
+  uint4 tA, tB;  // thresholds T_1..T_15 (fp16 patterns)
+  float gmin, scale, thr;
+  int zero, levels, gs;
+  bool four, regular;
+};
+
+__device__ __forceinline__ EncGroup enc_group_of(const GroupParams& pp, int64_t K, int g,
+                                                 bool four) {
+  EncGroup e;
+  e.tA = *reinterpret_cast<const uint4*>(&pp.thresh[0]);
+  e.tB = *reinterpret_cast<const uint4*>(&pp.thresh[8]);
+  e.gmin = pp.gmin;
+  e.scale = pp.scale;
+  e.thr = pp.thr;
+  e.zero = pp.zero;
+  e.levels = pp.levels;
+  e.gs = (int)min64(kGroup1, K - (int64_t)g * kGroup1);
+  e.four = four;
+  e.regular = (pp.flags & kFlagRegular) != 0;
+  return e;
+}
+
+__device__ __forceinline__ EncGroup enc_group(const QArgs& a, int g, bool four) {
+  return enc_group_of(a.ws.params[2 * g + (four ? 1 : 0)], a.K, g, four);
+}
+
+__device__ __forceinline__ int encode_run(const Row16& v, const EncGroup& e, uint32_t& wa,
+                                          uint32_t& wb) {
+  wa = wb = 0;
+  int cnt = 0;
+  const int gs = e.gs;
+  if (e.regular) {
+    auto T2 = [&](int j) -> __half2 {  // threshold j as a broadcast half2
+      const uint32_t w = j < 8 ? (&e.tA.x)[j >> 1] : (&e.tB.x)[(j - 8) >> 1];
+      const uint16_t h = (j & 1) ? (uint16_t)(w >> 16) : (uint16_t)(w & 0xFFFFu);
+      return __half2half2(__ushort_as_half(h));
+    };
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const __half2 w2 = as_h2(row_word(v, k));
+      __half2 acc = __float2half2_rn(1024.0f);
+      if (!e.four) {
+#pragma unroll
+        for (int j = 0; j < 3; ++j) acc = __hadd2(acc, __hge2(w2, T2(j)));
+      } else {
+#pragma unroll
+        for (int j = 0; j < 15; ++j) acc = __hadd2(acc, __hge2(w2, T2(j)));
+      }
+      // 1024 has an fp16 ulp of 1: the code sits in the low mantissa bits
+      const uint32_t b = h2_bits(acc);
+      if (!e.four) {
+        wa |= ((b & 0x3u) | ((b >> 14) & 0xCu)) << (4 * k);
+      } else {
+        const uint32_t t = (b & 0xFu) | ((b >> 12) & 0xF0u);
+        if (k < 4)
+          wa |= t << (8 * k);
+        else
+          wb |= t << (8 * (k - 4));
+      }
+    }
+    if (gs < kGroup1) {  // columns past K hold code 0 in the reference
+      if (!e.four) {
+        wa &= (1u << (2 * gs)) - 1u;
+      } else {
+        wa &= gs >= 8 ? 0xFFFFFFFFu : ((1u << (4 * gs)) - 1u);
+        wb &= gs <= 8 ? 0u : ((1u << (4 * (gs - 8))) - 1u);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      if (i < gs) {
+        const float x = row_elem(v, i);
+        const int q = code_of(x, e.gmin, e.scale, e.levels);
+        cnt += is_outlier(x, e.scale, e.zero, e.thr, q, kOutlierFma);
+        if (!e.four)
+          wa |= (uint32_t)(q & 0x3) << (2 * i);
+        else if (i < 8)
+          wa |= (uint32_t)(q & 0xF) << (4 * i);
+        else
+          wb |= (uint32_t)(q & 0xF) << (4 * (i - 8));
+      }
+    }
+  }
+  return cnt;
+}
+
+// Compact form of encode_run for the tile kernel: one loop over the group's
+// thresholds (read from shared memory, broadcast), 8 words per step, shared
+// by both precisions; the rare irregular groups loop over the elements of the
+// run in the tile (shared memory) instead of unrolling.
+__device__ __forceinline__ int encode_run_tile(const Row16& v, const GroupParams& gp,
+                                               const uint8_t* row_base, int lo_off, int hi_off,
+                                               int gs, uint32_t& wa, uint32_t& wb) {
+  const bool four = gp.levels == 16;
+  wa = wb = 0;
+  if (gp.flags & kFlagRegular) {
+    __half2 acc[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc[k] = __float2half2_rn(1024.0f);
+    const int nt = gp.levels - 1;
+#pragma unroll 1
+    for (int j = 0; j < nt; ++j) {
+      const __half2 T = __half2half2(__ushort_as_half(gp.thresh[j]));
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc[k] = __hadd2(acc[k], __hge2(as_h2(row_word(v, k)), T));
+    }
+    // 1024 has an fp16 ulp of 1: the code sits in the low mantissa bits
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const uint32_t b = h2_bits(acc[k]);
+      if (!four) {
+        wa |= ((b & 0x3u) | ((b >> 14) & 0xCu)) << (4 * k);
+      } else {
+        const uint32_t t = (b & 0xFu) | ((b >> 12) & 0xF0u);
+        if (k < 4)
+          wa |= t << (8 * k);
+        else
+          wb |= t << (8 * (k - 4));
+      }
+    }
+    if (gs < kGroup1) {  // columns past K hold code 0 in the reference
+      if (!four) {
+        wa &= (1u << (2 * gs)) - 1u;
+      } else {
+        wa &= gs >= 8 ? 0xFFFFFFFFu : ((1u << (4 * gs)) - 1u);
+        wb &= gs <= 8 ? 0u : ((1u << (4 * (gs - 8))) - 1u);
+      }
+    }
+    return 0;
+  }
+  int cnt = 0;
+#pragma unroll 1
+  for (int i = 0; i < gs; ++i) {
+    // element i of the run, from the tile (chunk offsets swizzled by the caller)
+    const uint16_t hb =
+        *reinterpret_cast<const uint16_t*>(row_base + (i < 8 ? lo_off : hi_off) + (i & 7) * 2);
+    const float x = __half2float(__ushort_as_half(hb));
+    const int q = code_of(x, gp.gmin, gp.scale, gp.levels);
+    cnt += is_outlier(x, gp.scale, gp.zero, gp.thr, q, kOutlierFma);
+    if (!four)
+      wa |= (uint32_t)(q & 0x3) << (2 * i);
+    else if (i < 8)
+      wa |= (uint32_t)(q & 0xF) << (4 * i);
+    else
+      wb |= (uint32_t)(q & 0xF) << (4 * (i - 8));
+  }
+  return cnt;
+}
+
+// 2nd-order code of scales_1st[r, g] (quantize.cu:274-280); u_r = (r * ng)
+// mod (period * 256) locates the flat index r * ng + g within one period of
+// full chunks.
+__device__ __forceinline__ uint8_t second_order_code(const QArgs& a, const float4* tab, float s1f,
+                                                     int64_t r, int g, int u_r) {
+  const ChunkLayout& cl = a.cl;
+  const int64_t si = r * a.ng + g;
+  int idx = cl.ntab_full;
+  if (si < cl.nfull * kGroup2) {
+    int jt = u_r + g;
+    if (jt >= cl.period * kGroup2) jt -= cl.period * kGroup2;
+    idx = jt >> 8;
+  }
+  const float4 ch = tab[idx];
+  const int q2 = f2i_rz(roundf(__fdiv_rn(__fsub_rn(s1f, ch.x), ch.y)));
+  return (uint8_t)max(0, min(15, q2));
+}
+
+// Rows [r0, r1) of group g, one thread (the pending groups, in `post`).
 __device__ void encode_rows(const QArgs& a, int g, int64_t r0, int64_t r1) {
   const int64_t K = a.K;
   const int ng = a.ng;
   const bool four = a.ws.prec[g] != 0;
-  const GroupParams& pp = a.ws.params[2 * g + (four ? 1 : 0)];
-  const float gmin = pp.gmin, scale = pp.scale, thr = pp.thr;
-  const int zero = pp.zero, levels = pp.levels;
-  const bool regular = (pp.flags & kFlagRegular) != 0;
-  const __half sh = __ushort_as_half((uint16_t)pp.scale_h);
+  const EncGroup e = enc_group(a, g, four);
+  const __half sh = __ushort_as_half((uint16_t)a.ws.params[2 * g + (four ? 1 : 0)].scale_h);
   const int64_t c0 = (int64_t)g * kGroup1;
-  const int gs = (int)min64(kGroup1, K - c0);
-  const bool vec = a.w_aligned && (gs == kGroup1) && ((K & 7) == 0);
-  const uint4 tA = *reinterpret_cast<const uint4*>(&pp.thresh[0]);
-  const uint4 tB = *reinterpret_cast<const uint4*>(&pp.thresh[8]);
-  // threshold j as a broadcast half2
-  auto T2 = [&](int j) -> __half2 {
-    const uint32_t w = j < 8 ? (&tA.x)[j >> 1] : (&tB.x)[(j - 8) >> 1];
-    const uint16_t h = (j & 1) ? (uint16_t)(w >> 16) : (uint16_t)(w & 0xFFFFu);
-    return __half2half2(__ushort_as_half(h));
-  };
-  // columns past K in a partial group hold code 0 in the reference
-  const uint32_t keep2 = gs >= 16 ? 0xFFFFFFFFu : ((1u << (2 * gs)) - 1u);
-  const uint32_t keep4a = gs >= 8 ? 0xFFFFFFFFu : ((1u << (4 * gs)) - 1u);
-  const uint32_t keep4b = gs >= 16 ? 0xFFFFFFFFu : (gs <= 8 ? 0u : ((1u << (4 * (gs - 8))) - 1u));
-  for (int64_t rb = r0; rb < r1; rb += 2) {
-    Row16 vb[2];
-#pragma unroll
-    for (int u = 0; u < 2; ++u)
-      if (rb + u < r1) vb[u] = load_row16(a.W, rb + u, K, c0, gs, vec);
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int64_t r = rb + u;
-      if (r >= r1) break;
-      const Row16& v = vb[u];
-      uint32_t wa = 0, wb = 0;
-      int cnt = 0;
-      if (regular) {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const __half2 w2 = as_h2(row_word(v, k));
-          __half2 acc = __float2half2_rn(1024.0f);
-          if (!four) {
-#pragma unroll
-            for (int j = 0; j < 3; ++j) acc = __hadd2(acc, __hge2(w2, T2(j)));
-          } else {
-#pragma unroll
-            for (int j = 0; j < 15; ++j) acc = __hadd2(acc, __hge2(w2, T2(j)));
-          }
-          // 1024 has an fp16 ulp of 1: the code sits in the low mantissa bits
-          const uint32_t b = h2_bits(acc);
-          if (!four) {
-            wa |= ((b & 0x3u) | ((b >> 14) & 0xCu)) << (4 * k);
-          } else {
-            const uint32_t t = (b & 0xFu) | ((b >> 12) & 0xF0u);
-            if (k < 4)
-              wa |= t << (8 * k);
-            else
-              wb |= t << (8 * (k - 4));
-          }
-        }
-        if (!four) {
-          wa &= keep2;
-        } else {
-          wa &= keep4a;
-          wb &= keep4b;
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          if (i < gs) {
-            const float x = row_elem(v, i);
-            const int q = code_of(x, gmin, scale, levels);
-            cnt += is_outlier(x, scale, zero, thr, q, kOutlierFma);
-            if (!four)
-              wa |= (uint32_t)(q & 0x3) << (2 * i);
-            else if (i < 8)
-              wa |= (uint32_t)(q & 0xF) << (4 * i);
-            else
-              wb |= (uint32_t)(q & 0xF) << (4 * (i - 8));
-          }
-        }
-      }
-      const int64_t si = r * ng + g;
-      a.packed2[si] = four ? 0 : (int32_t)wa;
-      reinterpret_cast<int2*>(a.packed4)[si] = four ? make_int2((int)wa, (int)wb) : make_int2(0, 0);
-      a.scales1[si] = sh;
-      a.zeros1[si] = (int8_t)zero;
-      if (cnt) atomicAdd(a.ws.row_counts + r, cnt);
-    }
+  const bool vec = a.w_aligned && (e.gs == kGroup1) && ((K & 7) == 0);
+  for (int64_t r = r0; r < r1; ++r) {
+    const Row16 v = load_row16(a.W, r, K, c0, e.gs, vec);
+    uint32_t wa, wb;
+    const int cnt = encode_run(v, e, wa, wb);
+    const int64_t si = r * ng + g;
+    a.packed2[si] = four ? 0 : (int32_t)wa;
+    reinterpret_cast<int2*>(a.packed4)[si] = four ? make_int2((int)wa, (int)wb) : make_int2(0, 0);
+    a.scales1[si] = sh;
+    a.zeros1[si] = (int8_t)e.zero;
+    if (cnt) atomicAdd(a.ws.row_counts + r, cnt);
   }
 }
 
@@ -1582,9 +1881,7 @@ __device__ __noinline__ void exact_ctas(const QArgs& a) {
     __threadfence();
     // the group's chunk programs are complete: its exact sum
     float S;
-    uint32_t fl = 0;
-    for (int j = lane; j < a.nrc; j += 32) fl |= __ldcg(a.ws.cflag + (size_t)g * a.nrc + j);
-    fl = __reduce_or_sync(0xffffffffu, fl);
+    const uint32_t fl = __ldcg(a.ws.gflag + g);
     if (fl & kGrpNaN)
       S = __int_as_float(0x7fc00000);
     else if (fl & kGrpInf)
@@ -1622,23 +1919,260 @@ __device__ __noinline__ void exact_ctas(const QArgs& a) {
   }
 }
 
-// encode grid: the first kExactCtas blocks compute exact sums of pending
-// groups (and exit at once when none are pending); the rest encode decided
-// group slots, one thread per (slot, block of kEncRows rows).
-__global__ void __launch_bounds__(256) encode_kernel(const QArgs a) {
-  grid_dependency_wait();  // stats (and its selection) complete
-  if (blockIdx.x < (unsigned)kExactCtas) {
-    exact_ctas(a);
-    return;
+// Exact sums of the pending groups: a kernel of its own between stats and
+// encode, which returns at once when nothing is pending.
+__global__ void __launch_bounds__(256) exact_kernel(const QArgs a) {
+  grid_launch_dependents();  // encode may start loading W
+  grid_dependency_wait();    // stats (and its selection) complete
+  exact_ctas(a);
+}
+
+// encode: persistent CTAs over the 128 x 128 tiles of W (from L2 through the
+// TMA tile ring; the first loads are issued before the wait for the
+// preceding kernels since W is an input), one warp per group (its precision
+// is uniform over the warp), lane = row.  Codes are staged in shared memory
+// and leave as whole tile rows: 16-byte stores of packed_2bit, packed_4bit,
+// scales_1st, and 8-byte stores of zeros_1st and scales_1st_quant.  Groups
+// still pending are left to `post`, and so are the 2nd-order codes when any
+// group is pending.
+constexpr int kEncTabMax = 64;  // 2nd-order table entries handled in shared memory
+
+// Staging of one tile's outputs, group-major so that a warp's 32 rows of one
+// group store to consecutive words (no bank conflicts); the write-out
+// gathers each output row from the 8 group columns.
+struct __align__(16) EncStage {
+  uint32_t p2[kTileGroups][kChunkRows];
+  uint2 p4[kTileGroups][kChunkRows];
+  uint8_t sq[kTileGroups][kChunkRows];
+  uint8_t q2[kTileGroups][kEncTabMax];  // 2nd-order code per (group, table entry)
+  uint16_t sh[kTileGroups];
+  int8_t z[kTileGroups];
+  uint8_t keep[kTileGroups];  // group decided: written here
+};
+
+// The next tile's group parameters (both precisions) and precisions, copied
+// asynchronously while the current tile is encoded.
+struct __align__(16) EncParamSlot {
+  GroupParams p[kTileGroups][2];
+  uint32_t prec[kTileGroups];
+};
+
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+}
+
+// Warp `warp` copies its group's two GroupParams (128 bytes: lanes 0-7) and
+// precision (lane 8) of tile t into slot `ps`.
+__device__ __forceinline__ void enc_prefetch(const QArgs& a, EncParamSlot& ps, int64_t t,
+                                             int warp, int lane) {
+  const int64_t g = (t % a.nct) * kTileGroups + warp;
+  if (g >= a.ng) return;
+  if (lane < 8) {
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(a.ws.params + 2 * g) + 16 * lane;
+    cp_async16(reinterpret_cast<uint8_t*>(&ps.p[warp][0]) + 16 * lane, src);
+  } else if (lane == 8) {
+    // the byte, 4-byte aligned below it (the reference's precisions are bytes)
+    const uintptr_t a4 = reinterpret_cast<uintptr_t>(a.ws.prec + g) & ~(uintptr_t)3;
+    cp_async4(&ps.prec[warp], reinterpret_cast<const void*>(a4));
   }
-  const int b = (int)blockIdx.x - kExactCtas;
-  const int bx = b % a.enc_nbx, by = b / a.enc_nbx;
-  const uint32_t ndec = a.ws.hdr->n_dec;
-  const int slot = bx * 256 + threadIdx.x;
-  if (slot >= (int)ndec) return;
-  const int g = a.ws.order[slot];
-  const int64_t r0 = (int64_t)by * kEncRows;
-  encode_rows(a, g, r0, min64(a.M, r0 + kEncRows));
+}
+
+__global__ void __launch_bounds__(256, 2)
+    encode_kernel(const __grid_constant__ CUtensorMap tmap, const QArgs a, int use_tma,
+                  int vec_out) {
+  extern __shared__ uint8_t dsm_raw[];
+  uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) &
+                                            ~(uintptr_t)1023);
+  __shared__ TileRing<kEncStages> R;
+  __shared__ EncStage st;
+  __shared__ EncParamSlot pslot[2];
+  __shared__ int s_u0;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t M = a.M;
+  const int ng = a.ng, nrc = a.nrc, nct = a.nct;
+  const int64_t ntiles = (int64_t)nct * nrc;
+  if (tid == 0) {  // W is an input: its loads may start before the wait below
+    R.parity_pending = 0;
+    for (int s = 0; s < kEncStages; ++s) mbar_init(&R.full[s], 1);
+    fence_mbar_init();
+    for (int s = 0; s < kEncStages; ++s)
+      ring_issue(R, s, &tmap, dsm, blockIdx.x + (int64_t)s * gridDim.x, ntiles, nct, use_tma);
+  }
+  grid_dependency_wait();  // the selection is complete
+  const bool write_sq = a.ws.hdr->n_pend == 0;
+  const int ntab = a.cl.ntab_full + 1;
+  const bool tab_smem = ntab <= kEncTabMax;  // else codes are computed per (row, group)
+  const float4* tab = a.ws.chunk_tab;
+  const int p256 = a.cl.period * kGroup2;
+  int dstep[kSteps];  // (32 s ng) mod (period * 256)
+#pragma unroll
+  for (int k = 0; k < kSteps; ++k) dstep[k] = (int)((32 * k * (int64_t)ng) % p256);
+  if ((int64_t)blockIdx.x < ntiles) enc_prefetch(a, pslot[0], blockIdx.x, warp, lane);
+  cp_async_commit();
+  __syncthreads();
+  bool failed = false;
+  int i = 0;
+  for (;; ++i) {
+    const int sg = i % kEncStages;
+    const int64_t t = R.tile[sg];
+    if (t >= ntiles) break;
+    uint8_t* buf = dsm + (size_t)sg * kTileBytes;
+    const int rc = (int)(t / nct), ct = (int)(t % nct);
+    const int64_t row0 = (int64_t)rc * kChunkRows;
+    if (tid == 0) s_u0 = (int)((row0 * (int64_t)ng) % p256);
+    cp_async_wait_all();  // this tile's parameters
+    __syncthreads();
+    // the next tile's parameters go into the other slot meanwhile
+    const int64_t tnext = t + gridDim.x;
+    if (tnext < ntiles) enc_prefetch(a, pslot[(i + 1) & 1], tnext, warp, lane);
+    cp_async_commit();
+    const EncParamSlot& ps = pslot[i & 1];
+    if (lane == 0) {
+      const int64_t gw = (int64_t)ct * kTileGroups + warp;
+      const uint8_t pw =
+          gw < ng ? (uint8_t)(ps.prec[warp] >> (8 * (int)((uintptr_t)(a.ws.prec + gw) & 3))) : 2;
+      st.keep[warp] = pw < 2;
+      if (pw < 2) {
+        st.sh[warp] = (uint16_t)ps.p[warp][pw].scale_h;
+        st.z[warp] = (int8_t)ps.p[warp][pw].zero;
+      }
+    }
+    if (use_tma) {
+      bool ok = true;
+      if (tid == 0) ok = ring_wait(R, sg, i);
+      failed |= __syncthreads_or(!ok) != 0;
+    } else {
+      tile_fill(a.W, M, a.K, buf, t, nct, 0);
+      __syncthreads();
+    }
+    // 2nd-order codes of this tile's groups for every table entry
+    if (write_sq && tab_smem) {
+      for (int k = tid; k < kTileGroups * ntab; k += blockDim.x) {
+        const int gw = k / ntab, idx = k % ntab;
+        if (!st.keep[gw]) continue;
+        const int64_t g = (int64_t)ct * kTileGroups + gw;
+        const uint8_t pr =
+            (uint8_t)(ps.prec[gw] >> (8 * (int)((uintptr_t)(a.ws.prec + g) & 3)));
+        const float s1f = __half2float(__ushort_as_half((uint16_t)ps.p[gw][pr].scale_h));
+        const float4 ch = tab[idx];
+        const int q2 = f2i_rz(roundf(__fdiv_rn(__fsub_rn(s1f, ch.x), ch.y)));
+        st.q2[gw][idx] = (uint8_t)max(0, min(15, q2));
+      }
+      __syncthreads();
+    }
+    // (row0 + lane) * ng mod (period * 256), the 2nd-order position of the
+    // lane's row in step 0
+    const int u_lane = write_sq ? (int)(((int64_t)s_u0 + (int64_t)lane * ng) % p256) : 0;
+    // work items (group, 32-row step): warp w takes items w, w+8, w+16, w+24,
+    // i.e. one step of four groups, so 4-bit groups spread over the warps
+#pragma unroll 1
+    for (int k = warp; k < kTileGroups * kSteps; k += kTileGroups) {
+      const int gw = k >> 2, s = k & 3;
+      if (!st.keep[gw]) continue;
+      const int64_t g = (int64_t)ct * kTileGroups + gw;
+      const uint8_t pr =
+          (uint8_t)(ps.prec[gw] >> (8 * (int)((uintptr_t)(a.ws.prec + g) & 3)));
+      const GroupParams& gpar = ps.p[gw][pr];
+      const bool four = pr != 0;
+      const int gs = (int)min64(kGroup1, a.K - g * kGroup1);
+      const int r = s * 32 + lane;
+      const uint8_t* row_base = buf + (gw >> 2) * kBoxBytes + r * 128;
+      const int c0 = 2 * (gw & 3), sw = r & 7;
+      const int lo_off = (c0 ^ sw) << 4, hi_off = ((c0 + 1) ^ sw) << 4;
+      Row16 v;
+      v.lo = *reinterpret_cast<const uint4*>(row_base + lo_off);
+      v.hi = *reinterpret_cast<const uint4*>(row_base + hi_off);
+      uint32_t wa, wb;
+      const int cnt = encode_run_tile(v, gpar, row_base, lo_off, hi_off, gs, wa, wb);
+      st.p2[gw][r] = four ? 0u : wa;
+      st.p4[gw][r] = four ? make_uint2(wa, wb) : make_uint2(0u, 0u);
+      if (write_sq) {
+        int u = u_lane + dstep[s];
+        if (u >= p256) u -= p256;
+        if (tab_smem) {
+          const int64_t si = (row0 + r) * ng + g;
+          int idx = a.cl.ntab_full;
+          if (si < a.cl.nfull * kGroup2) {
+            int jt = u + (int)g;
+            if (jt >= p256) jt -= p256;
+            idx = jt >> 8;
+          }
+          st.sq[gw][r] = st.q2[gw][idx];
+        } else {
+          const float s1f = __half2float(__ushort_as_half((uint16_t)gpar.scale_h));
+          st.sq[gw][r] = second_order_code(a, tab, s1f, row0 + r, (int)g, u);
+        }
+      }
+      if (cnt && row0 + r < M) atomicAdd(a.ws.row_counts + row0 + r, cnt);
+    }
+    __syncthreads();  // codes staged; the tile buffer is free
+    if (tid == 0)
+      ring_issue(R, sg, &tmap, dsm, t + (int64_t)kEncStages * gridDim.x, ntiles, nct, use_tma);
+    const int nr = (int)min64(kChunkRows, M - row0);
+    const int64_t gb = (int64_t)ct * kTileGroups;
+    bool all8 = gb + kTileGroups <= ng;
+#pragma unroll
+    for (int w = 0; w < kTileGroups; ++w) all8 &= st.keep[w] != 0;
+    if (vec_out && all8) {
+      for (int k = tid; k < nr * 2; k += blockDim.x) {
+        const int r = k >> 1, h = k & 1;
+        const uint4 v = make_uint4(st.p2[4 * h][r], st.p2[4 * h + 1][r], st.p2[4 * h + 2][r],
+                                   st.p2[4 * h + 3][r]);
+        reinterpret_cast<uint4*>(a.packed2 + (row0 + r) * ng + gb)[h] = v;
+      }
+      for (int k = tid; k < nr * 4; k += blockDim.x) {
+        const int r = k >> 2, q = k & 3;
+        const uint2 x = st.p4[2 * q][r], y = st.p4[2 * q + 1][r];
+        reinterpret_cast<uint4*>(a.packed4 + 2 * ((row0 + r) * ng + gb))[q] =
+            make_uint4(x.x, x.y, y.x, y.y);
+      }
+      const uint4 shv = *reinterpret_cast<const uint4*>(st.sh);
+      const uint2 zv = *reinterpret_cast<const uint2*>(st.z);
+      for (int r = tid; r < nr; r += blockDim.x) {
+        *reinterpret_cast<uint4*>(a.scales1 + (row0 + r) * ng + gb) = shv;
+        *reinterpret_cast<uint2*>(a.zeros1 + (row0 + r) * ng + gb) = zv;
+        if (write_sq) {
+          uint32_t lo = 0, hi = 0;
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            lo |= (uint32_t)st.sq[w][r] << (8 * w);
+            hi |= (uint32_t)st.sq[4 + w][r] << (8 * w);
+          }
+          *reinterpret_cast<uint2*>(a.sq + (row0 + r) * ng + gb) = make_uint2(lo, hi);
+        }
+      }
+    } else {
+      for (int k = tid; k < nr * kTileGroups; k += blockDim.x) {
+        const int r = k / kTileGroups, w = k % kTileGroups;
+        if (!st.keep[w]) continue;
+        const int64_t si = (row0 + r) * ng + gb + w;
+        a.packed2[si] = (int32_t)st.p2[w][r];
+        reinterpret_cast<uint2*>(a.packed4)[si] = st.p4[w][r];
+        a.scales1[si] = __ushort_as_half(st.sh[w]);
+        a.zeros1[si] = st.z[w];
+        if (write_sq) a.sq[si] = st.sq[w][r];
+      }
+    }
+    __syncthreads();  // staging is free again
+  }
+  cp_async_wait_all();
+  grid_launch_dependents();
+  if (tid == 0) {
+    if (failed) atomicOr(&a.ws.hdr->status, kStatusTimeout);
+    ring_drain(R, i);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -1662,13 +2196,15 @@ __global__ void __launch_bounds__(256) post_kernel(const QArgs a) {
     a.scales2[c] = __ushort_as_half((uint16_t)__float_as_int(e.z));
     a.zeros2[c] = (int8_t)__float_as_int(e.w);
   }
-  // 2nd-order codes (quantize.cu:274-280): block b covers rows
-  // [b * kPostRows, ...), thread t groups t, t + 256, ...  Flat index r*ng + g
-  // lies in full chunk (jt >> 8) of one period (period * 256 = lcm(ng, 256)
-  // flat indices), advanced by ng per row.
+  // 2nd-order codes (quantize.cu:274-280), unless encode wrote them (no
+  // group was pending): block b covers rows [b * kPostRows, ...), thread t
+  // groups t, t + 256, ...  Flat index r*ng + g lies in full chunk (jt >> 8)
+  // of one period (period * 256 = lcm(ng, 256) flat indices), advanced by ng
+  // per row.
   const int P256 = cl.period * kGroup2;
   const int64_t full_end = cl.nfull * kGroup2;
-  for (int64_t rb = blockIdx.x; rb * kPostRows < M; rb += gridDim.x) {
+  const uint32_t np = hdr->n_pend, ndec = hdr->n_dec;
+  for (int64_t rb = blockIdx.x; np > 0 && rb * kPostRows < M; rb += gridDim.x) {
     const int64_t r0 = rb * kPostRows, r1 = min64(M, r0 + kPostRows);
     for (int g = tid; g < ng; g += blockDim.x) {
       const float s1f = __half2float(
@@ -1685,7 +2221,6 @@ __global__ void __launch_bounds__(256) post_kernel(const QArgs a) {
     }
   }
   // the pending groups, now decided
-  const uint32_t np = hdr->n_pend, ndec = hdr->n_dec;
   const int64_t nrb = ceil_div(M, kEncRows);
   for (int64_t w = gtid; w < (int64_t)np * nrb; w += gthreads) {
     const int u = (int)(w / nrb);
@@ -1868,10 +2403,6 @@ extern "C" mb_status mb_quantize(const void* weights_fp16, int64_t M, int64_t K,
   qa.sq = scales_1st_quant;
   qa.row_ptrs = outlier_row_ptrs;
   qa.nnz = nnz_device;
-  qa.enc_nbx = (int)ceil_div(ng, 256);
-  qa.enc_nby = (int)ceil_div(M, kEncRows);
-  MB_REQUIRE((int64_t)qa.enc_nbx * qa.enc_nby + kExactCtas < (int64_t)INT32_MAX,
-             "too many rows for the encode grid");
 
   // TMA needs a 16-byte aligned base and a row pitch that is a multiple of 16
   // bytes; other inputs fill the same shared-memory layout with plain loads.
@@ -1880,19 +2411,49 @@ extern "C" mb_status mb_quantize(const void* weights_fp16, int64_t M, int64_t K,
   const bool tma = w_aligned && (K % 8 == 0) &&
                    make_tensor_map_2d_16bit_sw128(&tmap, weights_fp16, false, (uint64_t)M,
                                                   (uint64_t)K, kChunkRows, 64);
+  int dev = 0, sms = 148;
+  MB_CUDA_TRY(cudaGetDevice(&dev));
+  MB_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const int64_t ntiles = nct * nrc;
   {
     auto kern = sens ? stats_kernel<true> : stats_kernel<false>;
     static std::atomic<uint64_t> attr_done[2] = {{0}, {0}};
     MB_CUDA_TRY(set_smem_limit_once(kern, kStatsSmem, attr_done[sens ? 1 : 0]));
-    kern<<<(unsigned)(nct * nrc), kStatsThreads, kStatsSmem, stream>>>(tmap, qa, tma ? 1 : 0);
+    int per_sm = 0;
+    MB_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kStatsThreads,
+                                                              kStatsSmem));
+    const int64_t grid =
+        std::max<int64_t>(1, std::min<int64_t>(ntiles, (int64_t)sms * std::max(per_sm, 1)));
+    kern<<<(unsigned)grid, kStatsThreads, kStatsSmem, stream>>>(tmap, qa, tma ? 1 : 0);
     MB_LAUNCH_CHECK("stats_kernel");
   }
-  if (mb_status st = launch_pdl(encode_kernel, dim3((unsigned)(kExactCtas + qa.enc_nbx * qa.enc_nby)),
-                                dim3(256), 0, stream, qa))
+  {
+    auto kern = sens ? assemble_kernel<true> : assemble_kernel<false>;
+    static std::atomic<uint64_t> attr_done[2] = {{0}, {0}};
+    MB_CUDA_TRY(set_smem_limit_once(kern, kTileBytes + 16, attr_done[sens ? 1 : 0]));
+    if (mb_status st = launch_pdl(kern, dim3((unsigned)nct), dim3(kStatsThreads),
+                                  (size_t)kTileBytes + 16, stream, qa))
+      return st;
+  }
+  if (mb_status st = launch_pdl(exact_kernel, dim3(kExactCtas), dim3(256), 0, stream, qa))
     return st;
-  int dev = 0, sms = 148;
-  MB_CUDA_TRY(cudaGetDevice(&dev));
-  MB_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  {
+    static std::atomic<uint64_t> attr_done{0};
+    MB_CUDA_TRY(set_smem_limit_once(encode_kernel, kEncSmem, attr_done));
+    const auto al = [](const void* p, unsigned m) {
+      return (reinterpret_cast<uintptr_t>(p) & (m - 1)) == 0;
+    };
+    const int vec_out = (ng % 8 == 0) && al(packed_2bit, 16) && al(packed_4bit, 16) &&
+                        al(scales_1st_fp16, 16) && al(zeros_1st, 8) && al(scales_1st_quant, 8);
+    int per_sm = 0;
+    MB_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, encode_kernel, 256,
+                                                              kEncSmem));
+    const int64_t grid =
+        std::max<int64_t>(1, std::min<int64_t>(ntiles, (int64_t)sms * std::max(per_sm, 1)));
+    if (mb_status st = launch_pdl(encode_kernel, dim3((unsigned)grid), dim3(256), kEncSmem,
+                                  stream, tmap, qa, tma ? 1 : 0, vec_out))
+      return st;
+  }
   const int64_t post_grid = std::max<int64_t>(1, std::min<int64_t>(ceil_div(M, kPostRows), 8LL * sms));
   return launch_pdl(post_kernel, dim3((unsigned)post_grid), dim3(256), 0, stream, qa);
 }
