@@ -1,29 +1,31 @@
 // memboost quantize on sm_100a.
 //
 // Replaces the reference's six-kernel pipeline with host round trips
-// (core/torch_ops.cu:105-264 driving core/quantize.cu:72-321) by three
-// stream-ordered kernels and no host synchronisation:
+// (core/torch_ops.cu:105-264 driving core/quantize.cu:72-321) by five
+// stream-ordered kernels chained with programmatic dependent launch and no
+// host synchronisation:
 //
-//   stats   streams W once from HBM in 128 x 128 tiles through TMA, one warp
-//           per 16-column group (quantize.cu:72-128): min / max, and an fp64
-//           prediction of the group's serial fp32 sensitivity sum with a
-//           rigorous error interval.  The last CTA of each column tile
-//           derives its groups' scale / zero / code thresholds for both
-//           precisions (quantize.cu:153-176); the last of those selects the
-//           4-bit groups (torch_ops.cu:149-179): every group whose interval
-//           lies clear of the top-k boundary is decided from the intervals,
-//           the few that straddle it are left pending.  When nothing is
-//           pending it also builds the 2nd-order tables (quantize.cu:245-281).
-//   encode  reads W again (from L2) and writes both packed arrays, scales_1st
-//           and zeros_1st of every decided group (quantize.cu:132-242).  When
-//           groups are pending, extra CTAs compute their exact serial sums
-//           (transfer functions per chunk of rows, assembled in order) and
-//           the last of them completes the selection and the tables.
-//   post    writes the 2nd-order codes / scales / zeros, encodes the pending
-//           groups and turns per-row outlier counts into row pointers
-//           (quantize.cu:274-299, torch_ops.cu:210-229).
-//   extract (second entry point) CSR values / columns in ascending column
-//           order (quantize.cu:301-321).
+//   stats    streams W from HBM in 128 x 128 tiles through TMA, one warp per
+//            16-column group (quantize.cu:72-128): per (group, 128-row
+//            chunk) min / max and per-column sums of w*w.
+//   assemble one CTA per column tile: each group's min / max, scale / zero /
+//            code thresholds for both precisions (quantize.cu:153-176), and
+//            an fp64 prediction of its serial fp32 sensitivity sum with a
+//            rigorous error interval.  The last CTA selects the 4-bit groups
+//            (torch_ops.cu:149-179): every group whose interval lies clear of
+//            the top-k boundary is decided from the intervals, the few that
+//            straddle it are left pending; when nothing is pending it also
+//            builds the 2nd-order chunk table (quantize.cu:245-272).
+//   exact    only when groups are pending: their exact serial sums
+//            (transfer functions per chunk of rows, assembled in order); the
+//            last group completes the selection and the table.
+//   encode   reads W again (mostly from L2) and writes both packed arrays,
+//            scales_1st, zeros_1st and the 2nd-order codes
+//            (quantize.cu:132-242, 274-280), and counts outliers per row.
+//   post     2nd-order scales / zeros and the outlier row pointers
+//            (quantize.cu:245-272, 284-299, torch_ops.cu:210-229).
+//   extract  (second entry point) CSR values / columns in ascending column
+//            order (quantize.cu:301-321).
 //
 // Arithmetic that decides an output bit uses the reference's fp32 operations,
 // written with explicit rounding intrinsics so the compiler cannot contract
@@ -63,10 +65,8 @@ constexpr int kItemWindow = 0x40000000;  // item.x of a window
 constexpr uint32_t kCntOverflow = 1u << 18;  // icount: the chunk's program overflowed
 constexpr uint32_t kGrpNaN = 1u, kGrpInf = 2u, kGrpLoose = 4u;  // per-group prediction flags
 constexpr double kEps24 = 5.9604644775390625e-08;  // 2^-24
-constexpr int kExactCtas = 148;                    // exact-sum CTAs of the encode grid
-
-// encode: one thread per (group slot, block of kEncRows rows)
-constexpr int kEncRows = 16;
+constexpr int kExactCtas = 148;                    // CTAs of the exact-sum kernel
+constexpr int kMaxEncGrid = 4096;                  // encode CTAs (persistent grid) at most
 
 // Outlier-test arithmetic of the reference kernel: the product
 // scale*(q-zero) fused into the subtraction (one rounding).  Established
@@ -147,6 +147,7 @@ struct Workspace {
   int32_t* row_counts;  // [M]
   uint8_t* prec;        // [ng] selected precision (copy of group_precision)
   int32_t* order;       // [ng] decided 2-bit, decided 4-bit, then pending groups
+  int32_t* enc_start;   // [kMaxEncGrid + 1] first tile of each encode CTA
 };
 
 size_t workspace_layout(int64_t M, int64_t K, char* base, Workspace* ws) {
@@ -180,6 +181,7 @@ size_t workspace_layout(int64_t M, int64_t K, char* base, Workspace* ws) {
   char* p_rc = take(sizeof(int32_t) * M);
   char* p_pr = take(ng);
   char* p_or = take(sizeof(int32_t) * ng);
+  char* p_es = take(sizeof(int32_t) * (kMaxEncGrid + 1));
   if (ws) {
     ws->hdr = reinterpret_cast<Header*>(p_hdr);
     ws->ct_count = reinterpret_cast<uint32_t*>(p_hdr + sizeof(Header));
@@ -203,6 +205,7 @@ size_t workspace_layout(int64_t M, int64_t K, char* base, Workspace* ws) {
     ws->row_counts = reinterpret_cast<int32_t*>(p_rc);
     ws->prec = reinterpret_cast<uint8_t*>(p_pr);
     ws->order = reinterpret_cast<int32_t*>(p_or);
+    ws->enc_start = reinterpret_cast<int32_t*>(p_es);
   }
   return off;
 }
@@ -237,13 +240,8 @@ __device__ __forceinline__ uint32_t row_word(const Row16& v, int k) {
   return k < 4 ? (&v.lo.x)[k] : (&v.hi.x)[k - 4];
 }
 
-__device__ __forceinline__ float row_elem(const Row16& v, int i) {
-  const uint32_t w = row_word(v, i >> 1);
-  return __half2float(__ushort_as_half((uint16_t)((i & 1) ? (w >> 16) : (w & 0xFFFFu))));
-}
 
 __device__ __forceinline__ __half2 as_h2(uint32_t w) { return *reinterpret_cast<__half2*>(&w); }
-__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
 // Run r (0..127) of tile group gi from a tile in shared memory: two 64-column
 // TMA boxes written with the 128-byte swizzle (16-byte chunk c of row r sits
@@ -749,6 +747,7 @@ struct QArgs {
   int n4;      // 4-bit groups to select
   int select;  // the selection runs (sensitivity needed)
   int w_aligned;
+  int enc_grid;  // CTAs of the encode kernel
   // encode / post outputs
   int32_t* packed2;
   int32_t* packed4;
@@ -1091,6 +1090,65 @@ __device__ __forceinline__ uint32_t sens_key(float s) {
   return isnan(s) ? 0xFFFFFFFFu : __float_as_uint(s);
 }
 
+// Tile ranges of the encode CTAs, weighted by the work of each column tile
+// (once every precision is known; NT threads).  Encode works through a tile
+// in items: 64 rows of a 2-bit group cost about 1, 32 rows of a 4-bit group
+// about 1.35 and of an irregular group about 4.5, and a tile's write-out
+// about 16 (units of 1/10 below).  CTA b gets the tiles [S_b, S_b+1) (in
+// column-major order) where the weighted prefix reaches b / G of the total.
+__device__ __forceinline__ int64_t enc_uniform_start(int64_t b, int64_t ntiles, int G) {
+  return b * ntiles / G;
+}
+
+template <int NT>
+__device__ void enc_partition(const QArgs& a, const uint32_t* s_cost /* nct, or null */) {
+  const int tid = threadIdx.x % NT, lane = threadIdx.x & 31, warp = tid >> 5;
+  constexpr int NWARP = NT / 32;
+  __shared__ long long s_part[NWARP];
+  const int G = a.enc_grid, nct = a.nct, nrc = a.nrc;
+  const int64_t ntiles = (int64_t)nct * nrc;
+  if (G <= 0 || G > kMaxEncGrid) return;
+  int32_t* S = a.ws.enc_start;
+  if (ntiles < 2 * (int64_t)G || s_cost == nullptr) {
+    for (int b = tid; b <= G; b += NT) S[b] = (int32_t)enc_uniform_start(b, ntiles, G);
+    return;
+  }
+  const int per = (nct + NT - 1) / NT;
+  const int c0 = min(nct, tid * per), c1 = min(nct, c0 + per);
+  long long local = 0;
+  for (int ct = c0; ct < c1; ++ct) local += (long long)s_cost[ct] * nrc;
+  long long incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const long long y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) s_part[warp] = incl;
+  sync_nt<NT>();
+  long long P = incl - local, total = 0;
+  for (int w = 0; w < NWARP; ++w) {
+    if (w < warp) P += s_part[w];
+    total += s_part[w];
+  }
+  // CTA b starts where the weighted prefix reaches b * total / G (integers:
+  // P * G <= b * total < Pn * G selects the column tile)
+  for (int ct = c0; ct < c1; ++ct) {
+    const long long c = s_cost[ct];
+    const long long Pn = P + c * nrc;
+    long long b = (P * G + total - 1) / total;
+    if (b < 1) b = 1;
+    for (; b < G && b * total < Pn * G; ++b) {
+      const long long num = b * total - P * G, den = (long long)G * c;
+      S[b] = (int32_t)((int64_t)ct * nrc + (num + den - 1) / den);
+    }
+    P = Pn;
+  }
+  if (tid == 0) {
+    S[0] = 0;
+    S[G] = (int32_t)ntiles;
+  }
+}
+
 // 2nd-order tables, any_irregular and the group_precision output once every
 // group's precision is in ws.prec (quantize.cu:245-272 over the flattened
 // [M, ng] scales).  scales_1st[r, g] depends only on g, so full chunks repeat
@@ -1102,13 +1160,18 @@ __device__ __forceinline__ uint32_t sens_key(float s) {
 template <int NT>
 __device__ void finalize_tables(const QArgs& a, float* s1, size_t s1_bytes, uint32_t* s_wsum,
                                 int* s_irr, bool rebuild_order) {
-  const int ng = a.ng;
+  const int ng = a.ng, nct = a.nct;
   const int tid = threadIdx.x % NT, lane = threadIdx.x & 31, warp = tid >> 5;
   constexpr int NWARP = NT / 32;
   (void)s_wsum;
-  if (tid == 0) *s_irr = 0;
-  sync_nt<NT>();
   const bool s1_in_smem = (size_t)ng * sizeof(float) <= s1_bytes;
+  // encode work of each column tile, after s1 (for the tile split)
+  uint32_t* s_cost = reinterpret_cast<uint32_t*>(s1 + ng);
+  const bool cost_in_smem = s1_in_smem && (size_t)(ng + nct) * sizeof(float) <= s1_bytes;
+  if (tid == 0) *s_irr = 0;
+  if (cost_in_smem)
+    for (int ct = tid; ct < nct; ct += NT) s_cost[ct] = 160;
+  sync_nt<NT>();
   auto scale_from = [&](int g, uint8_t pr) -> float {
     const uint32_t sh2 = __ldcg(a.ws.gscale + g);
     return __half2float(__ushort_as_half((uint16_t)(pr ? (sh2 >> 16) : (sh2 & 0xFFFFu))));
@@ -1118,71 +1181,51 @@ __device__ void finalize_tables(const QArgs& a, float* s1, size_t s1_bytes, uint
     const uint8_t pr = a.ws.prec[g];
     a.gp[g] = pr;
     if (s1_in_smem) s1[g] = scale_from(g, pr);
-    irr |= !((a.ws.greg[g] >> pr) & 1);
+    const bool reg = (a.ws.greg[g] >> pr) & 1;
+    irr |= !reg;
+    if (cost_in_smem) atomicAdd(&s_cost[g / kTileGroups], !reg ? 180u : pr ? 54u : 20u);
   }
   if (__any_sync(0xffffffffu, irr) && lane == 0) atomicOr(s_irr, 1);
   sync_nt<NT>();
   auto scale_of = [&](int g) -> float {
     return s1_in_smem ? s1[g] : scale_from(g, a.ws.prec[g]);
   };
+  // one warp per chunk: min / max of the scales of its (cyclic) group range
   const ChunkLayout& cl = a.cl;
   const int nchunks = cl.ntab_full + cl.has_partial;
-  // block minima / maxima of 32 consecutive groups (in the scratch after s1)
-  const int nblk = (ng + 31) / 32;
-  const bool blk_in_smem =
-      s1_in_smem && (size_t)(ng + 2 * nblk) * sizeof(float) <= s1_bytes && NT > 32;
-  float* bmin = s1 + ng;
-  float* bmax = bmin + nblk;
-  if (blk_in_smem) {
-    for (int b = warp; b < nblk; b += NWARP) {
-      const int g = b * 32 + lane;
-      const float v = g < ng ? s1[g] : 1e10f;
-      const float mnv = warp_min(v), mxv = warp_max(g < ng ? v : -1e10f);
-      if (lane == 0) {
-        bmin[b] = mnv;
-        bmax[b] = mxv;
-      }
-    }
-    sync_nt<NT>();
-  }
-  // min / max of scales over groups [g0, g0 + n) cyclically
-  auto range_minmax = [&](int g0, int n, float& mn, float& mx) {
-    int g = g0, left = n;
-    while (left > 0) {
-      if (g >= ng) g -= ng;
-      if (blk_in_smem && (g & 31) == 0 && left >= 32 && g + 32 <= ng) {
-        mn = fminf(mn, bmin[g >> 5]);
-        mx = fmaxf(mx, bmax[g >> 5]);
-        g += 32;
-        left -= 32;
-      } else {
-        const float v = scale_of(g);
-        mn = fminf(mn, v);
-        mx = fmaxf(mx, v);
-        ++g;
-        --left;
-      }
-    }
-  };
-  for (int ci = tid; ci < nchunks; ci += NT) {
+  for (int ci = warp; ci < nchunks; ci += NWARP) {
     const int64_t cidx = ci < cl.ntab_full ? ci : cl.nfull;  // the partial chunk is the last
     const int64_t s0 = cidx * kGroup2;
     const int n = (int)min64(kGroup2, cl.total - s0);
     float mn = 1e10f, mx = -1e10f;
     if (n >= ng) {  // every group at least once
-      range_minmax(0, ng, mn, mx);
+      for (int g = lane; g < ng; g += 32) {
+        const float v = scale_of(g);
+        mn = fminf(mn, v);
+        mx = fmaxf(mx, v);
+      }
     } else {
-      range_minmax((int)(s0 % ng), n, mn, mx);
+      const int g0 = (int)(s0 % ng);
+      for (int k = lane; k < n; k += 32) {
+        int g = g0 + k;
+        if (g >= ng) g -= ng;
+        const float v = scale_of(g);
+        mn = fminf(mn, v);
+        mx = fmaxf(mx, v);
+      }
     }
-    float sc2 = __fdiv_rn(__fsub_rn(mx, mn), 15.0f);
-    if (sc2 < 1e-10f) sc2 = 1e-10f;
-    const int z2 = f2i_rz(roundf(__fdiv_rn(-mn, sc2)));
-    const int slot = ci < cl.ntab_full ? ci : cl.ntab_full;
-    a.ws.chunk_tab[slot] =
-        make_float4(mn, sc2, __int_as_float((int)__half_as_ushort(__float2half_rn(sc2))),
-                    __int_as_float((int)(int8_t)z2));
+    mn = warp_min(mn);
+    mx = warp_max(mx);
+    if (lane == 0) {
+      float sc2 = __fdiv_rn(__fsub_rn(mx, mn), 15.0f);
+      if (sc2 < 1e-10f) sc2 = 1e-10f;
+      const int z2 = f2i_rz(roundf(__fdiv_rn(-mn, sc2)));
+      const int slot = ci < cl.ntab_full ? ci : cl.ntab_full;
+      a.ws.chunk_tab[slot] =
+          make_float4(mn, sc2, __int_as_float((int)__half_as_ushort(__float2half_rn(sc2))),
+                      __int_as_float((int)(int8_t)z2));
+    }
   }
-  sync_nt<NT>();
   if (tid == 0) {
     a.ws.hdr->any_irregular = *s_irr;
     if (rebuild_order) {
@@ -1190,6 +1233,7 @@ __device__ void finalize_tables(const QArgs& a, float* s1, size_t s1_bytes, uint
       a.ws.hdr->n_pend = 0;
     }
   }
+  enc_partition<NT>(a, cost_in_smem ? s_cost : nullptr);
 }
 
 // Interval of a group's fp32 serial sum as sortable keys (lo rounded down,
@@ -1335,15 +1379,6 @@ __device__ __forceinline__ void sq_acc2(uint32_t w, float& a0, float& a1) {
       : "r"(w));
 }
 
-// Issue the TMA loads of tile `t` (two 64-column boxes) into `dst`.
-__device__ __forceinline__ void tile_load(const CUtensorMap* tmap, uint64_t* bar, uint8_t* dst,
-                                          int64_t t, int nct) {
-  const int rc = (int)(t / nct), ct = (int)(t % nct);
-  mbar_arrive_expect_tx(bar, kTileBytes);
-  tma_load_2d(dst, tmap, bar, ct * kTileCols, rc * kChunkRows);
-  tma_load_2d(dst + kBoxBytes, tmap, bar, ct * kTileCols + 64, rc * kChunkRows);
-}
-
 // The same swizzled tile layout from plain loads (inputs TMA cannot take);
 // `fill` outside the matrix.
 __device__ __forceinline__ void tile_fill(const __half* W, int64_t M, int64_t K, uint8_t* dst,
@@ -1370,6 +1405,22 @@ __device__ __noinline__ void ct_assemble(const QArgs& A, int ct, int warp, int l
   float mn = INFINITY, mx = -INFINITY;
   bool any_nan = false, any_inf = false, loose = false;
   double carry = 0.0, mom = 0.0;
+  // RN(1/h) of the group's 16 columns (1 where the reference does not
+  // divide): lane c computes column c, then every lane holds all 16
+  float rc16[16];
+  if (kSens) {
+    const int64_t c = g * kGroup1 + (lane & 15);
+    float r = 1.0f;
+    if (c < A.K) {
+      const float h = __ldg(A.hess + c);
+      if (h > 1e-8f) {
+        r = __frcp_rn(h);
+        loose = !(h >= 0x1p-60f && h <= 0x1p60f);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 16; ++k) rc16[k] = __shfl_sync(0xffffffffu, r, k);
+  }
   for (int j0 = 0; j0 < nrc; j0 += 96) {
     // up to three chunks per lane in flight
     float2 mm[3];
@@ -1390,31 +1441,25 @@ __device__ __noinline__ void ct_assemble(const QArgs& A, int ct, int warp, int l
         }
       }
     }
-    // RN(1/h) of the group's 16 columns (1 where the reference does not divide)
-    float rc16[16];
-    if (kSens) {
-      const int64_t c0 = g * kGroup1;
-#pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        float r = 1.0f;
-        if (c0 + c < A.K) {
-          const float h = __ldg(A.hess + c0 + c);
-          if (h > 1e-8f) {
-            r = __frcp_rn(h);
-            loose |= !(h >= 0x1p-60f && h <= 0x1p60f);
-          }
-        }
-        rc16[c] = r;
-      }
-    }
 #pragma unroll
     for (int u = 0; u < 3; ++u) {
       const int j = j0 + 32 * u + lane;
       mn = fminf(mn, mm[u].x);
       mx = fmaxf(mx, mm[u].y);
       if (kSens) {
-        double v = 0.0;
-        if (j < nrc) {
+        // products are exact in fp64; four partial sums shorten the chain
+        double part[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float cv[4] = {cc[u][q].x, cc[u][q].y, cc[u][q].z, cc[u][q].w};
+          double t = 0.0;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) t = fma((double)cv[e], (double)rc16[4 * q + e], t);
+          part[q] = t;
+        }
+        double v = (part[0] + part[1]) + (part[2] + part[3]);
+        if (!isfinite(v)) {  // a NaN / inf column sum: flag it, sum the finite ones
+          v = 0.0;
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             const float cv[4] = {cc[u][q].x, cc[u][q].y, cc[u][q].z, cc[u][q].w};
@@ -1425,8 +1470,8 @@ __device__ __noinline__ void ct_assemble(const QArgs& A, int ct, int warp, int l
               if (isfinite(cv[e])) v += (double)cv[e] * (double)rc16[4 * q + e];
             }
           }
-          A.ws.cpred[(size_t)g * nrc + j] = v;
         }
+        if (j < nrc) A.ws.cpred[(size_t)g * nrc + j] = v;
         double incl = v;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -1469,47 +1514,6 @@ __device__ __noinline__ void select_all(const QArgs& A, uint8_t* scratch) {
   select_from_intervals<kStatsThreads>(A, scratch, kTileBytes);
 }
 
-// Tile ring of a persistent CTA: kStages tile buffers fed by TMA; CTA b takes
-// tiles b, b + grid, b + 2 grid, ... (tile t covers row chunk t / nct and
-// column tile t % nct, so tiles in flight together span whole rows of W).  Thread 0 refills a stage as soon as the CTA is
-// done with it, so kStages - 1 loads stay in flight while the warps work.
-template <int S>
-struct TileRing {
-  uint64_t full[S];
-  int64_t tile[S];
-  uint32_t parity_pending;  // bit s: a load into stage s was issued and not waited for
-};
-
-// Load tile t (if it exists) into stage s; thread 0.
-template <int S>
-__device__ __forceinline__ void ring_issue(TileRing<S>& R, int s, const CUtensorMap* tmap,
-                                           uint8_t* dsm, int64_t t, int64_t ntiles, int nct,
-                                           bool use_tma) {
-  R.tile[s] = t;
-  if (use_tma && t < ntiles) {
-    fence_proxy_async_smem();
-    tile_load(tmap, &R.full[s], dsm + (size_t)s * kTileBytes, t, nct);
-    R.parity_pending |= 1u << s;
-  }
-}
-
-// Wait (thread 0) for the load of iteration i; false on timeout.
-template <int S>
-__device__ __forceinline__ bool ring_wait(TileRing<S>& R, int s, int i) {
-  const bool ok = mbar_wait(&R.full[s], (uint32_t)((i / S) & 1));
-  if (ok) R.parity_pending &= ~(1u << s);
-  return ok;
-}
-
-// Before exit (thread 0): loads still in flight must land.
-template <int S>
-__device__ __forceinline__ void ring_drain(TileRing<S>& R, int i_next) {
-  for (int k = 0; k < S; ++k) {
-    const int i = i_next + k, s = i % S;
-    if (R.parity_pending & (1u << s)) (void)mbar_wait(&R.full[s], (uint32_t)((i / S) & 1));
-  }
-}
-
 // stats: persistent CTAs streaming the tiles, one warp per group of the
 // current tile: per (group, row chunk) min / max and the per-column sums of
 // w*w (the sensitivity prediction before the division by h).
@@ -1519,35 +1523,55 @@ __global__ void __launch_bounds__(kStatsThreads, 2)
   extern __shared__ uint8_t dsm_raw[];
   uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) &
                                             ~(uintptr_t)1023);
-  __shared__ TileRing<kStages> R;
+  __shared__ uint64_t full[kStages];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t M = A.M, K = A.K;
   const int nrc = A.nrc, nct = A.nct;
-  const int64_t ntiles = (int64_t)nct * nrc;
-  if (tid == 0) {
-    R.parity_pending = 0;
-    for (int s = 0; s < kStages; ++s) mbar_init(&R.full[s], 1);
+  const int ntiles = nct * nrc;  // below 2^31 (checked on the host)
+  const int G = (int)gridDim.x;
+  // tile t = rc * nct + ct; t advances by G: (rc, ct) by (G / nct, G % nct)
+  const int drc = G / nct, dct = G - drc * nct;
+  auto advance = [&](int& rc, int& ct) {
+    rc += drc;
+    ct += dct;
+    if (ct >= nct) {
+      ct -= nct;
+      ++rc;
+    }
+  };
+  int t_ahead = (int)blockIdx.x;  // thread 0: the next tile to load
+  int rc_ahead = t_ahead / nct, ct_ahead = t_ahead - rc_ahead * nct;
+  auto issue = [&](int s) {
+    uint8_t* dst = dsm + (size_t)s * kTileBytes;
+    fence_proxy_async_smem();
+    mbar_arrive_expect_tx(&full[s], kTileBytes);
+    tma_load_2d(dst, &tmap, &full[s], ct_ahead * kTileCols, rc_ahead * kChunkRows);
+    tma_load_2d(dst + kBoxBytes, &tmap, &full[s], ct_ahead * kTileCols + 64,
+                rc_ahead * kChunkRows);
+    t_ahead += G;
+    advance(rc_ahead, ct_ahead);
+  };
+  if (tid == 0 && use_tma) {
+    for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
     fence_mbar_init();
-    for (int s = 0; s < kStages; ++s)
-      ring_issue(R, s, &tmap, dsm, blockIdx.x + (int64_t)s * gridDim.x, ntiles, nct, use_tma);
+    for (int s = 0; s < kStages && t_ahead < ntiles; ++s) issue(s);
   }
   __syncthreads();
   bool failed = false;
-  int i = 0;
-  for (;; ++i) {
-    const int st = i % kStages;
-    const int64_t t = R.tile[st];
-    if (t >= ntiles) break;
+  uint32_t bad = 0;  // thread 0: stages whose wait ran out
+  int st = 0;
+  uint32_t ph = 0;  // phase parity of stage st
+  int rc = (int)blockIdx.x / nct, ct = (int)blockIdx.x - rc * nct;
+  for (int t = (int)blockIdx.x; t < ntiles; t += G, advance(rc, ct)) {
     uint8_t* buf = dsm + (size_t)st * kTileBytes;
-    const int rc = (int)(t / nct), ct = (int)(t % nct);
     const int64_t row0 = (int64_t)rc * kChunkRows;
     const int gi = warp;
     const int64_t g = (int64_t)ct * kTileGroups + gi;
     const int64_t c0 = g * kGroup1;
     if (use_tma) {
-      bool ok = true;
-      if (tid == 0) ok = ring_wait(R, st, i);
-      failed |= __syncthreads_or(!ok) != 0;
+      const bool ok = mbar_wait(&full[st], ph);
+      failed |= !ok;
+      if (tid == 0 && !ok) bad |= 1u << st;
     } else {
       tile_fill(A.W, M, K, buf, t, nct, 0x7E00);
       __syncthreads();
@@ -1615,13 +1639,20 @@ __global__ void __launch_bounds__(kStatsThreads, 2)
       for (int r = tid; r < kChunkRows; r += kStatsThreads)
         if (row0 + r < M) A.ws.row_counts[row0 + r] = 0;
     __syncthreads();  // the stage is free
-    if (tid == 0)
-      ring_issue(R, st, &tmap, dsm, t + (int64_t)kStages * gridDim.x, ntiles, nct, use_tma);
+    if (tid == 0 && use_tma && t_ahead < ntiles) issue(st);
+    if (++st == kStages) {
+      st = 0;
+      ph ^= 1u;
+    }
   }
   grid_launch_dependents();
+  failed = __syncthreads_or(failed) != 0;
   if (tid == 0) {
     if (failed) atomicOr(&A.ws.hdr->status, kStatusTimeout);
-    ring_drain(R, i);
+    // loads whose wait ran out may still be in flight: let them land (the
+    // stage's last issued phase, bounded)
+    for (int s = 0; s < kStages; ++s)
+      if (bad & (1u << s)) (void)mbar_wait(&full[s], 0u), (void)mbar_wait(&full[s], 1u);
   }
 }
 
@@ -1647,7 +1678,7 @@ __global__ void __launch_bounds__(kStatsThreads) assemble_kernel(const QArgs A) 
 }
 
 // ---------------------------------------------------------------------------
-// encode: rows of one group slot, 2 rows per step.
+// encode: the outlier test of the reference and the code helpers.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ bool is_outlier(float x, float scale, int zero, float thr, int q,
                                            int fma_mode) {
@@ -1657,147 +1688,80 @@ __device__ __forceinline__ bool is_outlier(float x, float scale, int zero, float
   return err > thr;
 }
 
-// Codes of one run (16 values of one row) of a group: the 2-bit word (wa) or
-// the two 4-bit words (wa, wb), and the number of outliers.  Regular groups
-// compare against the code thresholds (packed half2: each comparison adds 1
-// to a 1024 + code accumulator, whose low mantissa bits are the code);
-// others evaluate the reference formula per element (quantize.cu:178-240).
-struct EncGroup {
-  uint4 tA, tB;  // thresholds T_1..T_15 (fp16 patterns)
-  float gmin, scale, thr;
-  int zero, levels, gs;
-  bool four, regular;
-};
+// Codes of a regular group's run (16 values of one row) from its code
+// thresholds T_j (the smallest fp16 value whose code is >= j; +inf if none):
+// code(w) = #{j : w >= T_j}.  The run's words are re-paired so that half-word
+// lane 0 of pair k holds element k and lane 1 element k + 8; then every
+// packed comparison feeds one output position per lane.
 
-__device__ __forceinline__ EncGroup enc_group_of(const GroupParams& pp, int64_t K, int g,
-                                                 bool four) {
-  EncGroup e;
-  e.tA = *reinterpret_cast<const uint4*>(&pp.thresh[0]);
-  e.tB = *reinterpret_cast<const uint4*>(&pp.thresh[8]);
-  e.gmin = pp.gmin;
-  e.scale = pp.scale;
-  e.thr = pp.thr;
-  e.zero = pp.zero;
-  e.levels = pp.levels;
-  e.gs = (int)min64(kGroup1, K - (int64_t)g * kGroup1);
-  e.four = four;
-  e.regular = (pp.flags & kFlagRegular) != 0;
-  return e;
+// Lane select: a where the mask is set, b elsewhere.
+__device__ __forceinline__ uint32_t lane_sel(uint32_t m, uint32_t a, uint32_t b) {
+  return (m & a) | (~m & b);
 }
 
-__device__ __forceinline__ EncGroup enc_group(const QArgs& a, int g, bool four) {
-  return enc_group_of(a.ws.params[2 * g + (four ? 1 : 0)], a.K, g, four);
-}
+// 2-bit: c_k = [P_k >= T1] + [P_k >= T2] + [P_k >= T3] (fp16 0..3, exact),
+// accumulated as 1024 + c_0 + 4 c_1 + 16 c_2 + 64 c_3 (an fp16 integer below
+// 2048, so its low mantissa byte is the four codes' 2-bit fields).
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
-__device__ __forceinline__ int encode_run(const Row16& v, const EncGroup& e, uint32_t& wa,
-                                          uint32_t& wb) {
-  wa = wb = 0;
-  int cnt = 0;
-  const int gs = e.gs;
-  if (e.regular) {
-    auto T2 = [&](int j) -> __half2 {  // threshold j as a broadcast half2
-      const uint32_t w = j < 8 ? (&e.tA.x)[j >> 1] : (&e.tB.x)[(j - 8) >> 1];
-      const uint16_t h = (j & 1) ? (uint16_t)(w >> 16) : (uint16_t)(w & 0xFFFFu);
-      return __half2half2(__ushort_as_half(h));
-    };
+__device__ __forceinline__ uint32_t enc2_run(const Row16& v, uint32_t t1, uint32_t t2,
+                                             uint32_t t3) {
+  const uint32_t w[8] = {v.lo.x, v.lo.y, v.lo.z, v.lo.w, v.hi.x, v.hi.y, v.hi.z, v.hi.w};
+  const __half2 T1 = as_h2(t1), T2 = as_h2(t2), T3 = as_h2(t3);
+  // fp16 bit patterns: 1024, and the weights 1, 4, 16, 64 in both lanes
+  constexpr uint32_t kW[4] = {0x3C003C00u, 0x44004400u, 0x4C004C00u, 0x54005400u};
+  __half2 acc[2] = {as_h2(0x64006400u), as_h2(0x64006400u)};
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const __half2 w2 = as_h2(row_word(v, k));
-      __half2 acc = __float2half2_rn(1024.0f);
-      if (!e.four) {
-#pragma unroll
-        for (int j = 0; j < 3; ++j) acc = __hadd2(acc, __hge2(w2, T2(j)));
-      } else {
-#pragma unroll
-        for (int j = 0; j < 15; ++j) acc = __hadd2(acc, __hge2(w2, T2(j)));
-      }
-      // 1024 has an fp16 ulp of 1: the code sits in the low mantissa bits
-      const uint32_t b = h2_bits(acc);
-      if (!e.four) {
-        wa |= ((b & 0x3u) | ((b >> 14) & 0xCu)) << (4 * k);
-      } else {
-        const uint32_t t = (b & 0xFu) | ((b >> 12) & 0xF0u);
-        if (k < 4)
-          wa |= t << (8 * k);
-        else
-          wb |= t << (8 * (k - 4));
-      }
-    }
-    if (gs < kGroup1) {  // columns past K hold code 0 in the reference
-      if (!e.four) {
-        wa &= (1u << (2 * gs)) - 1u;
-      } else {
-        wa &= gs >= 8 ? 0xFFFFFFFFu : ((1u << (4 * gs)) - 1u);
-        wb &= gs <= 8 ? 0u : ((1u << (4 * (gs - 8))) - 1u);
-      }
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      if (i < gs) {
-        const float x = row_elem(v, i);
-        const int q = code_of(x, e.gmin, e.scale, e.levels);
-        cnt += is_outlier(x, e.scale, e.zero, e.thr, q, kOutlierFma);
-        if (!e.four)
-          wa |= (uint32_t)(q & 0x3) << (2 * i);
-        else if (i < 8)
-          wa |= (uint32_t)(q & 0xF) << (4 * i);
-        else
-          wb |= (uint32_t)(q & 0xF) << (4 * (i - 8));
-      }
-    }
+  for (int k = 0; k < 8; ++k) {
+    const __half2 P = as_h2(__byte_perm(w[k >> 1], w[4 + (k >> 1)], (k & 1) ? 0x7632 : 0x5410));
+    const __half2 c = __hadd2(__hadd2(__hge2(P, T1), __hge2(P, T2)), __hge2(P, T3));
+    acc[k >> 2] = __hfma2(c, as_h2(kW[k & 3]), acc[k >> 2]);
   }
-  return cnt;
+  // bytes: elements 0-3, 4-7 (low lanes), 8-11, 12-15 (high lanes)
+  return __byte_perm(h2_bits(acc[0]), h2_bits(acc[1]), 0x6240);
 }
 
-// Compact form of encode_run for the tile kernel: one loop over the group's
-// thresholds (read from shared memory, broadcast), 8 words per step, shared
-// by both precisions; the rare irregular groups loop over the elements of the
-// run in the tile (shared memory) instead of unrolling.
-__device__ __forceinline__ int encode_run_tile(const Row16& v, const GroupParams& gp,
-                                               const uint8_t* row_base, int lo_off, int hi_off,
-                                               int gs, uint32_t& wa, uint32_t& wb) {
+// 4-bit: a two-level search with lane masks.  The coarse level compares with
+// T4, T8, T12 (nested masks m4 >= m8 >= m12, c1 = their count); the fine
+// level compares with T(4 c1 + 1..3), selected per lane from the masks; the
+// code is 4 c1 + c2 with bit 3 = m8, bit 2 = m4 ^ m8 ^ m12, bit 1 = f2 and
+// bit 0 = f1 ^ f2 ^ f3.  Lane masks are 0xFFFF per half, so each nibble is
+// taken from its lane directly.
+
+__device__ __forceinline__ void enc4_run(const Row16& v, const uint32_t (&t)[16], uint32_t& wa,
+                                         uint32_t& wb) {
+  const uint32_t w[8] = {v.lo.x, v.lo.y, v.lo.z, v.lo.w, v.hi.x, v.hi.y, v.hi.z, v.hi.w};
+  uint32_t X[2] = {0u, 0u};
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const __half2 P = as_h2(__byte_perm(w[k >> 1], w[4 + (k >> 1)], (k & 1) ? 0x7632 : 0x5410));
+    const uint32_t m4 = __hge2_mask(P, as_h2(t[3]));
+    const uint32_t m8 = __hge2_mask(P, as_h2(t[7]));
+    const uint32_t m12 = __hge2_mask(P, as_h2(t[11]));
+    uint32_t f[3];
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+      const uint32_t F = lane_sel(m12, t[12 + i], lane_sel(m8, t[8 + i], lane_sel(m4, t[4 + i], t[i])));
+      f[i] = __hge2_mask(P, as_h2(F));
+    }
+    const uint32_t b2 = m4 ^ m8 ^ m12, b0 = f[0] ^ f[1] ^ f[2];
+    const int sh = 4 * (k & 3);
+    X[k >> 2] |= (m8 & (0x00080008u << sh)) | (b2 & (0x00040004u << sh)) |
+                 (f[1] & (0x00020002u << sh)) | (b0 & (0x00010001u << sh));
+  }
+  wa = __byte_perm(X[0], X[1], 0x5410);  // elements 0-7
+  wb = __byte_perm(X[0], X[1], 0x7632);  // elements 8-15
+}
+
+// Irregular groups: the reference formula per element (quantize.cu:178-240),
+// reading the run from the swizzled tile: (2-bit word or first 4-bit word,
+// second 4-bit word, outlier count).
+__device__ __noinline__ uint3 enc_irregular(const GroupParams& gp, const uint8_t* row_base,
+                                            int lo_off, int hi_off, int gs) {
   const bool four = gp.levels == 16;
-  wa = wb = 0;
-  if (gp.flags & kFlagRegular) {
-    __half2 acc[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) acc[k] = __float2half2_rn(1024.0f);
-    const int nt = gp.levels - 1;
-#pragma unroll 1
-    for (int j = 0; j < nt; ++j) {
-      const __half2 T = __half2half2(__ushort_as_half(gp.thresh[j]));
-#pragma unroll
-      for (int k = 0; k < 8; ++k) acc[k] = __hadd2(acc[k], __hge2(as_h2(row_word(v, k)), T));
-    }
-    // 1024 has an fp16 ulp of 1: the code sits in the low mantissa bits
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const uint32_t b = h2_bits(acc[k]);
-      if (!four) {
-        wa |= ((b & 0x3u) | ((b >> 14) & 0xCu)) << (4 * k);
-      } else {
-        const uint32_t t = (b & 0xFu) | ((b >> 12) & 0xF0u);
-        if (k < 4)
-          wa |= t << (8 * k);
-        else
-          wb |= t << (8 * (k - 4));
-      }
-    }
-    if (gs < kGroup1) {  // columns past K hold code 0 in the reference
-      if (!four) {
-        wa &= (1u << (2 * gs)) - 1u;
-      } else {
-        wa &= gs >= 8 ? 0xFFFFFFFFu : ((1u << (4 * gs)) - 1u);
-        wb &= gs <= 8 ? 0u : ((1u << (4 * (gs - 8))) - 1u);
-      }
-    }
-    return 0;
-  }
-  int cnt = 0;
+  uint32_t wa = 0, wb = 0, cnt = 0;
 #pragma unroll 1
   for (int i = 0; i < gs; ++i) {
-    // element i of the run, from the tile (chunk offsets swizzled by the caller)
     const uint16_t hb =
         *reinterpret_cast<const uint16_t*>(row_base + (i < 8 ? lo_off : hi_off) + (i & 7) * 2);
     const float x = __half2float(__ushort_as_half(hb));
@@ -1810,47 +1774,7 @@ __device__ __forceinline__ int encode_run_tile(const Row16& v, const GroupParams
     else
       wb |= (uint32_t)(q & 0xF) << (4 * (i - 8));
   }
-  return cnt;
-}
-
-// 2nd-order code of scales_1st[r, g] (quantize.cu:274-280); u_r = (r * ng)
-// mod (period * 256) locates the flat index r * ng + g within one period of
-// full chunks.
-__device__ __forceinline__ uint8_t second_order_code(const QArgs& a, const float4* tab, float s1f,
-                                                     int64_t r, int g, int u_r) {
-  const ChunkLayout& cl = a.cl;
-  const int64_t si = r * a.ng + g;
-  int idx = cl.ntab_full;
-  if (si < cl.nfull * kGroup2) {
-    int jt = u_r + g;
-    if (jt >= cl.period * kGroup2) jt -= cl.period * kGroup2;
-    idx = jt >> 8;
-  }
-  const float4 ch = tab[idx];
-  const int q2 = f2i_rz(roundf(__fdiv_rn(__fsub_rn(s1f, ch.x), ch.y)));
-  return (uint8_t)max(0, min(15, q2));
-}
-
-// Rows [r0, r1) of group g, one thread (the pending groups, in `post`).
-__device__ void encode_rows(const QArgs& a, int g, int64_t r0, int64_t r1) {
-  const int64_t K = a.K;
-  const int ng = a.ng;
-  const bool four = a.ws.prec[g] != 0;
-  const EncGroup e = enc_group(a, g, four);
-  const __half sh = __ushort_as_half((uint16_t)a.ws.params[2 * g + (four ? 1 : 0)].scale_h);
-  const int64_t c0 = (int64_t)g * kGroup1;
-  const bool vec = a.w_aligned && (e.gs == kGroup1) && ((K & 7) == 0);
-  for (int64_t r = r0; r < r1; ++r) {
-    const Row16 v = load_row16(a.W, r, K, c0, e.gs, vec);
-    uint32_t wa, wb;
-    const int cnt = encode_run(v, e, wa, wb);
-    const int64_t si = r * ng + g;
-    a.packed2[si] = four ? 0 : (int32_t)wa;
-    reinterpret_cast<int2*>(a.packed4)[si] = four ? make_int2((int)wa, (int)wb) : make_int2(0, 0);
-    a.scales1[si] = sh;
-    a.zeros1[si] = (int8_t)e.zero;
-    if (cnt) atomicAdd(a.ws.row_counts + r, cnt);
-  }
+  return make_uint3(wa, wb, cnt);
 }
 
 // Exact sums of the pending groups (the first kExactCtas blocks of the encode
@@ -1863,6 +1787,7 @@ __device__ __noinline__ void exact_ctas(const QArgs& a) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t ndec = *reinterpret_cast<const volatile uint32_t*>(&hdr->n_dec);
   __shared__ GroupDiv s_div[8];
+  __shared__ __align__(16) float s_scr[1024];  // the completing warp's tables
   __shared__ uint32_t hist[256];
   __shared__ uint32_t s2[2];
   __shared__ uint32_t s_wsum[1];
@@ -1915,7 +1840,7 @@ __device__ __noinline__ void exact_ctas(const QArgs& a) {
     if (lane == 0 && total_eq > need_eq) atomicOr(&a.ws.hdr->status, kStatusTie);
     __syncwarp();
     // decided slots of `order` are being encoded meanwhile: keep it as is
-    finalize_tables<32>(a, nullptr, 0, s_wsum, &s_irr, false);
+    finalize_tables<32>(a, s_scr, sizeof(s_scr), s_wsum, &s_irr, false);
   }
 }
 
@@ -1927,66 +1852,127 @@ __global__ void __launch_bounds__(256) exact_kernel(const QArgs a) {
   exact_ctas(a);
 }
 
-// encode: persistent CTAs over the 128 x 128 tiles of W (from L2 through the
-// TMA tile ring; the first loads are issued before the wait for the
-// preceding kernels since W is an input), one warp per group (its precision
-// is uniform over the warp), lane = row.  Codes are staged in shared memory
-// and leave as whole tile rows: 16-byte stores of packed_2bit, packed_4bit,
-// scales_1st, and 8-byte stores of zeros_1st and scales_1st_quant.  Groups
-// still pending are left to `post`, and so are the 2nd-order codes when any
-// group is pending.
-constexpr int kEncTabMax = 64;  // 2nd-order table entries handled in shared memory
+// encode: persistent CTAs over the 128 x 128 tiles of W.  CTA b takes a
+// contiguous range of tiles in column-major order (tile u: column tile
+// u / nrc, row chunk u % nrc), weighted by work when the selection split the
+// tiles (enc_partition), so its tiles mostly share one column tile and
+// the per-column-tile context -- kinds and thresholds of the 8 groups, their
+// 2nd-order codes and the list of work items sorted by cost -- is built once
+// per column tile.  An item is 64 rows of a 2-bit group (a lane codes rows r
+// and r + 32) or 32 rows of a 4-bit or irregular group (about 2.7 times
+// costlier per row); warps take items from a shared counter, costliest
+// first, so the tile's items spread evenly over the warps.  Tiles arrive
+// through a two-stage TMA ring and every thread waits on the stage's mbarrier
+// itself; codes are
+// staged group-major (lane = row; rows padded so the transposing reads are
+// conflict-free too) in one of two buffers and leave as whole tile rows:
+// 16-byte stores of packed_2bit, packed_4bit, scales_1st and 8-byte stores of
+// zeros_1st and scales_1st_quant.  One block barrier per tile.
+constexpr int kEncKind2 = 0, kEncKind4 = 1, kEncKindIrr = 2, kEncKindNone = 3;
+constexpr int kMaxRowPeriod = kGroup2;           // 256 / gcd(ng, 256) rows
 
-// Staging of one tile's outputs, group-major so that a warp's 32 rows of one
-// group store to consecutive words (no bank conflicts); the write-out
-// gathers each output row from the 8 group columns.
-struct __align__(16) EncStage {
-  uint32_t p2[kTileGroups][kChunkRows];
-  uint2 p4[kTileGroups][kChunkRows];
-  uint8_t sq[kTileGroups][kChunkRows];
-  uint8_t q2[kTileGroups][kEncTabMax];  // 2nd-order code per (group, table entry)
-  uint16_t sh[kTileGroups];
-  int8_t z[kTileGroups];
-  uint8_t keep[kTileGroups];  // group decided: written here
+struct __align__(16) EncCtx {
+  uint4 thr[kTileGroups][4];                   // T_1..T_15 as broadcast half2, +inf pad
+  uint8_t sqrow[kMaxRowPeriod][kTileGroups];   // 2nd-order code by (row mod period, group)
+  uint4 shv;                                   // scales_1st of the 8 groups (fp16)
+  uint2 zv;                                    // zeros_1st of the 8 groups
+  uint8_t kind[kTileGroups];
+  uint8_t gs[kTileGroups];                     // columns of the group inside K
+  uint8_t pr[kTileGroups];                     // precision (1 = 4-bit)
+  uint8_t items[kTileGroups * kSteps];         // group | step << 3 | (64 rows) << 5
+  int nitems;
 };
 
-// The next tile's group parameters (both precisions) and precisions, copied
-// asynchronously while the current tile is encoded.
-struct __align__(16) EncParamSlot {
-  GroupParams p[kTileGroups][2];
-  uint32_t prec[kTileGroups];
+// Output words of (group, row) of one tile, exactly as stored: packed_2bit
+// (0 for a 4-bit group) and packed_4bit (0 for a 2-bit group).
+constexpr int kCodePitch = kChunkRows + 4;
+struct __align__(16) EncCodes {
+  uint32_t p2[kTileGroups][kCodePitch];
+  uint2 p4[kTileGroups][kCodePitch];
 };
 
-
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() {
-  asm volatile("cp.async.commit_group;" ::: "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
-}
-
-// Warp `warp` copies its group's two GroupParams (128 bytes: lanes 0-7) and
-// precision (lane 8) of tile t into slot `ps`.
-__device__ __forceinline__ void enc_prefetch(const QArgs& a, EncParamSlot& ps, int64_t t,
-                                             int warp, int lane) {
-  const int64_t g = (t % a.nct) * kTileGroups + warp;
-  if (g >= a.ng) return;
-  if (lane < 8) {
-    const uint8_t* src = reinterpret_cast<const uint8_t*>(a.ws.params + 2 * g) + 16 * lane;
-    cp_async16(reinterpret_cast<uint8_t*>(&ps.p[warp][0]) + 16 * lane, src);
-  } else if (lane == 8) {
-    // the byte, 4-byte aligned below it (the reference's precisions are bytes)
-    const uintptr_t a4 = reinterpret_cast<uintptr_t>(a.ws.prec + g) & ~(uintptr_t)3;
-    cp_async4(&ps.prec[warp], reinterpret_cast<const void*>(a4));
+// The context of column tile ct (all threads; ends with a block barrier).
+// rp = 256 / gcd(ng, 256): the flat index r * ng + g of scales_1st advances
+// by a whole number of 256-long 2nd-order chunks every rp rows, so row r's
+// codes depend on r mod rp only (full chunks; rows that reach the partial
+// last chunk are coded directly in the write-out).
+__device__ __forceinline__ void enc_build_ctx(const QArgs& a, EncCtx& cx, int ct, int rp) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int ng = a.ng;
+  const int64_t g = (int64_t)ct * kTileGroups + warp;
+  uint32_t t = 0x7C007C00u;  // +inf: never reached
+  int kind = kEncKindNone, pr = 0, gs = 0;
+  uint16_t sh = 0;
+  int8_t z = 0;
+  if (g < ng) {
+    pr = a.ws.prec[g];
+    const GroupParams& p = a.ws.params[2 * g + pr];
+    if (lane < 15) t = (uint32_t)p.thresh[lane] * 0x00010001u;
+    kind = (p.flags & kFlagRegular) ? (pr ? kEncKind4 : kEncKind2) : kEncKindIrr;
+    gs = (int)min64(kGroup1, a.K - g * kGroup1);
+    sh = (uint16_t)p.scale_h;
+    z = (int8_t)p.zero;
   }
+  if (lane < 16) (&cx.thr[warp][0].x)[lane] = t;
+  if (lane == 0) {
+    cx.kind[warp] = (uint8_t)kind;
+    cx.gs[warp] = (uint8_t)gs;
+    cx.pr[warp] = (uint8_t)pr;
+    reinterpret_cast<uint16_t*>(&cx.shv)[warp] = sh;
+    reinterpret_cast<int8_t*>(&cx.zv)[warp] = z;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    // the item list: irregular groups, then 4-bit (4 items of 32 rows each),
+    // then 2-bit groups (2 items of 64 rows), each kind in group order
+    const int kd = lane < kTileGroups ? cx.kind[lane] : kEncKindNone;
+    const int n = kd == kEncKind2 ? 2 : kd == kEncKindNone ? 0 : 4;
+    const unsigned below = (1u << lane) - 1u;
+    int pos = 0;
+    const int order[3] = {kEncKindIrr, kEncKind4, kEncKind2};
+#pragma unroll
+    for (int q = 0; q < 3; ++q) {
+      const unsigned m = __ballot_sync(0xffffffffu, kd == order[q]);
+      const int per = order[q] == kEncKind2 ? 2 : 4;
+      if (kd == order[q]) pos += per * __popc(m & below);
+      else if ((kd == kEncKind4 && q == 0) || (kd == kEncKind2 && q < 2)) pos += per * __popc(m);
+    }
+    for (int k = 0; k < n; ++k)
+      cx.items[pos + k] = (uint8_t)(n == 2 ? (lane | ((2 * k) << 3) | (1 << 5)) : (lane | (k << 3)));
+    int tot = n;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+    if (lane == 0) cx.nitems = tot;
+  }
+  // 2nd-order codes by (row mod rp, group) from the final chunk table
+  const ChunkLayout& cl = a.cl;
+  const int P256 = cl.period * kGroup2;
+  for (int e = tid; e < rp * kTileGroups; e += blockDim.x) {
+    const int rho = e >> 3, gw = e & 7;
+    const int64_t gg = (int64_t)ct * kTileGroups + gw;
+    uint8_t q = 0;
+    if (gg < ng) {
+      const int u = (int)(((int64_t)rho * ng + gg) % P256);
+      const float4 ch = a.ws.chunk_tab[min(u >> 8, cl.ntab_full)];
+      const float s1f =
+          __half2float(__ushort_as_half(reinterpret_cast<const uint16_t*>(&cx.shv)[gw]));
+      const int q2 = f2i_rz(roundf(__fdiv_rn(__fsub_rn(s1f, ch.x), ch.y)));
+      q = (uint8_t)max(0, min(15, q2));
+    }
+    cx.sqrow[rho][gw] = q;
+  }
+  __syncthreads();
+}
+
+// 2nd-order code of scales_1st[r, g] (quantize.cu:274-280) computed directly.
+__device__ __forceinline__ uint8_t sq_direct(const QArgs& a, float s1f, int64_t r, int64_t g) {
+  const ChunkLayout& cl = a.cl;
+  const int64_t si = r * a.ng + g;
+  const int idx = si < cl.nfull * kGroup2 ? (int)((si % ((int64_t)cl.period * kGroup2)) >> 8)
+                                          : cl.ntab_full;
+  const float4 ch = a.ws.chunk_tab[idx];
+  const int q2 = f2i_rz(roundf(__fdiv_rn(__fsub_rn(s1f, ch.x), ch.y)));
+  return (uint8_t)max(0, min(15, q2));
 }
 
 __global__ void __launch_bounds__(256, 2)
@@ -1995,198 +1981,213 @@ __global__ void __launch_bounds__(256, 2)
   extern __shared__ uint8_t dsm_raw[];
   uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) &
                                             ~(uintptr_t)1023);
-  __shared__ TileRing<kEncStages> R;
-  __shared__ EncStage st;
-  __shared__ EncParamSlot pslot[2];
-  __shared__ int s_u0;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __shared__ uint64_t full[kEncStages];
+  __shared__ EncCtx cx;
+  __shared__ EncCodes cbuf[2];
+  __shared__ int item_next[2];  // next item of the tiles using code buffer 0 / 1
+  const int tid = threadIdx.x, lane = tid & 31;
   const int64_t M = a.M;
-  const int ng = a.ng, nrc = a.nrc, nct = a.nct;
-  const int64_t ntiles = (int64_t)nct * nrc;
-  if (tid == 0) {  // W is an input: its loads may start before the wait below
-    R.parity_pending = 0;
-    for (int s = 0; s < kEncStages; ++s) mbar_init(&R.full[s], 1);
+  const int ng = a.ng, nrc = a.nrc;
+  // The CTA's tiles [S0, S1) come from the selection (weighted by work);
+  // tile u = ct * nrc + rc, and (ct, rc) advance without divisions.
+  struct Seq {
+    int ct, rc;
+  };
+  auto seq_next = [&](Seq& q) {
+    if (++q.rc == nrc) {
+      q.rc = 0;
+      ++q.ct;
+    }
+  };
+  auto issue = [&](const Seq& q, int s) {
+    uint8_t* dst = dsm + (size_t)s * kTileBytes;
+    mbar_arrive_expect_tx(&full[s], kTileBytes);
+    tma_load_2d(dst, &tmap, &full[s], q.ct * kTileCols, q.rc * kChunkRows);
+    tma_load_2d(dst + kBoxBytes, &tmap, &full[s], q.ct * kTileCols + 64, q.rc * kChunkRows);
+  };
+  if (tid == 0 && use_tma) {
+    for (int s = 0; s < kEncStages; ++s) mbar_init(&full[s], 1);
     fence_mbar_init();
-    for (int s = 0; s < kEncStages; ++s)
-      ring_issue(R, s, &tmap, dsm, blockIdx.x + (int64_t)s * gridDim.x, ntiles, nct, use_tma);
   }
-  grid_dependency_wait();  // the selection is complete
-  const bool write_sq = a.ws.hdr->n_pend == 0;
-  const int ntab = a.cl.ntab_full + 1;
-  const bool tab_smem = ntab <= kEncTabMax;  // else codes are computed per (row, group)
-  const float4* tab = a.ws.chunk_tab;
-  const int p256 = a.cl.period * kGroup2;
-  int dstep[kSteps];  // (32 s ng) mod (period * 256)
-#pragma unroll
-  for (int k = 0; k < kSteps; ++k) dstep[k] = (int)((32 * k * (int64_t)ng) % p256);
-  if ((int64_t)blockIdx.x < ntiles) enc_prefetch(a, pslot[0], blockIdx.x, warp, lane);
-  cp_async_commit();
-  __syncthreads();
+  if (tid < 2) item_next[tid] = 0;  // visible after the context's barriers
+  grid_dependency_wait();  // the selection, parameters, 2nd-order table and ranges are final
+  const int64_t S0 = a.ws.enc_start[blockIdx.x], S1 = a.ws.enc_start[blockIdx.x + 1];
+  const int64_t ntile_cta = S1 - S0;
+  Seq ahead{(int)(S0 / nrc), (int)(S0 % nrc)};  // thread 0: the next tile to load
+  if (tid == 0 && use_tma)
+    for (int s = 0; s < kEncStages && s < ntile_cta; ++s) {
+      issue(ahead, s);
+      seq_next(ahead);
+    }
+  const int P256 = a.cl.period * kGroup2;
+  const int rp = P256 / ng;  // a power of two, at most 256
+  const int64_t row_full_end = a.cl.nfull * kGroup2;
+  const int64_t full_rows = row_full_end / ng;  // rows whose scales lie in full 2nd-order chunks
   bool failed = false;
-  int i = 0;
-  for (;; ++i) {
-    const int sg = i % kEncStages;
-    const int64_t t = R.tile[sg];
-    if (t >= ntiles) break;
-    uint8_t* buf = dsm + (size_t)sg * kTileBytes;
-    const int rc = (int)(t / nct), ct = (int)(t % nct);
-    const int64_t row0 = (int64_t)rc * kChunkRows;
-    if (tid == 0) s_u0 = (int)((row0 * (int64_t)ng) % p256);
-    cp_async_wait_all();  // this tile's parameters
-    __syncthreads();
-    // the next tile's parameters go into the other slot meanwhile
-    const int64_t tnext = t + gridDim.x;
-    if (tnext < ntiles) enc_prefetch(a, pslot[(i + 1) & 1], tnext, warp, lane);
-    cp_async_commit();
-    const EncParamSlot& ps = pslot[i & 1];
-    if (lane == 0) {
-      const int64_t gw = (int64_t)ct * kTileGroups + warp;
-      const uint8_t pw =
-          gw < ng ? (uint8_t)(ps.prec[warp] >> (8 * (int)((uintptr_t)(a.ws.prec + gw) & 3))) : 2;
-      st.keep[warp] = pw < 2;
-      if (pw < 2) {
-        st.sh[warp] = (uint16_t)ps.p[warp][pw].scale_h;
-        st.z[warp] = (int8_t)ps.p[warp][pw].zero;
-      }
+  uint32_t bad = 0;  // thread 0: stages whose wait ran out
+  int cur_ct = -1;
+  Seq cur{(int)(S0 / nrc), (int)(S0 % nrc)};
+  for (int64_t i = 0; i < ntile_cta; ++i, seq_next(cur)) {
+    const int ct = cur.ct, rc = cur.rc;
+    const int s = (int)(i & 1);
+    if (ct != cur_ct) {
+      if (cur_ct >= 0) __syncthreads();  // the previous write-out is done with the context
+      enc_build_ctx(a, cx, ct, rp);
+      cur_ct = ct;
     }
+    uint8_t* buf = dsm + (size_t)s * kTileBytes;
     if (use_tma) {
-      bool ok = true;
-      if (tid == 0) ok = ring_wait(R, sg, i);
-      failed |= __syncthreads_or(!ok) != 0;
+      const bool ok = mbar_wait(&full[s], (uint32_t)((i >> 1) & 1));
+      failed |= !ok;
+      if (tid == 0 && !ok) bad |= 1u << s;
     } else {
-      tile_fill(a.W, M, a.K, buf, t, nct, 0);
+      tile_fill(a.W, M, a.K, buf, (int64_t)rc * a.nct + ct, a.nct, 0);
       __syncthreads();
     }
-    // 2nd-order codes of this tile's groups for every table entry
-    if (write_sq && tab_smem) {
-      for (int k = tid; k < kTileGroups * ntab; k += blockDim.x) {
-        const int gw = k / ntab, idx = k % ntab;
-        if (!st.keep[gw]) continue;
-        const int64_t g = (int64_t)ct * kTileGroups + gw;
-        const uint8_t pr =
-            (uint8_t)(ps.prec[gw] >> (8 * (int)((uintptr_t)(a.ws.prec + g) & 3)));
-        const float s1f = __half2float(__ushort_as_half((uint16_t)ps.p[gw][pr].scale_h));
-        const float4 ch = tab[idx];
-        const int q2 = f2i_rz(roundf(__fdiv_rn(__fsub_rn(s1f, ch.x), ch.y)));
-        st.q2[gw][idx] = (uint8_t)max(0, min(15, q2));
-      }
-      __syncthreads();
-    }
-    // (row0 + lane) * ng mod (period * 256), the 2nd-order position of the
-    // lane's row in step 0
-    const int u_lane = write_sq ? (int)(((int64_t)s_u0 + (int64_t)lane * ng) % p256) : 0;
-    // work items (group, 32-row step): warp w takes items w, w+8, w+16, w+24,
-    // i.e. one step of four groups, so 4-bit groups spread over the warps
+    const int64_t row0 = (int64_t)rc * kChunkRows;
+    const int nr = (int)min64(kChunkRows, M - row0);
+    EncCodes& cb = cbuf[i & 1];
+    const int nitems = cx.nitems;
 #pragma unroll 1
-    for (int k = warp; k < kTileGroups * kSteps; k += kTileGroups) {
-      const int gw = k >> 2, s = k & 3;
-      if (!st.keep[gw]) continue;
-      const int64_t g = (int64_t)ct * kTileGroups + gw;
-      const uint8_t pr =
-          (uint8_t)(ps.prec[gw] >> (8 * (int)((uintptr_t)(a.ws.prec + g) & 3)));
-      const GroupParams& gpar = ps.p[gw][pr];
-      const bool four = pr != 0;
-      const int gs = (int)min64(kGroup1, a.K - g * kGroup1);
-      const int r = s * 32 + lane;
-      const uint8_t* row_base = buf + (gw >> 2) * kBoxBytes + r * 128;
-      const int c0 = 2 * (gw & 3), sw = r & 7;
+    for (;;) {
+      int j = 0;
+      if (lane == 0) j = atomicAdd(&item_next[i & 1], 1);
+      j = __shfl_sync(0xffffffffu, j, 0);
+      if (j >= nitems) break;
+      const int it = cx.items[j];
+      const int gw = it & 7, st = (it >> 3) & 3;
+      if (st * 32 >= nr) continue;
+      const int r0 = st * 32 + lane;  // rows r0 (and r0 + 32 for 2-bit; same swizzle phase)
+      const uint8_t* rb = buf + (gw >> 2) * kBoxBytes + r0 * 128;
+      const int c0 = 2 * (gw & 3), sw = lane & 7;
       const int lo_off = (c0 ^ sw) << 4, hi_off = ((c0 + 1) ^ sw) << 4;
-      Row16 v;
-      v.lo = *reinterpret_cast<const uint4*>(row_base + lo_off);
-      v.hi = *reinterpret_cast<const uint4*>(row_base + hi_off);
-      uint32_t wa, wb;
-      const int cnt = encode_run_tile(v, gpar, row_base, lo_off, hi_off, gs, wa, wb);
-      st.p2[gw][r] = four ? 0u : wa;
-      st.p4[gw][r] = four ? make_uint2(wa, wb) : make_uint2(0u, 0u);
-      if (write_sq) {
-        int u = u_lane + dstep[s];
-        if (u >= p256) u -= p256;
-        if (tab_smem) {
-          const int64_t si = (row0 + r) * ng + g;
-          int idx = a.cl.ntab_full;
-          if (si < a.cl.nfull * kGroup2) {
-            int jt = u + (int)g;
-            if (jt >= p256) jt -= p256;
-            idx = jt >> 8;
-          }
-          st.sq[gw][r] = st.q2[gw][idx];
-        } else {
-          const float s1f = __half2float(__ushort_as_half((uint16_t)gpar.scale_h));
-          st.sq[gw][r] = second_order_code(a, tab, s1f, row0 + r, (int)g, u);
+      auto run_at = [&](int h) {
+        Row16 v;
+        v.lo = *reinterpret_cast<const uint4*>(rb + 32 * 128 * h + lo_off);
+        v.hi = *reinterpret_cast<const uint4*>(rb + 32 * 128 * h + hi_off);
+        return v;
+      };
+      const int kind = cx.kind[gw];
+      const int gs = cx.gs[gw];
+      if (kind == kEncKind2) {
+        const Row16 v0 = run_at(0), v1 = run_at(1);
+        const uint4 T = cx.thr[gw][0];
+        uint32_t w0 = enc2_run(v0, T.x, T.y, T.z), w1 = enc2_run(v1, T.x, T.y, T.z);
+        if (gs < kGroup1) {  // columns past K hold code 0
+          w0 &= (1u << (2 * gs)) - 1u;
+          w1 &= (1u << (2 * gs)) - 1u;
         }
+        cb.p2[gw][r0] = w0;
+        cb.p2[gw][r0 + 32] = w1;
+        cb.p4[gw][r0] = make_uint2(0u, 0u);
+        cb.p4[gw][r0 + 32] = make_uint2(0u, 0u);
+      } else if (kind == kEncKind4) {
+        uint32_t t[16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 T = cx.thr[gw][q];
+          t[4 * q] = T.x;
+          t[4 * q + 1] = T.y;
+          t[4 * q + 2] = T.z;
+          t[4 * q + 3] = T.w;
+        }
+        const uint32_t ma = gs >= 8 ? 0xFFFFFFFFu : ((1u << (4 * gs)) - 1u);
+        const uint32_t mb = gs <= 8 ? 0u : gs >= 16 ? 0xFFFFFFFFu : ((1u << (4 * (gs - 8))) - 1u);
+        uint2 c;
+        enc4_run(run_at(0), t, c.x, c.y);
+        cb.p2[gw][r0] = 0u;
+        cb.p4[gw][r0] = make_uint2(c.x & ma, c.y & mb);  // columns past K: code 0
+      } else {
+        const int64_t g = (int64_t)ct * kTileGroups + gw;
+        const GroupParams& gp = a.ws.params[2 * g + cx.pr[gw]];
+        const bool four = cx.pr[gw] != 0;
+        const uint3 c = enc_irregular(gp, rb, lo_off, hi_off, gs);
+        if (c.z && r0 < nr) atomicAdd(a.ws.row_counts + row0 + r0, (int)c.z);
+        cb.p2[gw][r0] = four ? 0u : c.x;
+        cb.p4[gw][r0] = four ? make_uint2(c.x, c.y) : make_uint2(0u, 0u);
       }
-      if (cnt && row0 + r < M) atomicAdd(a.ws.row_counts + row0 + r, cnt);
     }
     __syncthreads();  // codes staged; the tile buffer is free
-    if (tid == 0)
-      ring_issue(R, sg, &tmap, dsm, t + (int64_t)kEncStages * gridDim.x, ntiles, nct, use_tma);
-    const int nr = (int)min64(kChunkRows, M - row0);
-    const int64_t gb = (int64_t)ct * kTileGroups;
-    bool all8 = gb + kTileGroups <= ng;
-#pragma unroll
-    for (int w = 0; w < kTileGroups; ++w) all8 &= st.keep[w] != 0;
-    if (vec_out && all8) {
+    if (tid == 32) item_next[i & 1] = 0;  // its next user starts after the next barrier
+    if (tid == 0 && use_tma && i + kEncStages < ntile_cta) {
+      fence_proxy_async_smem();
+      issue(ahead, s);
+      seq_next(ahead);
+    }
+    const int gb = ct * kTileGroups;
+    const int64_t obase = row0 * ng + gb;  // flat index of (row0, gb)
+    if (vec_out && gb + kTileGroups <= ng) {
       for (int k = tid; k < nr * 2; k += blockDim.x) {
         const int r = k >> 1, h = k & 1;
-        const uint4 v = make_uint4(st.p2[4 * h][r], st.p2[4 * h + 1][r], st.p2[4 * h + 2][r],
-                                   st.p2[4 * h + 3][r]);
-        reinterpret_cast<uint4*>(a.packed2 + (row0 + r) * ng + gb)[h] = v;
+        const uint4 x = make_uint4(cb.p2[4 * h][r], cb.p2[4 * h + 1][r], cb.p2[4 * h + 2][r],
+                                   cb.p2[4 * h + 3][r]);
+        reinterpret_cast<uint4*>(a.packed2 + obase + r * ng)[h] = x;
       }
       for (int k = tid; k < nr * 4; k += blockDim.x) {
         const int r = k >> 2, q = k & 3;
-        const uint2 x = st.p4[2 * q][r], y = st.p4[2 * q + 1][r];
-        reinterpret_cast<uint4*>(a.packed4 + 2 * ((row0 + r) * ng + gb))[q] =
+        const uint2 x = cb.p4[2 * q][r], y = cb.p4[2 * q + 1][r];
+        reinterpret_cast<uint4*>(a.packed4 + 2 * (obase + r * ng))[q] =
             make_uint4(x.x, x.y, y.x, y.y);
       }
-      const uint4 shv = *reinterpret_cast<const uint4*>(st.sh);
-      const uint2 zv = *reinterpret_cast<const uint2*>(st.z);
+      const uint4 shv = cx.shv;
+      const uint2 zv = cx.zv;
+      // rows before nfast take their 2nd-order codes from the table
+      const int nfast = (int)max64(0, min64(nr, full_rows - row0));
       for (int r = tid; r < nr; r += blockDim.x) {
-        *reinterpret_cast<uint4*>(a.scales1 + (row0 + r) * ng + gb) = shv;
-        *reinterpret_cast<uint2*>(a.zeros1 + (row0 + r) * ng + gb) = zv;
-        if (write_sq) {
-          uint32_t lo = 0, hi = 0;
+        const int64_t o = obase + r * ng;
+        *reinterpret_cast<uint4*>(a.scales1 + o) = shv;
+        *reinterpret_cast<uint2*>(a.zeros1 + o) = zv;
+        uint2 q;
+        if (r < nfast) {
+          q = *reinterpret_cast<const uint2*>(&cx.sqrow[(rc * kChunkRows + r) & (rp - 1)][0]);
+        } else {
+          uint8_t b[kTileGroups];
 #pragma unroll
-          for (int w = 0; w < 4; ++w) {
-            lo |= (uint32_t)st.sq[w][r] << (8 * w);
-            hi |= (uint32_t)st.sq[4 + w][r] << (8 * w);
-          }
-          *reinterpret_cast<uint2*>(a.sq + (row0 + r) * ng + gb) = make_uint2(lo, hi);
+          for (int w = 0; w < kTileGroups; ++w)
+            b[w] = sq_direct(a, __half2float(__ushort_as_half(
+                                    reinterpret_cast<const uint16_t*>(&cx.shv)[w])),
+                             row0 + r, gb + w);
+          q.x = b[0] | (b[1] << 8) | (b[2] << 16) | ((uint32_t)b[3] << 24);
+          q.y = b[4] | (b[5] << 8) | (b[6] << 16) | ((uint32_t)b[7] << 24);
         }
+        *reinterpret_cast<uint2*>(a.sq + o) = q;
       }
     } else {
       for (int k = tid; k < nr * kTileGroups; k += blockDim.x) {
-        const int r = k / kTileGroups, w = k % kTileGroups;
-        if (!st.keep[w]) continue;
-        const int64_t si = (row0 + r) * ng + gb + w;
-        a.packed2[si] = (int32_t)st.p2[w][r];
-        reinterpret_cast<uint2*>(a.packed4)[si] = st.p4[w][r];
-        a.scales1[si] = __ushort_as_half(st.sh[w]);
-        a.zeros1[si] = st.z[w];
-        if (write_sq) a.sq[si] = st.sq[w][r];
+        const int r = k >> 3, w = k & 7;
+        const int g = gb + w;
+        if (g >= ng) continue;
+        const int64_t row = row0 + r;
+        const int64_t si = row * ng + g;
+        a.packed2[si] = (int32_t)cb.p2[w][r];
+        reinterpret_cast<uint2*>(a.packed4)[si] = cb.p4[w][r];
+        const uint16_t shb = reinterpret_cast<const uint16_t*>(&cx.shv)[w];
+        a.scales1[si] = __ushort_as_half(shb);
+        a.zeros1[si] = reinterpret_cast<const int8_t*>(&cx.zv)[w];
+        a.sq[si] = (row + 1) * ng <= row_full_end
+                       ? cx.sqrow[row & (rp - 1)][w]
+                       : sq_direct(a, __half2float(__ushort_as_half(shb)), row, g);
       }
     }
-    __syncthreads();  // staging is free again
   }
-  cp_async_wait_all();
   grid_launch_dependents();
+  failed = __syncthreads_or(failed) != 0;
   if (tid == 0) {
     if (failed) atomicOr(&a.ws.hdr->status, kStatusTimeout);
-    ring_drain(R, i);
+    // loads whose wait ran out may still be in flight: let them land
+    for (int s = 0; s < kEncStages; ++s)
+      if (bad & (1u << s)) (void)mbar_wait(&full[s], 0u), (void)mbar_wait(&full[s], 1u);
   }
 }
 
 // ---------------------------------------------------------------------------
-// post: 2nd-order scales / zeros / codes (quantize.cu:245-281 over the
-// flattened [M, ng] scales), the pending groups' codes, and the outlier row
-// pointers (torch_ops.cu:210-229).
+// post: 2nd-order scales / zeros (quantize.cu:245-272 over the flattened
+// [M, ng] scales) and the outlier row pointers (torch_ops.cu:210-229).
 // ---------------------------------------------------------------------------
-constexpr int kPostRows = 16;
-
 __global__ void __launch_bounds__(256) post_kernel(const QArgs a) {
-  grid_dependency_wait();  // encode (and the exact selection) complete
+  grid_dependency_wait();  // encode complete
   const Header* hdr = a.ws.hdr;
   const int64_t M = a.M;
-  const int ng = a.ng;
   const int tid = threadIdx.x;
   const int64_t gtid = (int64_t)blockIdx.x * blockDim.x + tid;
   const int64_t gthreads = (int64_t)gridDim.x * blockDim.x;
@@ -2195,37 +2196,6 @@ __global__ void __launch_bounds__(256) post_kernel(const QArgs a) {
     const float4 e = a.ws.chunk_tab[c < cl.nfull ? (int)(c % cl.period) : cl.ntab_full];
     a.scales2[c] = __ushort_as_half((uint16_t)__float_as_int(e.z));
     a.zeros2[c] = (int8_t)__float_as_int(e.w);
-  }
-  // 2nd-order codes (quantize.cu:274-280), unless encode wrote them (no
-  // group was pending): block b covers rows [b * kPostRows, ...), thread t
-  // groups t, t + 256, ...  Flat index r*ng + g lies in full chunk (jt >> 8)
-  // of one period (period * 256 = lcm(ng, 256) flat indices), advanced by ng
-  // per row.
-  const int P256 = cl.period * kGroup2;
-  const int64_t full_end = cl.nfull * kGroup2;
-  const uint32_t np = hdr->n_pend, ndec = hdr->n_dec;
-  for (int64_t rb = blockIdx.x; np > 0 && rb * kPostRows < M; rb += gridDim.x) {
-    const int64_t r0 = rb * kPostRows, r1 = min64(M, r0 + kPostRows);
-    for (int g = tid; g < ng; g += blockDim.x) {
-      const float s1f = __half2float(
-          __ushort_as_half((uint16_t)a.ws.params[2 * g + a.ws.prec[g]].scale_h));
-      int jt = (int)((r0 * ng + g) % P256);
-      for (int64_t r = r0; r < r1; ++r) {
-        const int64_t si = r * ng + g;
-        const float4 ch = a.ws.chunk_tab[si < full_end ? (jt >> 8) : cl.ntab_full];
-        const int q2 = f2i_rz(roundf(__fdiv_rn(__fsub_rn(s1f, ch.x), ch.y)));
-        a.sq[si] = (uint8_t)max(0, min(15, q2));
-        jt += ng;
-        if (jt >= P256) jt -= P256;
-      }
-    }
-  }
-  // the pending groups, now decided
-  const int64_t nrb = ceil_div(M, kEncRows);
-  for (int64_t w = gtid; w < (int64_t)np * nrb; w += gthreads) {
-    const int u = (int)(w / nrb);
-    const int64_t r0 = (w % nrb) * kEncRows;
-    encode_rows(a, a.ws.order[ndec + u], r0, min64(M, r0 + kEncRows));
   }
   const bool any_irr = hdr->any_irregular != 0;
   if (!any_irr) {
@@ -2415,6 +2385,19 @@ extern "C" mb_status mb_quantize(const void* weights_fp16, int64_t M, int64_t K,
   MB_CUDA_TRY(cudaGetDevice(&dev));
   MB_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   const int64_t ntiles = nct * nrc;
+  // the encode grid (persistent: every CTA resident), known to the selection,
+  // which splits the tiles among its CTAs
+  int64_t enc_grid = 1;
+  {
+    static std::atomic<uint64_t> attr_done{0};
+    MB_CUDA_TRY(set_smem_limit_once(encode_kernel, kEncSmem, attr_done));
+    int per_sm = 0;
+    MB_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, encode_kernel, 256,
+                                                              kEncSmem));
+    enc_grid = std::max<int64_t>(
+        1, std::min<int64_t>({ntiles, (int64_t)sms * std::max(per_sm, 1), (int64_t)kMaxEncGrid}));
+  }
+  qa.enc_grid = (int)enc_grid;
   {
     auto kern = sens ? stats_kernel<true> : stats_kernel<false>;
     static std::atomic<uint64_t> attr_done[2] = {{0}, {0}};
@@ -2438,23 +2421,17 @@ extern "C" mb_status mb_quantize(const void* weights_fp16, int64_t M, int64_t K,
   if (mb_status st = launch_pdl(exact_kernel, dim3(kExactCtas), dim3(256), 0, stream, qa))
     return st;
   {
-    static std::atomic<uint64_t> attr_done{0};
-    MB_CUDA_TRY(set_smem_limit_once(encode_kernel, kEncSmem, attr_done));
     const auto al = [](const void* p, unsigned m) {
       return (reinterpret_cast<uintptr_t>(p) & (m - 1)) == 0;
     };
     const int vec_out = (ng % 8 == 0) && al(packed_2bit, 16) && al(packed_4bit, 16) &&
                         al(scales_1st_fp16, 16) && al(zeros_1st, 8) && al(scales_1st_quant, 8);
-    int per_sm = 0;
-    MB_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, encode_kernel, 256,
-                                                              kEncSmem));
-    const int64_t grid =
-        std::max<int64_t>(1, std::min<int64_t>(ntiles, (int64_t)sms * std::max(per_sm, 1)));
-    if (mb_status st = launch_pdl(encode_kernel, dim3((unsigned)grid), dim3(256), kEncSmem,
+    if (mb_status st = launch_pdl(encode_kernel, dim3((unsigned)enc_grid), dim3(256), kEncSmem,
                                   stream, tmap, qa, tma ? 1 : 0, vec_out))
       return st;
   }
-  const int64_t post_grid = std::max<int64_t>(1, std::min<int64_t>(ceil_div(M, kPostRows), 8LL * sms));
+  const int64_t post_grid = std::max<int64_t>(
+      1, std::min<int64_t>(ceil_div(std::max<int64_t>(qa.cl.ng2, M + 1), 256), 2LL * sms));
   return launch_pdl(post_kernel, dim3((unsigned)post_grid), dim3(256), 0, stream, qa);
 }
 
