@@ -1020,6 +1020,16 @@ __device__ __forceinline__ void radix_pick(const uint32_t* hist, uint32_t* s2, u
   }
 }
 
+// hist[bin] += 1 for the lanes with `on`, one shared-memory atomic per
+// distinct bin of the warp (keys cluster in few bins in the early passes).
+__device__ __forceinline__ void hist_add(uint32_t* hist, uint32_t bin, bool on) {
+  const unsigned act = __ballot_sync(0xffffffffu, on);
+  if (!act) return;
+  const unsigned same = __match_any_sync(0xffffffffu, on ? bin : 0xFFFFFFFFu);
+  const int lane = threadIdx.x & 31;
+  if (on && (__ffs(same) - 1) == lane) atomicAdd(&hist[bin], (uint32_t)__popc(same));
+}
+
 // k-th largest (1-based, 1 <= k <= n) of n 32-bit keys key(i), by 4 passes
 // of 8 bits; returns the key and, in *need_eq, how many keys equal to it the
 // k largest include.  All NT threads call it with the same arguments.
@@ -1036,9 +1046,10 @@ __device__ uint32_t kth_largest(int n, int k, KeyF key, uint32_t* hist, uint32_t
     for (int i = tid; i < 256; i += NT) hist[i] = 0;
     sync_nt<NT>();
     const uint32_t prefix = s2[0];
-    for (int i = tid; i < n; i += NT) {
-      const uint32_t kk = key(i);
-      if ((kk & mask) == prefix) atomicAdd(&hist[(kk >> shift) & 255u], 1u);
+    for (int i0 = 0; i0 < n; i0 += NT) {  // whole warps (match_any)
+      const int i = i0 + tid;
+      const uint32_t kk = i < n ? key(i) : 0u;
+      hist_add(hist, (kk >> shift) & 255u, i < n && (kk & mask) == prefix);
     }
     sync_nt<NT>();
     if (warp == 0) radix_pick(hist, s2, prefix, shift, lane);
@@ -1068,10 +1079,11 @@ __device__ void kth_largest2(int n, int ka, KeyA a, int kb, KeyB b, uint32_t* hi
     for (int i = tid; i < 512; i += NT) hist[i] = 0;
     sync_nt<NT>();
     const uint32_t pa = s4[0], pb = s4[2];
-    for (int i = tid; i < n; i += NT) {
-      const uint32_t x = a(i), y = b(i);
-      if ((x & mask) == pa) atomicAdd(&hist[(x >> shift) & 255u], 1u);
-      if ((y & mask) == pb) atomicAdd(&hist[256 + ((y >> shift) & 255u)], 1u);
+    for (int i0 = 0; i0 < n; i0 += NT) {  // whole warps (match_any)
+      const int i = i0 + tid;
+      const uint32_t x = i < n ? a(i) : 0u, y = i < n ? b(i) : 0u;
+      hist_add(hist, (x >> shift) & 255u, i < n && (x & mask) == pa);
+      hist_add(hist, 256 + ((y >> shift) & 255u), i < n && (y & mask) == pb);
     }
     sync_nt<NT>();
     if (warp == 0) radix_pick(hist, s4, pa, shift, lane);
@@ -1190,13 +1202,17 @@ __device__ void finalize_tables(const QArgs& a, float* s1, size_t s1_bytes, uint
   auto scale_of = [&](int g) -> float {
     return s1_in_smem ? s1[g] : scale_from(g, a.ws.prec[g]);
   };
-  // one warp per chunk: min / max of the scales of its (cyclic) group range
+  // Chunk c's scales are the groups s0 mod ng, s0 mod ng + 1, ... (cyclic,
+  // s0 = 256 c; the partial chunk is the last).  Phase 1: one warp per chunk
+  // reduces min / max (into the chunk table's slots); phase 2: one thread per
+  // chunk derives scale / zero.
   const ChunkLayout& cl = a.cl;
   const int nchunks = cl.ntab_full + cl.has_partial;
+  const int64_t step = kGroup2 % ng;  // s0 mod ng advances by this per chunk
   for (int ci = warp; ci < nchunks; ci += NWARP) {
-    const int64_t cidx = ci < cl.ntab_full ? ci : cl.nfull;  // the partial chunk is the last
-    const int64_t s0 = cidx * kGroup2;
-    const int n = (int)min64(kGroup2, cl.total - s0);
+    const bool partial = ci >= cl.ntab_full;
+    const int64_t cidx = partial ? cl.nfull : ci;
+    const int n = (int)min64(kGroup2, cl.total - cidx * kGroup2);
     float mn = 1e10f, mx = -1e10f;
     if (n >= ng) {  // every group at least once
       for (int g = lane; g < ng; g += 32) {
@@ -1205,7 +1221,10 @@ __device__ void finalize_tables(const QArgs& a, float* s1, size_t s1_bytes, uint
         mx = fmaxf(mx, v);
       }
     } else {
-      const int g0 = (int)(s0 % ng);
+      // (cidx * 256) mod ng, without a 64-bit division when the product fits
+      const int64_t prod = cidx * step;
+      const int g0 = prod < (int64_t)0xFFFFFFFF ? (int)((uint32_t)prod % (uint32_t)ng)
+                                                : (int)(prod % ng);
       for (int k = lane; k < n; k += 32) {
         int g = g0 + k;
         if (g >= ng) g -= ng;
@@ -1216,15 +1235,18 @@ __device__ void finalize_tables(const QArgs& a, float* s1, size_t s1_bytes, uint
     }
     mn = warp_min(mn);
     mx = warp_max(mx);
-    if (lane == 0) {
-      float sc2 = __fdiv_rn(__fsub_rn(mx, mn), 15.0f);
-      if (sc2 < 1e-10f) sc2 = 1e-10f;
-      const int z2 = f2i_rz(roundf(__fdiv_rn(-mn, sc2)));
-      const int slot = ci < cl.ntab_full ? ci : cl.ntab_full;
-      a.ws.chunk_tab[slot] =
-          make_float4(mn, sc2, __int_as_float((int)__half_as_ushort(__float2half_rn(sc2))),
-                      __int_as_float((int)(int8_t)z2));
-    }
+    if (lane == 0) a.ws.chunk_tab[partial ? cl.ntab_full : ci] = make_float4(mn, mx, 0.f, 0.f);
+  }
+  sync_nt<NT>();
+  for (int ci = tid; ci < nchunks; ci += NT) {
+    float4* e = a.ws.chunk_tab + (ci < cl.ntab_full ? ci : cl.ntab_full);
+    const float4 r = __ldcg(e);
+    const float mn = r.x, mx = r.y;
+    float sc2 = __fdiv_rn(__fsub_rn(mx, mn), 15.0f);
+    if (sc2 < 1e-10f) sc2 = 1e-10f;
+    const int z2 = f2i_rz(roundf(__fdiv_rn(-mn, sc2)));
+    *e = make_float4(mn, sc2, __int_as_float((int)__half_as_ushort(__float2half_rn(sc2))),
+                     __int_as_float((int)(int8_t)z2));
   }
   if (tid == 0) {
     a.ws.hdr->any_irregular = *s_irr;
@@ -1268,7 +1290,6 @@ __device__ void select_from_intervals(const QArgs& a, uint8_t* scratch, size_t s
   __shared__ uint32_t s4[4];
   __shared__ uint32_t s_wsum[NWARP];
   __shared__ uint32_t s_cnt[2];
-  __shared__ int s_irr;
   uint2* keys = reinterpret_cast<uint2*>(scratch);
   const bool keys_in_smem = (size_t)ng * 8 <= scratch_bytes;
   auto lo_of = [&](int g) -> uint32_t { return keys_in_smem ? keys[g].x : __ldcg(a.ws.gkey + g).x; };
@@ -1320,8 +1341,26 @@ __device__ void select_from_intervals(const QArgs& a, uint8_t* scratch, size_t s
   }
   sync_nt<NT>();
   if (!pending) {
-    finalize_tables<NT>(a, reinterpret_cast<float*>(scratch), scratch_bytes, s_wsum, &s_irr,
-                        true);
+    // every precision is known: the column tiles' encode work and the tile
+    // split here; group_precision, any_irregular and the 2nd-order table are
+    // written by the CTAs of the next kernel in parallel (tables_grid)
+    uint32_t* s_cost = reinterpret_cast<uint32_t*>(scratch);  // the keys are done with
+    const bool cost_in_smem = (size_t)a.nct * sizeof(uint32_t) <= scratch_bytes;
+    if (cost_in_smem) {
+      for (int ct = tid; ct < a.nct; ct += NT) s_cost[ct] = 160;
+      sync_nt<NT>();
+      for (int g = tid; g < ng; g += NT) {
+        const int pr = a.ws.prec[g];
+        const bool reg = (a.ws.greg[g] >> pr) & 1;
+        atomicAdd(&s_cost[g / kTileGroups], !reg ? 180u : pr ? 54u : 20u);
+      }
+      sync_nt<NT>();
+    }
+    enc_partition<NT>(a, cost_in_smem ? s_cost : nullptr);
+    if (tid == 0) {
+      a.ws.hdr->n_dec = (uint32_t)ng;
+      a.ws.hdr->n_pend = 0;
+    }
     return;
   }
   // pending: order = decided 2-bit, decided 4-bit, pending (each ascending)
@@ -1844,12 +1883,74 @@ __device__ __noinline__ void exact_ctas(const QArgs& a) {
   }
 }
 
-// Exact sums of the pending groups: a kernel of its own between stats and
-// encode, which returns at once when nothing is pending.
+// group_precision, any_irregular and the 2nd-order chunk table
+// (quantize.cu:245-272) once every precision is known, by all CTAs of the
+// grid: threads over groups, one warp per chunk.  Chunk c's scales are those
+// of the groups s0 mod ng, s0 mod ng + 1, ... (cyclic, s0 = 256 c; the
+// partial chunk is the last).
+__device__ __noinline__ void tables_grid(const QArgs& a) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int ng = a.ng;
+  bool irr = false;
+  for (int g = blockIdx.x * blockDim.x + tid; g < ng; g += gridDim.x * blockDim.x) {
+    const uint8_t pr = a.ws.prec[g];
+    a.gp[g] = pr;
+    irr |= !((a.ws.greg[g] >> pr) & 1);
+  }
+  if (__any_sync(0xffffffffu, irr) && lane == 0) atomicOr(&a.ws.hdr->any_irregular, 1u);
+  auto scale_of = [&](int g) -> float {
+    const uint32_t sh2 = __ldcg(a.ws.gscale + g);
+    return __half2float(
+        __ushort_as_half((uint16_t)(a.ws.prec[g] ? (sh2 >> 16) : (sh2 & 0xFFFFu))));
+  };
+  const ChunkLayout& cl = a.cl;
+  const int nchunks = cl.ntab_full + cl.has_partial;
+  const int64_t step = kGroup2 % ng;  // s0 mod ng advances by this per chunk
+  const int nwarps = gridDim.x * (blockDim.x >> 5);
+  for (int ci = blockIdx.x * (blockDim.x >> 5) + warp; ci < nchunks; ci += nwarps) {
+    const bool partial = ci >= cl.ntab_full;
+    const int64_t cidx = partial ? cl.nfull : ci;
+    const int n = (int)min64(kGroup2, cl.total - cidx * kGroup2);
+    float mn = 1e10f, mx = -1e10f;
+    if (n >= ng) {  // every group at least once
+      for (int g = lane; g < ng; g += 32) {
+        const float v = scale_of(g);
+        mn = fminf(mn, v);
+        mx = fmaxf(mx, v);
+      }
+    } else {
+      const int g0 = (int)((cidx * step) % ng);
+      for (int k = lane; k < n; k += 32) {
+        int g = g0 + k;
+        if (g >= ng) g -= ng;
+        const float v = scale_of(g);
+        mn = fminf(mn, v);
+        mx = fmaxf(mx, v);
+      }
+    }
+    mn = warp_min(mn);
+    mx = warp_max(mx);
+    if (lane == 0) {
+      float sc2 = __fdiv_rn(__fsub_rn(mx, mn), 15.0f);
+      if (sc2 < 1e-10f) sc2 = 1e-10f;
+      const int z2 = f2i_rz(roundf(__fdiv_rn(-mn, sc2)));
+      a.ws.chunk_tab[partial ? cl.ntab_full : ci] =
+          make_float4(mn, sc2, __int_as_float((int)__half_as_ushort(__float2half_rn(sc2))),
+                      __int_as_float((int)(int8_t)z2));
+    }
+  }
+}
+
+// Between the selection and encode: the tables when every precision is
+// known, else the exact sums of the pending groups (whose last warp completes
+// the selection and the tables).
 __global__ void __launch_bounds__(256) exact_kernel(const QArgs a) {
-  grid_launch_dependents();  // encode may start loading W
-  grid_dependency_wait();    // stats (and its selection) complete
-  exact_ctas(a);
+  grid_launch_dependents();  // encode may start launching
+  grid_dependency_wait();    // stats, assemble and the selection complete
+  if (*reinterpret_cast<const volatile uint32_t*>(&a.ws.hdr->n_pend) == 0)
+    tables_grid(a);
+  else
+    exact_ctas(a);
 }
 
 // encode: persistent CTAs over the 128 x 128 tiles of W.  CTA b takes a
