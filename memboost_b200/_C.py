@@ -268,11 +268,13 @@ class QuantizePlan:
     matrices on one device (whole-model loops, benchmarks).
 
     ``launch`` enqueues phase 1 (every output except the CSR arrays) on the
-    current stream without synchronising; ``finish`` reads the outlier count
-    (one stream synchronisation) and extracts the CSR arrays.  Launching
-    several plans before finishing any keeps the GPU busy across matrices.
-    The tensors returned by ``finish`` alias the plan's buffers until the
-    next ``launch``.
+    current stream without synchronising, followed by an asynchronous copy of
+    the outlier count into pinned host memory and an event; ``finish`` waits
+    for that event only (work enqueued after this plan's launch keeps
+    running), reads the count and extracts the CSR arrays.  Launching several
+    plans before finishing any keeps the GPU busy across matrices.  The
+    tensors returned by ``finish`` alias the plan's buffers until the next
+    ``launch``.
     """
 
     def __init__(self, M: int, K: int, device=None):
@@ -286,6 +288,8 @@ class QuantizePlan:
                     e((M, ng), torch.int8), e((ng2,), torch.float16), e((ng2,), torch.int8),
                     e((M, ng), torch.uint8), e((ng,), torch.uint8)]
         self.row_ptrs = e((M + 1,), torch.int32)
+        self.nnz_host = torch.zeros((1,), dtype=torch.int32).pin_memory()
+        self.done = torch.cuda.Event()
         self._w = None
 
     def launch(self, weights: torch.Tensor, ratio_4bit: float = 0.1,
@@ -300,10 +304,14 @@ class QuantizePlan:
             0 if h is None else h.numel(), _ptr(o[0]), _ptr(o[1]), _ptr(o[2]), _ptr(o[3]),
             _ptr(o[4]), _ptr(o[5]), _ptr(o[6]), _ptr(o[7]), _ptr(self.row_ptrs),
             _ptr(self.ws.nnz), _ptr(self.ws.buf), self.ws.nbytes, _stream(self.device)))
+        with torch.cuda.device(self.device):
+            self.nnz_host.copy_(self.ws.nnz, non_blocking=True)
+            self.done.record()
         self._w = weights
 
     def finish(self) -> list:
-        nnz = int(self.ws.nnz.item())
+        self.done.synchronize()
+        nnz = int(self.nnz_host[0])
         dev = self.device
         vals = torch.empty((nnz,), dtype=torch.float16, device=dev)
         cols = torch.empty((nnz,), dtype=torch.int32, device=dev)

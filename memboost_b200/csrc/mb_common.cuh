@@ -57,6 +57,33 @@ inline cudaError_t set_smem_limit_once(F* func, int bytes, std::atomic<uint64_t>
   return e;
 }
 
+// Resident blocks per SM of `func` (threads, dynamic shared memory) on the
+// current device, queried once per device and kept in `cache` (one slot per
+// device; 0 = not yet known).  Also raises the dynamic shared-memory limit.
+template <typename F>
+inline cudaError_t blocks_per_sm_once(F* func, int threads, int smem, std::atomic<int>* cache,
+                                      int ncache, int* out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < ncache) {
+    const int v = cache[dev].load(std::memory_order_acquire);
+    if (v > 0) {
+      *out = v;
+      return cudaSuccess;
+    }
+  }
+  e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, func, threads, smem);
+  if (e != cudaSuccess) return e;
+  per_sm = per_sm > 0 ? per_sm : 1;
+  if (dev < ncache) cache[dev].store(per_sm, std::memory_order_release);
+  *out = per_sm;
+  return cudaSuccess;
+}
+
 #define MB_REQUIRE(cond, msg)                                                  \
   do {                                                                         \
     if (!(cond)) return ::mb::set_error(MB_ERR_INVALID_ARGUMENT, (msg));       \

@@ -2124,6 +2124,14 @@ __global__ void __launch_bounds__(256, 2)
   const int rp = P256 / ng;  // a power of two, at most 256
   const int64_t row_full_end = a.cl.nfull * kGroup2;
   const int64_t full_rows = row_full_end / ng;  // rows whose scales lie in full 2nd-order chunks
+  // write-out offsets of this thread in a full tile (elements / words from
+  // the tile's first output): packed_2bit row tid/2, half tid%2; packed_4bit
+  // rows tid/4 and tid/4 + 64, quarter tid%4; the per-row arrays row tid
+  const int wo_r2 = tid >> 1, wo_h2 = tid & 1;
+  const int64_t wo_o2 = (int64_t)wo_r2 * ng + 4 * wo_h2;
+  const int wo_r4 = tid >> 2, wo_q4 = tid & 3;
+  const int64_t wo_o4 = 2 * (int64_t)wo_r4 * ng + 4 * wo_q4;
+  const int64_t wo_or = (int64_t)tid * ng;
   bool failed = false;
   uint32_t bad = 0;  // thread 0: stages whose wait ran out
   int cur_ct = -1;
@@ -2149,12 +2157,13 @@ __global__ void __launch_bounds__(256, 2)
     const int nr = (int)min64(kChunkRows, M - row0);
     EncCodes& cb = cbuf[i & 1];
     const int nitems = cx.nitems;
+    int* next_item = &item_next[i & 1];
+    int grab = lane == 0 ? atomicAdd(next_item, 1) : 0;
 #pragma unroll 1
     for (;;) {
-      int j = 0;
-      if (lane == 0) j = atomicAdd(&item_next[i & 1], 1);
-      j = __shfl_sync(0xffffffffu, j, 0);
+      const int j = __shfl_sync(0xffffffffu, grab, 0);
       if (j >= nitems) break;
+      if (lane == 0) grab = atomicAdd(next_item, 1);  // the next item, in flight meanwhile
       const int it = cx.items[j];
       const int gw = it & 7, st = (it >> 3) & 3;
       if (st * 32 >= nr) continue;
@@ -2217,7 +2226,26 @@ __global__ void __launch_bounds__(256, 2)
     }
     const int gb = ct * kTileGroups;
     const int64_t obase = row0 * ng + gb;  // flat index of (row0, gb)
-    if (vec_out && gb + kTileGroups <= ng) {
+    if (vec_out && gb + kTileGroups <= ng && nr == kChunkRows && row0 + kChunkRows <= full_rows) {
+      // a full tile: fixed trip counts, per-thread offsets from the prologue
+      const uint4 x2 = make_uint4(cb.p2[wo_h2 * 4][wo_r2], cb.p2[wo_h2 * 4 + 1][wo_r2],
+                                  cb.p2[wo_h2 * 4 + 2][wo_r2], cb.p2[wo_h2 * 4 + 3][wo_r2]);
+      *reinterpret_cast<uint4*>(a.packed2 + obase + wo_o2) = x2;
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int r = wo_r4 + 64 * k;
+        const uint2 x = cb.p4[2 * wo_q4][r], y = cb.p4[2 * wo_q4 + 1][r];
+        *reinterpret_cast<uint4*>(a.packed4 + 2 * obase + wo_o4 + (int64_t)k * 128 * ng) =
+            make_uint4(x.x, x.y, y.x, y.y);
+      }
+      if (tid < kChunkRows) {
+        const int64_t o = obase + wo_or;
+        *reinterpret_cast<uint4*>(a.scales1 + o) = cx.shv;
+        *reinterpret_cast<uint2*>(a.zeros1 + o) = cx.zv;
+        *reinterpret_cast<uint2*>(a.sq + o) =
+            *reinterpret_cast<const uint2*>(&cx.sqrow[(rc * kChunkRows + tid) & (rp - 1)][0]);
+      }
+    } else if (vec_out && gb + kTileGroups <= ng) {
       for (int k = tid; k < nr * 2; k += blockDim.x) {
         const int r = k >> 1, h = k & 1;
         const uint4 x = make_uint4(cb.p2[4 * h][r], cb.p2[4 * h + 1][r], cb.p2[4 * h + 2][r],
@@ -2484,28 +2512,33 @@ extern "C" mb_status mb_quantize(const void* weights_fp16, int64_t M, int64_t K,
                                                   (uint64_t)K, kChunkRows, 64);
   int dev = 0, sms = 148;
   MB_CUDA_TRY(cudaGetDevice(&dev));
-  MB_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  {
+    static std::atomic<int> sm_cache[64];
+    if (dev < 64 && sm_cache[dev].load(std::memory_order_acquire) > 0) {
+      sms = sm_cache[dev].load(std::memory_order_acquire);
+    } else {
+      MB_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+      if (dev < 64) sm_cache[dev].store(sms, std::memory_order_release);
+    }
+  }
   const int64_t ntiles = nct * nrc;
   // the encode grid (persistent: every CTA resident), known to the selection,
   // which splits the tiles among its CTAs
   int64_t enc_grid = 1;
   {
-    static std::atomic<uint64_t> attr_done{0};
-    MB_CUDA_TRY(set_smem_limit_once(encode_kernel, kEncSmem, attr_done));
-    int per_sm = 0;
-    MB_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, encode_kernel, 256,
-                                                              kEncSmem));
+    static std::atomic<int> occ[64];
+    int per_sm = 1;
+    MB_CUDA_TRY(blocks_per_sm_once(encode_kernel, 256, kEncSmem, occ, 64, &per_sm));
     enc_grid = std::max<int64_t>(
         1, std::min<int64_t>({ntiles, (int64_t)sms * std::max(per_sm, 1), (int64_t)kMaxEncGrid}));
   }
   qa.enc_grid = (int)enc_grid;
   {
     auto kern = sens ? stats_kernel<true> : stats_kernel<false>;
-    static std::atomic<uint64_t> attr_done[2] = {{0}, {0}};
-    MB_CUDA_TRY(set_smem_limit_once(kern, kStatsSmem, attr_done[sens ? 1 : 0]));
-    int per_sm = 0;
-    MB_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kStatsThreads,
-                                                              kStatsSmem));
+    static std::atomic<int> occ[2][64];
+    int per_sm = 1;
+    MB_CUDA_TRY(blocks_per_sm_once(kern, kStatsThreads, kStatsSmem, occ[sens ? 1 : 0], 64,
+                                   &per_sm));
     const int64_t grid =
         std::max<int64_t>(1, std::min<int64_t>(ntiles, (int64_t)sms * std::max(per_sm, 1)));
     kern<<<(unsigned)grid, kStatsThreads, kStatsSmem, stream>>>(tmap, qa, tma ? 1 : 0);
