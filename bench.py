@@ -79,11 +79,8 @@ def barrier(ws):
 def max_over_ranks(ws, x: float) -> float:
     if ws == 1:
         return x
-    import torch
-    import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    from memboost_b200 import shard
+    return shard.max_over_ranks(x)
 
 
 class ClockSampler:
