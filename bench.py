@@ -14,10 +14,10 @@ the data path); rank 0 prints one JSON line.
   e2e        the public memboost_b200.quantize() call per matrix with host
              buffers: pinned H2D copy of the weights and hessian, quantize,
              D2H of every output tensor, inside the timed region
-  roofline   algorithmic bytes of one quantize call (3.0 B per weight plus
-             hessian, 2nd-order, CSR and precision bytes) / its CUDA-event
-             duration on the launching stream, against MEASURED_PEAKS.json;
-             traffic = DRAM bytes per call from the committed ncu summary
+  roofline   algorithmic bytes of a step's quantize calls (3.0 B per weight
+             plus hessian, 2nd-order, CSR and precision bytes) / the device
+             time per step, against MEASURED_PEAKS.json; traffic = DRAM bytes
+             per call from the committed ncu summary
   cpu_baseline  the CPU oracle (C++ restatement of the reference algorithm)
              on all host cores, on the same matrices
 
@@ -32,7 +32,6 @@ import json
 import os
 import statistics
 import sys
-import threading
 import time
 
 import numpy as np
@@ -83,51 +82,89 @@ def max_over_ranks(ws, x: float) -> float:
     return shard.max_over_ranks(x)
 
 
+_SAMPLER = r"""
+import sys, time, pynvml
+pynvml.nvmlInit()
+h = pynvml.nvmlDeviceGetHandleByUUID(sys.argv[1])
+mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+print("ready", flush=True)
+while True:
+    try:
+        t = time.time()
+        sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+        rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+        pw = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
+        print(t, sm, mx, rs, pw, flush=True)
+    except Exception:
+        pass
+    time.sleep(float(sys.argv[2]))
+"""
+
+
 class ClockSampler:
-    """Samples this GPU's SM clock and throttle reasons through NVML every
-    ~2 ms while the timed region runs (read-only queries)."""
+    """Samples this GPU's SM clock, throttle reasons and power through NVML
+    every ~5 ms (read-only queries) from a separate process, and reports the
+    samples taken inside the timed window (``mark_start`` / ``mark_end``;
+    the nearest one if the window is shorter than the period).  NVML queries
+    slow the launching process down measurably at millisecond periods, hence
+    the longer one."""
+
+    PERIOD_S = 0.005
 
     REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
                "sw_power_cap": 0x4}
 
     def __init__(self, device_index: int):
         self.samples = []
-        self._stop = threading.Event()
-        self.handle = None
+        self.proc = None
         try:
-            import pynvml
-            import torch
-            pynvml.nvmlInit()
-            uuid = "GPU-" + str(torch.cuda.get_device_properties(device_index).uuid)
-            self.nvml = pynvml
-            self.handle = pynvml.nvmlDeviceGetHandleByUUID(uuid)
-        except Exception:
-            self.handle = None
+            import subprocess
 
-    def _run(self):
-        nv = self.nvml
-        while not self._stop.is_set():
-            try:
-                sm = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
-                mx = nv.nvmlDeviceGetMaxClockInfo(self.handle, nv.NVML_CLOCK_SM)
-                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
-                pw = nv.nvmlDeviceGetPowerUsage(self.handle) / 1000.0
-                self.samples.append((sm, mx, rs, pw))
-            except Exception:
-                pass
-            time.sleep(0.002)
+            import torch
+            uuid = "GPU-" + str(torch.cuda.get_device_properties(device_index).uuid)
+            self.proc = subprocess.Popen([sys.executable, "-c", _SAMPLER, uuid,
+                                          str(self.PERIOD_S)],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                                         text=True)
+            if self.proc.stdout.readline().strip() != "ready":
+                self.proc.kill()
+                self.proc = None
+        except Exception:
+            self.proc = None
 
     def __enter__(self):
-        if self.handle is not None:
-            self.t = threading.Thread(target=self._run, daemon=True)
-            self.t.start()
-            time.sleep(0.01)
+        self.t_start = self.t_end = time.time()
         return self
 
+    def mark_start(self):
+        self.t_start = time.time()
+
+    def mark_end(self):
+        self.t_end = time.time()
+
     def __exit__(self, *exc):
-        if self.handle is not None:
-            self._stop.set()
-            self.t.join(timeout=2)
+        if self.proc is None:
+            return
+        time.sleep(2 * self.PERIOD_S)  # a sample after the window, for short windows
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        allsamp = []
+        for line in out.splitlines():
+            try:
+                t, sm, mx, rs, pw = line.split()
+                allsamp.append((float(t), int(sm), int(mx), int(rs), float(pw)))
+            except ValueError:
+                pass
+        inside = [x for x in allsamp if self.t_start <= x[0] <= self.t_end]
+        self.in_window = len(inside)
+        if not inside and allsamp:  # window shorter than the period: the nearest sample
+            mid = 0.5 * (self.t_start + self.t_end)
+            inside = [min(allsamp, key=lambda x: abs(x[0] - mid))]
+        self.samples = [x[1:] for x in inside]
 
     def summary(self) -> dict:
         if not self.samples:
@@ -137,7 +174,10 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(s[0] for s in self.samples),
                 "sm_max_mhz": max(s[1] for s in self.samples),
                 "power_w_max": round(max(s[3] for s in self.samples), 1),
-                "samples": len(self.samples), "source": "NVML, 2 ms", "reasons": reasons}
+                "samples": len(self.samples), "samples_in_window": self.in_window,
+                "source": "NVML every ~5 ms from a separate process, samples inside the "
+                          "timed window (else the nearest)",
+                "reasons": reasons}
 
 
 def peaks():
@@ -205,18 +245,22 @@ def run_ours(args, ws, rank, local):
     # two sets of plans: step k + 1 is enqueued before step k is finished
     # (its outlier count read and CSR extracted), so the GPU does not idle
     # while the host works; every step's outputs are complete inside the
-    # timed region
-    plan_sets = [[_C.QuantizePlan(*w.shape, dev) for w in W] for _ in range(2)]
+    # timed region.  The two matrices are independent and run on streams of
+    # their own, so one's latency-bound selection overlaps the other's
+    # streaming kernels.
+    streams = [torch.cuda.Stream(dev) for _ in W]
+    plan_sets = [[_C.QuantizePlan(*w.shape, dev, stream=st) for w, st in zip(W, streams)]
+                 for _ in range(2)]
     fp16_bytes = sum(2 * w.numel() for w in W)
     nnz_seen = []
 
     def launch_step(k, ev=None):
         for i, (p, w, h, c) in enumerate(zip(plan_sets[k % 2], W, H, cases)):
             if ev is not None:
-                ev[i][0].record()
+                p.record_on(ev[i][0])
             p.launch(w, c.ratio_4bit, h)
             if ev is not None:
-                ev[i][1].record()
+                p.record_on(ev[i][1])
 
     def finish_step(k):
         res = [p.finish() for p in plan_sets[k % 2]]
@@ -233,30 +277,43 @@ def run_ours(args, ws, rank, local):
     torch.cuda.synchronize()
     per_call = [[] for _ in W]
     events = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in W]
-              for _ in range(args.steps)]
+              for _ in range(min(args.steps, 5))]
     barrier(ws)
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
+        clk.mark_start()
         t0.record()
-        run_steps(args.steps, events)
+        for st in streams:  # the plans' streams start after t0 ...
+            st.wait_event(t0)
+        run_steps(args.steps)
+        for st in streams:  # ... and t1 follows all of their work
+            torch.cuda.current_stream(dev).wait_stream(st)
         t1.record()
         torch.cuda.synchronize()
+        clk.mark_end()
     barrier(ws)
     ms_local = t0.elapsed_time(t1)
     ms = max_over_ranks(ws, ms_local)
-    for k in range(args.steps):
+    # per-call durations (informational), in an untimed pass of their own:
+    # the events between launches cost host time
+    n_ev = min(args.steps, 5)
+    run_steps(n_ev, events)
+    torch.cuda.synchronize()
+    for k in range(n_ev):
         for i in range(len(W)):
             per_call[i].append(events[k][i][0].elapsed_time(events[k][i][1]))
     value = fp16_bytes * args.steps * ws / (ms / 1e3) / 1e9
 
-    # roofline of the quantize call (all its kernels, one stream)
+    # roofline of the quantize path: the algorithmic bytes of a step's calls
+    # over the device time per step (the two calls overlap on their streams;
+    # call_ms, each call from its first to its last kernel, is informational)
     peak, peak_kind = peaks()
     nnz = nnz_seen[-1]
     alg = [algorithmic_bytes(*w.shape, n, True) for w, n in zip(W, nnz)]
     dur = [statistics.mean(x) for x in per_call]
-    achieved = sum(alg) / (sum(dur) / 1e3) / 1e9
+    achieved = sum(alg) / (ms / args.steps / 1e3) / 1e9
     # stats, assemble, exact (tables), encode, post per matrix; extract when
     # the matrix has outliers
     launches_per_step = sum(5 + (1 if n > 0 else 0) for n in nnz)
@@ -317,9 +374,9 @@ def run_ours(args, ws, rank, local):
                      "peak_kind": peak_kind, "traffic": profiled_traffic(),
                      "traffic_source": "profiles/quantize_mlp7b_launches.md (ncu, one "
                                        "pipelined step, DRAM read+write per call)",
-                     "kernel": "quantize call: stats, assemble (+selection), exact/tables, "
-                               "encode, post -- 5 kernels chained with PDL on one stream, "
-                               "timed together (CUDA events around each call)",
+                     "kernel": "quantize calls of a step: stats, assemble (+selection), "
+                               "exact/tables, encode, post -- 5 kernels chained with PDL per "
+                               "matrix, the two matrices on two streams; device time per step",
                      "algorithmic_bytes_per_call": alg,
                      "call_ms": [round(d, 4) for d in dur]},
         "gpu_launches": launches_per_step * args.steps,

@@ -275,11 +275,17 @@ class QuantizePlan:
     plans before finishing any keeps the GPU busy across matrices.  The
     tensors returned by ``finish`` alias the plan's buffers until the next
     ``launch``.
+
+    ``stream`` (optional): the plan's work runs there instead of on the
+    current stream (after the current stream's work, which produced the
+    inputs); independent matrices on different streams overlap one matrix's
+    latency-bound selection with another's streaming kernels.
     """
 
-    def __init__(self, M: int, K: int, device=None):
+    def __init__(self, M: int, K: int, device=None, stream: torch.cuda.Stream | None = None):
         device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         self.M, self.K, self.device = M, K, device
+        self.stream = stream
         ng = (K + GROUP_SIZE_1ST - 1) // GROUP_SIZE_1ST
         ng2 = (M * ng + GROUP_SIZE_2ND - 1) // GROUP_SIZE_2ND
         e = lambda shape, dt: torch.empty(shape, dtype=dt, device=device)  # noqa: E731
@@ -299,14 +305,19 @@ class QuantizePlan:
         h = hessian_diag if (hessian_diag is not None and hessian_diag.numel() > 0
                              and ratio_4bit > 0) else None
         o = self.out
-        _check(_lib.mb_quantize(
-            _ptr(weights), self.M, self.K, float(ratio_4bit), _ptr(h),
-            0 if h is None else h.numel(), _ptr(o[0]), _ptr(o[1]), _ptr(o[2]), _ptr(o[3]),
-            _ptr(o[4]), _ptr(o[5]), _ptr(o[6]), _ptr(o[7]), _ptr(self.row_ptrs),
-            _ptr(self.ws.nnz), _ptr(self.ws.buf), self.ws.nbytes, _stream(self.device)))
         with torch.cuda.device(self.device):
-            self.nnz_host.copy_(self.ws.nnz, non_blocking=True)
-            self.done.record()
+            if self.stream is not None:
+                self.stream.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(self.stream if self.stream is not None
+                                   else torch.cuda.current_stream(self.device)):
+                _check(_lib.mb_quantize(
+                    _ptr(weights), self.M, self.K, float(ratio_4bit), _ptr(h),
+                    0 if h is None else h.numel(), _ptr(o[0]), _ptr(o[1]), _ptr(o[2]),
+                    _ptr(o[3]), _ptr(o[4]), _ptr(o[5]), _ptr(o[6]), _ptr(o[7]),
+                    _ptr(self.row_ptrs), _ptr(self.ws.nnz), _ptr(self.ws.buf), self.ws.nbytes,
+                    _stream(self.device)))
+                self.nnz_host.copy_(self.ws.nnz, non_blocking=True)
+                self.done.record()
         self._w = weights
 
     def finish(self) -> list:
@@ -320,6 +331,11 @@ class QuantizePlan:
                 _ptr(self._w), self.M, self.K, _ptr(self.row_ptrs), _ptr(vals), _ptr(cols),
                 _ptr(self.ws.buf), self.ws.nbytes, _stream(dev)))
         return [*self.out, vals, cols, self.row_ptrs]
+
+    def record_on(self, event: torch.cuda.Event) -> None:
+        """Record ``event`` on the stream the plan's work runs on."""
+        event.record(self.stream if self.stream is not None
+                     else torch.cuda.current_stream(self.device))
 
 
 # ---- GPTQ calibration (models/llama.py) ----

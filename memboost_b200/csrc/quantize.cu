@@ -1944,13 +1944,16 @@ __device__ __noinline__ void tables_grid(const QArgs& a) {
 // Between the selection and encode: the tables when every precision is
 // known, else the exact sums of the pending groups (whose last warp completes
 // the selection and the tables).
+// Encode is launched only when this kernel is done: its CTAs are large
+// (two fill an SM) and, resident early, would hold the SMs that other work
+// on other streams can use meanwhile.
 __global__ void __launch_bounds__(256) exact_kernel(const QArgs a) {
-  grid_launch_dependents();  // encode may start launching
-  grid_dependency_wait();    // stats, assemble and the selection complete
+  grid_dependency_wait();  // stats, assemble and the selection complete
   if (*reinterpret_cast<const volatile uint32_t*>(&a.ws.hdr->n_pend) == 0)
     tables_grid(a);
   else
     exact_ctas(a);
+  grid_launch_dependents();
 }
 
 // encode: persistent CTAs over the 128 x 128 tiles of W.  CTA b takes a
