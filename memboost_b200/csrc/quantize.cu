@@ -1560,8 +1560,9 @@ template <bool kSens>
 __global__ void __launch_bounds__(kStatsThreads, 2)
     stats_kernel(const __grid_constant__ CUtensorMap tmap, const QArgs A, int use_tma) {
   extern __shared__ uint8_t dsm_raw[];
-  uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) &
-                                            ~(uintptr_t)1023);
+  // 1024-byte aligned for the 128-byte swizzle; offset arithmetic on the
+  // shared array keeps the pointer in the shared space (plain LDS)
+  uint8_t* dsm = dsm_raw + ((1024u - (smem_u32(dsm_raw) & 1023u)) & 1023u);
   __shared__ uint64_t full[kStages];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t M = A.M, K = A.K;
@@ -1624,24 +1625,36 @@ __global__ void __launch_bounds__(kStatsThreads, 2)
       float acc[16];
 #pragma unroll
       for (int c = 0; c < 16; ++c) acc[c] = 0.0f;
+      if (!edge) {  // the whole tile lies inside the matrix (all but the edge tiles)
 #pragma unroll
-      for (int s = 0; s < kSteps; ++s) {
-        const int r = s * 32 + lane;
-        const Row16 v = tile_run(buf, gi, r);
-        const uint32_t vmask = row0 + r < M ? cmask : 0u;
+        for (int s = 0; s < kSteps; ++s) {
+          const Row16 v = tile_run(buf, gi, s * 32 + lane);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const uint32_t w = row_word(v, k);
-          uint32_t wm = w, ws = w;
-          if (edge) {  // outside the matrix: NaN for min / max (ignored), 0 for sums
+          for (int k = 0; k < 8; ++k) {
+            const uint32_t w = row_word(v, k);
+            hmn = __hmin2(hmn, as_h2(w));
+            hmx = __hmax2(hmx, as_h2(w));
+            if (kSens) sq_acc2(w, acc[2 * k], acc[2 * k + 1]);
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int s = 0; s < kSteps; ++s) {
+          const int r = s * 32 + lane;
+          const Row16 v = tile_run(buf, gi, r);
+          const uint32_t vmask = row0 + r < M ? cmask : 0u;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            // outside the matrix: NaN for min / max (ignored), 0 for sums
+            const uint32_t w = row_word(v, k);
             const uint32_t keep = (((vmask >> (2 * k)) & 1u) ? 0x0000FFFFu : 0u) |
                                   (((vmask >> (2 * k + 1)) & 1u) ? 0xFFFF0000u : 0u);
-            ws = w & keep;
-            wm = ws | (0x7E007E00u & ~keep);
+            const uint32_t ws = w & keep;
+            const uint32_t wm = ws | (0x7E007E00u & ~keep);
+            hmn = __hmin2(hmn, as_h2(wm));
+            hmx = __hmax2(hmx, as_h2(wm));
+            if (kSens) sq_acc2(ws, acc[2 * k], acc[2 * k + 1]);
           }
-          hmn = __hmin2(hmn, as_h2(wm));
-          hmx = __hmax2(hmx, as_h2(wm));
-          if (kSens) sq_acc2(ws, acc[2 * k], acc[2 * k + 1]);
         }
       }
       float mn = fminf(__half2float(__low2half(hmn)), __half2float(__high2half(hmn)));
@@ -1700,8 +1713,7 @@ __global__ void __launch_bounds__(kStatsThreads, 2)
 template <bool kSens>
 __global__ void __launch_bounds__(kStatsThreads) assemble_kernel(const QArgs A) {
   extern __shared__ uint8_t dsm_raw[];
-  uint8_t* scratch = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 15) &
-                                                ~(uintptr_t)15);
+  uint8_t* scratch = dsm_raw + ((16u - (smem_u32(dsm_raw) & 15u)) & 15u);
   __shared__ int s_flag;
   grid_launch_dependents();  // exact / encode may start loading W
   grid_dependency_wait();    // the chunk records are complete
@@ -2027,19 +2039,20 @@ __device__ __forceinline__ void enc_build_ctx(const QArgs& a, EncCtx& cx, int ct
   }
   __syncthreads();
   if (warp == 0) {
-    // the item list: irregular groups, then 4-bit (4 items of 32 rows each),
-    // then 2-bit groups (2 items of 64 rows), each kind in group order
+    // the item list, costliest items first: irregular groups (4 items of 32
+    // rows), 2-bit groups (2 items of 64 rows), 4-bit groups (4 items of 32
+    // rows), each kind in group order
     const int kd = lane < kTileGroups ? cx.kind[lane] : kEncKindNone;
     const int n = kd == kEncKind2 ? 2 : kd == kEncKindNone ? 0 : 4;
     const unsigned below = (1u << lane) - 1u;
     int pos = 0;
-    const int order[3] = {kEncKindIrr, kEncKind4, kEncKind2};
+    const int order[3] = {kEncKindIrr, kEncKind2, kEncKind4};
 #pragma unroll
     for (int q = 0; q < 3; ++q) {
       const unsigned m = __ballot_sync(0xffffffffu, kd == order[q]);
       const int per = order[q] == kEncKind2 ? 2 : 4;
       if (kd == order[q]) pos += per * __popc(m & below);
-      else if ((kd == kEncKind4 && q == 0) || (kd == kEncKind2 && q < 2)) pos += per * __popc(m);
+      else if ((kd == kEncKind2 && q == 0) || (kd == kEncKind4 && q < 2)) pos += per * __popc(m);
     }
     for (int k = 0; k < n; ++k)
       cx.items[pos + k] = (uint8_t)(n == 2 ? (lane | ((2 * k) << 3) | (1 << 5)) : (lane | (k << 3)));
@@ -2083,8 +2096,9 @@ __global__ void __launch_bounds__(256, 2)
     encode_kernel(const __grid_constant__ CUtensorMap tmap, const QArgs a, int use_tma,
                   int vec_out) {
   extern __shared__ uint8_t dsm_raw[];
-  uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) &
-                                            ~(uintptr_t)1023);
+  // 1024-byte aligned for the 128-byte swizzle; offset arithmetic on the
+  // shared array keeps the pointer in the shared space (plain LDS)
+  uint8_t* dsm = dsm_raw + ((1024u - (smem_u32(dsm_raw) & 1023u)) & 1023u);
   __shared__ uint64_t full[kEncStages];
   __shared__ EncCtx cx;
   __shared__ EncCodes cbuf[2];
