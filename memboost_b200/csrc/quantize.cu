@@ -1460,18 +1460,25 @@ __device__ __noinline__ void ct_assemble(const QArgs& A, int ct, int warp, int l
 #pragma unroll
     for (int k = 0; k < 16; ++k) rc16[k] = __shfl_sync(0xffffffffu, r, k);
   }
-  for (int j0 = 0; j0 < nrc; j0 += 96) {
-    // up to three chunks per lane in flight
-    float2 mm[3];
-    float4 cc[3][4];
+  // lane l takes the contiguous chunks [l per, (l+1) per): local prefix sums,
+  // then one scan of the lane totals gives every chunk's inclusive prefix;
+  // the moment sum_j terms_j * P_incl(j) = sum_j terms_j * p_j + E * sum_j
+  // terms_j with p_j the local prefix and E the lanes before (any fp64
+  // summation order is covered by the interval's slack)
+  const int per = (nrc + 31) / 32;
+  const int j_begin = min(nrc, lane * per), j_end = min(nrc, j_begin + per);
+  double lsum = 0.0, lmom = 0.0, lterms = 0.0;
+  for (int jb = j_begin; jb < j_end; jb += 2) {
+    float2 mm[2];
+    float4 cc[2][4];
 #pragma unroll
-    for (int u = 0; u < 3; ++u) {
-      const int j = j0 + 32 * u + lane;
+    for (int u = 0; u < 2; ++u) {  // two chunks' records in flight
+      const int j = jb + u;
       const size_t rec = (size_t)g * nrc + j;
       mm[u] = make_float2(INFINITY, -INFINITY);
 #pragma unroll
       for (int q = 0; q < 4; ++q) cc[u][q] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (j < nrc) {
+      if (j < j_end) {
         mm[u] = __ldcg(A.ws.cminmax + rec);
         if (kSens) {
           const float4* src = reinterpret_cast<const float4*>(A.ws.ccol + rec * 16);
@@ -1481,8 +1488,9 @@ __device__ __noinline__ void ct_assemble(const QArgs& A, int ct, int warp, int l
       }
     }
 #pragma unroll
-    for (int u = 0; u < 3; ++u) {
-      const int j = j0 + 32 * u + lane;
+    for (int u = 0; u < 2; ++u) {
+      const int j = jb + u;
+      if (j >= j_end) break;
       mn = fminf(mn, mm[u].x);
       mx = fmaxf(mx, mm[u].y);
       if (kSens) {
@@ -1510,19 +1518,23 @@ __device__ __noinline__ void ct_assemble(const QArgs& A, int ct, int warp, int l
             }
           }
         }
-        if (j < nrc) A.ws.cpred[(size_t)g * nrc + j] = v;
-        double incl = v;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const double y = __shfl_up_sync(0xffffffffu, incl, o);
-          if (lane >= o) incl += y;
-        }
-        const double terms =
-            j < nrc ? 16.0 * (double)min64(kChunkRows, M - (int64_t)j * kChunkRows) : 0.0;
-        mom += terms * (carry + incl);
-        carry += __shfl_sync(0xffffffffu, incl, 31);
+        A.ws.cpred[(size_t)g * nrc + j] = v;
+        const double terms = 16.0 * (double)min64(kChunkRows, M - (int64_t)j * kChunkRows);
+        lsum += v;
+        lmom += terms * lsum;
+        lterms += terms;
       }
     }
+  }
+  if (kSens) {
+    double incl = lsum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    mom = lmom + (incl - lsum) * lterms;
+    carry = __shfl_sync(0xffffffffu, incl, 31);
   }
   mn = warp_min(mn);
   mx = warp_max(mx);
