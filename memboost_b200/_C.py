@@ -268,13 +268,15 @@ class QuantizePlan:
     matrices on one device (whole-model loops, benchmarks).
 
     ``launch`` enqueues phase 1 (every output except the CSR arrays) on the
-    current stream without synchronising, followed by an asynchronous copy of
-    the outlier count into pinned host memory and an event; ``finish`` waits
-    for that event only (work enqueued after this plan's launch keeps
-    running), reads the count and extracts the CSR arrays.  Launching several
-    plans before finishing any keeps the GPU busy across matrices.  The
-    tensors returned by ``finish`` alias the plan's buffers until the next
-    ``launch``.
+    current stream without synchronising, then an event.  The outlier count
+    goes straight to pinned host memory (page-locked memory is addressable
+    from the device under unified addressing, so the kernel writes it there);
+    ``finish`` waits for the event only (work enqueued after this plan's
+    launch keeps running), reads the count and extracts the CSR arrays.
+    Launching several plans before finishing any keeps the GPU busy across
+    matrices.  The tensors returned by ``finish`` alias the plan's buffers
+    until the next ``launch``.  The fixed arguments of the C call are built
+    once, so a launch costs little host time.
 
     ``stream`` (optional): the plan's work runs there instead of on the
     current stream (after the current stream's work, which produced the
@@ -295,8 +297,12 @@ class QuantizePlan:
                     e((M, ng), torch.uint8), e((ng,), torch.uint8)]
         self.row_ptrs = e((M + 1,), torch.int32)
         self.nnz_host = torch.zeros((1,), dtype=torch.int32).pin_memory()
+        self._nnz = self.nnz_host.numpy()
         self.done = torch.cuda.Event()
         self._w = None
+        # outputs, row pointers, count, workspace: fixed for the plan's life
+        self._fixed = (*(_ptr(t) for t in self.out), _ptr(self.row_ptrs), _ptr(self.nnz_host),
+                       _ptr(self.ws.buf), ctypes.c_size_t(self.ws.nbytes))
 
     def launch(self, weights: torch.Tensor, ratio_4bit: float = 0.1,
                hessian_diag: torch.Tensor | None = None) -> None:
@@ -304,32 +310,33 @@ class QuantizePlan:
         assert tuple(weights.shape) == (self.M, self.K) and weights.device == self.device
         h = hessian_diag if (hessian_diag is not None and hessian_diag.numel() > 0
                              and ratio_4bit > 0) else None
-        o = self.out
-        with torch.cuda.device(self.device):
-            if self.stream is not None:
-                self.stream.wait_stream(torch.cuda.current_stream(self.device))
-            with torch.cuda.stream(self.stream if self.stream is not None
-                                   else torch.cuda.current_stream(self.device)):
-                _check(_lib.mb_quantize(
-                    _ptr(weights), self.M, self.K, float(ratio_4bit), _ptr(h),
-                    0 if h is None else h.numel(), _ptr(o[0]), _ptr(o[1]), _ptr(o[2]),
-                    _ptr(o[3]), _ptr(o[4]), _ptr(o[5]), _ptr(o[6]), _ptr(o[7]),
-                    _ptr(self.row_ptrs), _ptr(self.ws.nnz), _ptr(self.ws.buf), self.ws.nbytes,
-                    _stream(self.device)))
-                self.nnz_host.copy_(self.ws.nnz, non_blocking=True)
-                self.done.record()
+        dev = self.device
+        cur = torch.cuda.current_stream(dev)
+        st = cur
+        if self.stream is not None:
+            self.stream.wait_stream(cur)
+            st = self.stream
+        args = (_ptr(weights), self.M, self.K, float(ratio_4bit), _ptr(h),
+                0 if h is None else h.numel(), *self._fixed, ctypes.c_void_p(st.cuda_stream))
+        if torch.cuda.current_device() == dev.index:
+            _check(_lib.mb_quantize(*args))
+        else:
+            with torch.cuda.device(dev):
+                _check(_lib.mb_quantize(*args))
+        self.done.record(st)
         self._w = weights
 
     def finish(self) -> list:
         self.done.synchronize()
-        nnz = int(self.nnz_host[0])
+        nnz = int(self._nnz[0])
         dev = self.device
         vals = torch.empty((nnz,), dtype=torch.float16, device=dev)
         cols = torch.empty((nnz,), dtype=torch.int32, device=dev)
         if nnz > 0:
-            _check(_lib.mb_quantize_extract_outliers(
-                _ptr(self._w), self.M, self.K, _ptr(self.row_ptrs), _ptr(vals), _ptr(cols),
-                _ptr(self.ws.buf), self.ws.nbytes, _stream(dev)))
+            with torch.cuda.device(dev):
+                _check(_lib.mb_quantize_extract_outliers(
+                    _ptr(self._w), self.M, self.K, _ptr(self.row_ptrs), _ptr(vals), _ptr(cols),
+                    _ptr(self.ws.buf), self.ws.nbytes, _stream(dev)))
         return [*self.out, vals, cols, self.row_ptrs]
 
     def record_on(self, event: torch.cuda.Event) -> None:
