@@ -1,7 +1,7 @@
 // memboost quantize on sm_100a.
 //
 // Replaces the reference's six-kernel pipeline with host round trips
-// (core/torch_ops.cu:105-264 driving core/quantize.cu:72-321) by five
+// (core/torch_ops.cu:105-264 driving core/quantize.cu:72-321) by four
 // stream-ordered kernels chained with programmatic dependent launch and no
 // host synchronisation:
 //
@@ -21,9 +21,9 @@
 //            last group completes the selection and the table.
 //   encode   reads W again (mostly from L2) and writes both packed arrays,
 //            scales_1st, zeros_1st and the 2nd-order codes
-//            (quantize.cu:132-242, 274-280), and counts outliers per row.
-//   post     2nd-order scales / zeros and the outlier row pointers
-//            (quantize.cu:245-272, 284-299, torch_ops.cu:210-229).
+//            (quantize.cu:132-242, 274-280), counts outliers per row, and
+//            writes the 2nd-order scales / zeros and the outlier row
+//            pointers (quantize.cu:245-272, 284-299, torch_ops.cu:210-229).
 //   extract  (second entry point) CSR values / columns in ascending column
 //            order (quantize.cu:301-321).
 //
@@ -1980,6 +1980,65 @@ __global__ void __launch_bounds__(256) exact_kernel(const QArgs a) {
   grid_launch_dependents();
 }
 
+// ---------------------------------------------------------------------------
+// post: 2nd-order scales / zeros (quantize.cu:245-272 over the flattened
+// [M, ng] scales) and the outlier row pointers (torch_ops.cu:210-229), done
+// by encode's CTAs.
+// ---------------------------------------------------------------------------
+// 2nd-order scales / zeros, and the row pointers when no group can hold
+// outliers (all CTAs of encode, grid-stride, once the tables are final).
+__device__ __forceinline__ void post_prologue(const QArgs& a) {
+  const int64_t M = a.M;
+  const int64_t gtid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t gthreads = (int64_t)gridDim.x * blockDim.x;
+  const ChunkLayout& cl = a.cl;
+  for (int64_t c = gtid; c < cl.ng2; c += gthreads) {
+    const float4 e = a.ws.chunk_tab[c < cl.nfull ? (int)(c % cl.period) : cl.ntab_full];
+    a.scales2[c] = __ushort_as_half((uint16_t)__float_as_int(e.z));
+    a.zeros2[c] = (int8_t)__float_as_int(e.w);
+  }
+  if (a.ws.hdr->any_irregular == 0) {
+    for (int64_t r = gtid; r <= M; r += gthreads) a.row_ptrs[r] = 0;
+    if (gtid == 0) *a.nnz = 0;
+  }
+}
+
+// When groups may hold outliers: the last encode CTA to finish turns the
+// per-row counts into row pointers (all threads of every CTA call it).
+__device__ __forceinline__ void post_rowptr_scan(const QArgs& a) {
+  if (a.ws.hdr->any_irregular == 0) return;
+  __shared__ int s_last;
+  __shared__ long long part[256];
+  const int tid = threadIdx.x;
+  const int64_t M = a.M;
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = atomicAdd(&a.ws.hdr->ticket_post, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const int nt = blockDim.x;
+  const int64_t per = ceil_div(M, (int64_t)nt);
+  const int64_t q0 = min64(M, tid * per), q1 = min64(M, q0 + per);
+  long long sum = 0;
+  for (int64_t r = q0; r < q1; ++r) sum += __ldcg(a.ws.row_counts + r);
+  part[tid] = sum;
+  __syncthreads();
+  for (int o = 1; o < nt; o <<= 1) {
+    const long long y = tid >= o ? part[tid - o] : 0;
+    __syncthreads();
+    part[tid] += y;
+    __syncthreads();
+  }
+  long long run = part[tid] - sum;
+  if (tid == 0) a.row_ptrs[0] = 0;
+  for (int64_t r = q0; r < q1; ++r) {
+    run += __ldcg(a.ws.row_counts + r);
+    a.row_ptrs[r + 1] = (int32_t)run;
+  }
+  if (tid == nt - 1) *a.nnz = (int32_t)part[tid];
+}
+
 // encode: persistent CTAs over the 128 x 128 tiles of W.  CTA b takes a
 // contiguous range of tiles in column-major order (tile u: column tile
 // u / nrc, row chunk u % nrc), weighted by work when the selection split the
@@ -2141,6 +2200,7 @@ __global__ void __launch_bounds__(256, 2)
   }
   if (tid < 2) item_next[tid] = 0;  // visible after the context's barriers
   grid_dependency_wait();  // the selection, parameters, 2nd-order table and ranges are final
+  post_prologue(a);
   const int64_t S0 = a.ws.enc_start[blockIdx.x], S1 = a.ws.enc_start[blockIdx.x + 1];
   const int64_t ntile_cta = S1 - S0;
   Seq ahead{(int)(S0 / nrc), (int)(S0 % nrc)};  // thread 0: the next tile to load
@@ -2336,61 +2396,9 @@ __global__ void __launch_bounds__(256, 2)
     for (int s = 0; s < kEncStages; ++s)
       if (bad & (1u << s)) (void)mbar_wait(&full[s], 0u), (void)mbar_wait(&full[s], 1u);
   }
+  post_rowptr_scan(a);
 }
 
-// ---------------------------------------------------------------------------
-// post: 2nd-order scales / zeros (quantize.cu:245-272 over the flattened
-// [M, ng] scales) and the outlier row pointers (torch_ops.cu:210-229).
-// ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) post_kernel(const QArgs a) {
-  grid_dependency_wait();  // encode complete
-  const Header* hdr = a.ws.hdr;
-  const int64_t M = a.M;
-  const int tid = threadIdx.x;
-  const int64_t gtid = (int64_t)blockIdx.x * blockDim.x + tid;
-  const int64_t gthreads = (int64_t)gridDim.x * blockDim.x;
-  const ChunkLayout& cl = a.cl;
-  for (int64_t c = gtid; c < cl.ng2; c += gthreads) {
-    const float4 e = a.ws.chunk_tab[c < cl.nfull ? (int)(c % cl.period) : cl.ntab_full];
-    a.scales2[c] = __ushort_as_half((uint16_t)__float_as_int(e.z));
-    a.zeros2[c] = (int8_t)__float_as_int(e.w);
-  }
-  const bool any_irr = hdr->any_irregular != 0;
-  if (!any_irr) {
-    for (int64_t r = gtid; r <= M; r += gthreads) a.row_ptrs[r] = 0;
-    if (gtid == 0) *a.nnz = 0;
-    return;
-  }
-  // the last CTA turns per-row counts into row pointers
-  __shared__ int s_last;
-  __shared__ long long part[256];
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) s_last = atomicAdd(&a.ws.hdr->ticket_post, 1u) == gridDim.x - 1;
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  const int nt = blockDim.x;
-  const int64_t per = ceil_div(M, (int64_t)nt);
-  const int64_t q0 = min64(M, tid * per), q1 = min64(M, q0 + per);
-  long long s = 0;
-  for (int64_t r = q0; r < q1; ++r) s += __ldcg(a.ws.row_counts + r);
-  part[tid] = s;
-  __syncthreads();
-  for (int o = 1; o < nt; o <<= 1) {
-    const long long y = tid >= o ? part[tid - o] : 0;
-    __syncthreads();
-    part[tid] += y;
-    __syncthreads();
-  }
-  long long run = part[tid] - s;
-  if (tid == 0) a.row_ptrs[0] = 0;
-  for (int64_t r = q0; r < q1; ++r) {
-    run += __ldcg(a.ws.row_counts + r);
-    a.row_ptrs[r + 1] = (int32_t)run;
-  }
-  if (tid == nt - 1) *a.nnz = (int32_t)part[tid];
-}
 
 // extract: one warp per row with outliers; only non-regular groups can hold
 // them.  Lanes 0-15 take the group's 16 columns; the ballot order is the
@@ -2593,9 +2601,7 @@ extern "C" mb_status mb_quantize(const void* weights_fp16, int64_t M, int64_t K,
                                   stream, tmap, qa, tma ? 1 : 0, vec_out))
       return st;
   }
-  const int64_t post_grid = std::max<int64_t>(
-      1, std::min<int64_t>(ceil_div(std::max<int64_t>(qa.cl.ng2, M + 1), 256), 2LL * sms));
-  return launch_pdl(post_kernel, dim3((unsigned)post_grid), dim3(256), 0, stream, qa);
+  return MB_OK;
 }
 
 extern "C" mb_status mb_quantize_extract_outliers(const void* weights_fp16, int64_t M, int64_t K,
