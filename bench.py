@@ -334,10 +334,15 @@ def run_ours(args, ws, rank, local):
         d2h_holder = {}
 
         def e2e_step(sync=True):
-            for i, (wh, hhh, c, st) in enumerate(zip(hw, hh, cases, e_streams)):
+            # both uploads first: the link stays busy while quantize() waits
+            # for a matrix's outlier count
+            dev_in = []
+            for wh, hhh, st in zip(hw, hh, e_streams):
                 with torch.cuda.stream(st):
-                    wd = wh.to(dev, non_blocking=True)
-                    hd = hhh.to(dev, non_blocking=True)
+                    dev_in.append((wh.to(dev, non_blocking=True),
+                                   hhh.to(dev, non_blocking=True)))
+            for i, ((wd, hd), c, st) in enumerate(zip(dev_in, cases, e_streams)):
+                with torch.cuda.stream(st):
                     qt = mb.quantize(wd, c.ratio_4bit, hd)
                     for k, v in qt.state_dict().items():
                         if not (isinstance(v, torch.Tensor) and v.is_cuda):
