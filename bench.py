@@ -314,9 +314,9 @@ def run_ours(args, ws, rank, local):
     alg = [algorithmic_bytes(*w.shape, n, True) for w, n in zip(W, nnz)]
     dur = [statistics.mean(x) for x in per_call]
     achieved = sum(alg) / (ms / args.steps / 1e3) / 1e9
-    # stats, assemble, exact (tables), encode per matrix; extract when the
+    # stats (+selection), exact (tables), encode per matrix; extract when the
     # matrix has outliers
-    launches_per_step = sum(4 + (1 if n > 0 else 0) for n in nnz)
+    launches_per_step = sum(3 + (1 if n > 0 else 0) for n in nnz)
 
     # e2e: public API, host buffers, copies in the timed region.  Each matrix
     # has a stream of its own: its upload, quantize() (which reads the
@@ -398,10 +398,10 @@ def run_ours(args, ws, rank, local):
                      "peak_kind": peak_kind, "traffic": profiled_traffic(),
                      "traffic_source": "profiles/quantize_mlp7b_launches.md (ncu, one "
                                        "pipelined step, DRAM read+write per call)",
-                     "kernel": "quantize calls of a step: stats, assemble (+selection), "
-                               "exact/tables, encode (+row pointers) -- 4 kernels chained with "
-                               "PDL per matrix, the two matrices on two streams; device time "
-                               "per step",
+                     "kernel": "quantize calls of a step: stats (+group parameters and "
+                               "selection), exact/tables, encode (+row pointers) -- 3 kernels "
+                               "chained with PDL per matrix, the two matrices on two streams; "
+                               "device time per step",
                      "algorithmic_bytes_per_call": alg,
                      "call_ms": [round(d, 4) for d in dur]},
         "gpu_launches": launches_per_step * args.steps,

@@ -1,25 +1,27 @@
 // memboost quantize on sm_100a.
 //
 // Replaces the reference's six-kernel pipeline with host round trips
-// (core/torch_ops.cu:105-264 driving core/quantize.cu:72-321) by four
+// (core/torch_ops.cu:105-264 driving core/quantize.cu:72-321) by three
 // stream-ordered kernels chained with programmatic dependent launch and no
 // host synchronisation:
 //
-//   stats    streams W from HBM in 128 x 128 tiles through TMA, one warp per
-//            16-column group (quantize.cu:72-128): per (group, 128-row
-//            chunk) min / max and per-column sums of w*w.
-//   assemble one CTA per column tile: each group's min / max, scale / zero /
-//            code thresholds for both precisions (quantize.cu:153-176), and
-//            an fp64 prediction of its serial fp32 sensitivity sum with a
-//            rigorous error interval.  The last CTA selects the 4-bit groups
-//            (torch_ops.cu:149-179): every group whose interval lies clear of
-//            the top-k boundary is decided from the intervals, the few that
-//            straddle it are left pending; when nothing is pending it also
-//            builds the 2nd-order chunk table (quantize.cu:245-272).
-//   exact    only when groups are pending: their exact serial sums
-//            (transfer functions per chunk of rows, assembled in order); the
-//            last group completes the selection and the table.
-//   encode   reads W again (mostly from L2) and writes both packed arrays,
+//   stats    streams W from HBM in 128 x 128 tiles through TMA, each CTA a
+//            contiguous column-major range of tiles, one warp per 16-column
+//            group (quantize.cu:72-128): per-column sums of w*w per 128-row
+//            chunk, and per segment (a CTA's chunks of one column tile)
+//            min / max and an fp64 prediction of the group's serial fp32
+//            sensitivity sum.  The CTA completing a column tile combines its
+//            segments: min / max, scale / zero / code thresholds for both
+//            precisions (quantize.cu:153-176) and a rigorous interval around
+//            each sensitivity.  The CTA completing the last column tile
+//            selects the 4-bit groups (torch_ops.cu:149-179): every group
+//            whose interval lies clear of the top-k boundary is decided, the
+//            few that straddle it are left pending.
+//   exact    the 2nd-order chunk table (quantize.cu:245-272) when nothing
+//            is pending; otherwise the pending groups' exact serial sums
+//            (transfer functions per chunk of rows, assembled in order), the
+//            last of which completes the selection and the table.
+//   encode   reads W again and writes both packed arrays,
 //            scales_1st, zeros_1st and the 2nd-order codes
 //            (quantize.cu:132-242, 274-280), counts outliers per row, and
 //            writes the 2nd-order scales / zeros and the outlier row
@@ -67,6 +69,13 @@ constexpr uint32_t kGrpNaN = 1u, kGrpInf = 2u, kGrpLoose = 4u;  // per-group pre
 constexpr double kEps24 = 5.9604644775390625e-08;  // 2^-24
 constexpr int kExactCtas = 148;                    // CTAs of the exact-sum kernel
 constexpr int kMaxEncGrid = 4096;                  // encode CTAs (persistent grid) at most
+constexpr int kMaxStatsGrid = 4096;                // stats CTAs (persistent grid) at most
+
+// The stats grid never exceeds the tile count or kMaxStatsGrid (the segment
+// records are sized by it).
+__host__ __device__ __forceinline__ int64_t stats_grid_cap(int64_t ntiles) {
+  return ntiles < kMaxStatsGrid ? ntiles : kMaxStatsGrid;
+}
 
 // Outlier-test arithmetic of the reference kernel: the product
 // scale*(q-zero) fused into the subtraction (one rounding).  Established
@@ -124,12 +133,22 @@ ChunkLayout chunk_layout(int64_t M, int64_t ng) {
   return c;
 }
 
+// One stats CTA's share of one group: its consecutive row chunks of the
+// group's column tile (a segment).  sum: prediction of the segment's rows;
+// mom: sum over its chunks of terms * prediction through the chunk (from the
+// segment's first chunk); rows: rows covered; flags: kGrp* bits.
+struct __align__(16) SegRec {
+  double sum, mom;
+  float mn, mx;
+  uint32_t rows, flags;
+};
+static_assert(sizeof(SegRec) == 32, "SegRec must stay 32 bytes");
+
 struct Workspace {
   Header* hdr;
   uint32_t* ct_count;   // [nct] stats tiles finished per column tile (zeroed with hdr)
   float* ccol;          // [ng * nrc * 16] per-column sums of w*w over the chunk
-  double* cpred;        // [ng * nrc] chunk prediction sums (from ccol and 1/h)
-  float2* cminmax;      // [ng * nrc] chunk min / max
+  SegRec* seg;          // [(stats CTAs + nct) * 8]: segment id (CTA + column tile), group
   double* gpred;        // [ng] predicted sensitivity
   double* gmom;         // [ng] sum over chunks of terms * inclusive prediction
   uint32_t* gflag;      // [ng] kGrp* bits
@@ -162,8 +181,7 @@ size_t workspace_layout(int64_t M, int64_t K, char* base, Workspace* ws) {
   const int64_t nct = ceil_div(K, kTileCols), nrc = ceil_div(M, kChunkRows), nrec = ng * nrc;
   char* p_hdr = take(sizeof(Header) + sizeof(uint32_t) * nct);  // zeroed per call
   char* p_cc = take(sizeof(float) * 16 * nrec);
-  char* p_cp = take(sizeof(double) * nrec);
-  char* p_mm = take(sizeof(float2) * nrec);
+  char* p_sg = take(sizeof(SegRec) * kTileGroups * (size_t)(stats_grid_cap(nct * nrc) + nct));
   char* p_gp = take(sizeof(double) * ng);
   char* p_gm = take(sizeof(double) * ng);
   char* p_gf = take(sizeof(uint32_t) * ng);
@@ -186,8 +204,7 @@ size_t workspace_layout(int64_t M, int64_t K, char* base, Workspace* ws) {
     ws->hdr = reinterpret_cast<Header*>(p_hdr);
     ws->ct_count = reinterpret_cast<uint32_t*>(p_hdr + sizeof(Header));
     ws->ccol = reinterpret_cast<float*>(p_cc);
-    ws->cpred = reinterpret_cast<double*>(p_cp);
-    ws->cminmax = reinterpret_cast<float2*>(p_mm);
+    ws->seg = reinterpret_cast<SegRec*>(p_sg);
     ws->gpred = reinterpret_cast<double*>(p_gp);
     ws->gmom = reinterpret_cast<double*>(p_gm);
     ws->gflag = reinterpret_cast<uint32_t*>(p_gf);
@@ -480,6 +497,33 @@ __device__ __forceinline__ bool load_group_div(const float* hess, int64_t c0, in
   const bool any_div = __any_sync(0xffffffffu, div), any_slow = __any_sync(0xffffffffu, slow);
   if (lane == 0) gd->mode = any_slow ? 2 : (any_div ? 1 : 0);
   return !any_slow;
+}
+
+// Prediction of one row chunk of a group from its 16 column sums of w*w and
+// the columns' RN(1/h) (1 where nothing is divided): fp64, the products are
+// exact; non-finite column sums are left out (the group's flags hold them).
+__device__ __forceinline__ double chunk_pred(const float4 (&cc)[4], const float (&rc16)[16]) {
+  double part[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float cv[4] = {cc[q].x, cc[q].y, cc[q].z, cc[q].w};
+    double t = 0.0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) t = fma((double)cv[e], (double)rc16[4 * q + e], t);
+    part[q] = t;
+  }
+  double v = (part[0] + part[1]) + (part[2] + part[3]);
+  if (!isfinite(v)) {
+    v = 0.0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float cv[4] = {cc[q].x, cc[q].y, cc[q].z, cc[q].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (isfinite(cv[e])) v += (double)cv[e] * (double)rc16[4 * q + e];
+    }
+  }
+  return v;
 }
 
 // w*w of a run's 16 fp16 values; `valid` bit i clear -> 0
@@ -924,9 +968,18 @@ __device__ __noinline__ void exact_chunk(const QArgs& A, const GroupDiv& gd, int
   const bool vec = A.w_aligned && gs == kGroup1 && (A.K & 7) == 0;
   const uint32_t cmask = gs >= 16 ? 0xFFFFu : ((1u << gs) - 1u);
   const size_t rec = (size_t)g * A.nrc + rc;
-  // predicted prefix before the chunk
+  // predicted prefix before the chunk, from the column sums of the chunks
+  float rc16[16];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) f2_unpack(gd.R2[k], rc16[2 * k], rc16[2 * k + 1]);
   double pstart = 0.0;
-  for (int j = lane; j < rc; j += 32) pstart += __ldcg(A.ws.cpred + (size_t)g * A.nrc + j);
+  for (int j = lane; j < rc; j += 32) {
+    const float4* src = reinterpret_cast<const float4*>(A.ws.ccol + ((size_t)g * A.nrc + j) * 16);
+    float4 cc[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) cc[q] = __ldcg(src + q);
+    pstart += chunk_pred(cc, rc16);
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) pstart += __shfl_xor_sync(0xffffffffu, pstart, o);
   const int64_t row0 = (int64_t)rc * kChunkRows;
@@ -1404,9 +1457,9 @@ __device__ void select_from_intervals(const QArgs& a, uint8_t* scratch, size_t s
 }
 
 // ---------------------------------------------------------------------------
-// stats kernel: persistent CTAs over the 128 x 128 tiles (row chunks of a
-// column tile are consecutive tile indices), two tile buffers so the next
-// tile's TMA load overlaps the current tile's work, one warp per group.
+// stats kernel: persistent CTAs, each over a contiguous column-major range of
+// the 128 x 128 tiles, a three-stage TMA ring so the next tiles' loads
+// overlap the current tile's work, one warp per group.
 // ---------------------------------------------------------------------------
 
 // w*w of the two fp16 values of `w`, accumulated into a0 / a1 in fp32 (the
@@ -1433,108 +1486,67 @@ __device__ __forceinline__ void tile_fill(const __half* W, int64_t M, int64_t K,
   }
 }
 
-// The last CTA of a column tile: totals, flags, min / max and parameters of
-// its groups (one warp per group).
+// Tile u of the stats pass is (column tile u / nrc, row chunk u % nrc); stats
+// CTA b takes the tiles [U_b, U_b+1), U_b = floor(b * ntiles / G), G <= ntiles
+// (so no range is empty).  A CTA's tiles of one column tile form a segment,
+// identified by b + ct (both grow along u, so the ids are distinct).
+// floor(x / d) for 0 <= x < 2^53 and d > 0 without a 64-bit division.
+__device__ __forceinline__ int64_t floor_div_small(int64_t x, int64_t d) {
+  int64_t q = (int64_t)((double)x / (double)d);
+  if (q * d > x)
+    --q;
+  else if ((q + 1) * d <= x)
+    ++q;
+  return q;
+}
+__device__ __forceinline__ int stats_start(int b, int ntiles, int G) {
+  return (int)floor_div_small((int64_t)b * ntiles, G);
+}
+
+// The last CTA to finish column tile ct: each group's totals from its
+// segments (one warp per group, lanes over the segments in row order), its
+// flags, min / max, sensitivity interval and the parameters of both
+// precisions.  The prediction P is the sum of the segments' sums; the moment
+// sum_j terms_j * P_incl(j) adds, per segment, its own moment and
+// (prediction before the segment) * (its terms); any fp64 summation order is
+// covered by the interval's slack.
 template <bool kSens>
-__device__ __noinline__ void ct_assemble(const QArgs& A, int ct, int warp, int lane) {
-  const int64_t M = A.M;
-  const int nrc = A.nrc;
+__device__ __noinline__ void ct_combine(const QArgs& A, int ct, int warp, int lane) {
   const int64_t g = (int64_t)ct * kTileGroups + warp;
   if (g >= A.ng) return;
+  const int64_t M = A.M;
+  const int nrc = A.nrc, G = (int)gridDim.x, ntiles = A.nct * A.nrc;
+  const int64_t u0 = (int64_t)ct * nrc, u1 = u0 + nrc;
+  // the CTAs holding the column tile's first and last chunk
+  const int b0 = (int)floor_div_small((u0 + 1) * G - 1, ntiles);
+  const int b1 = (int)floor_div_small(u1 * G - 1, ntiles);
   float mn = INFINITY, mx = -INFINITY;
-  bool any_nan = false, any_inf = false, loose = false;
+  uint32_t flags = 0;
   double carry = 0.0, mom = 0.0;
-  // RN(1/h) of the group's 16 columns (1 where the reference does not
-  // divide): lane c computes column c, then every lane holds all 16
-  float rc16[16];
-  if (kSens) {
-    const int64_t c = g * kGroup1 + (lane & 15);
-    float r = 1.0f;
-    if (c < A.K) {
-      const float h = __ldg(A.hess + c);
-      if (h > 1e-8f) {
-        r = __frcp_rn(h);
-        loose = !(h >= 0x1p-60f && h <= 0x1p60f);
+  for (int bb = b0; bb <= b1; bb += 32) {
+    const int b = bb + lane;
+    double sum = 0.0, smom = 0.0;
+    uint4 w = make_uint4(__float_as_uint(INFINITY), __float_as_uint(-INFINITY), 0u, 0u);
+    if (b <= b1) {
+      const SegRec* src = A.ws.seg + ((size_t)(b + ct) * kTileGroups + warp);
+      const double2 d = __ldcg(reinterpret_cast<const double2*>(src));
+      w = __ldcg(reinterpret_cast<const uint4*>(src) + 1);
+      sum = d.x;
+      smom = d.y;
+    }
+    mn = fminf(mn, __uint_as_float(w.x));
+    mx = fmaxf(mx, __uint_as_float(w.y));
+    flags |= w.w;
+    if (kSens) {
+      double incl = sum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const double y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
       }
+      mom += smom + (carry + (incl - sum)) * (16.0 * (double)w.z);
+      carry += __shfl_sync(0xffffffffu, incl, 31);
     }
-#pragma unroll
-    for (int k = 0; k < 16; ++k) rc16[k] = __shfl_sync(0xffffffffu, r, k);
-  }
-  // lane l takes the contiguous chunks [l per, (l+1) per): local prefix sums,
-  // then one scan of the lane totals gives every chunk's inclusive prefix;
-  // the moment sum_j terms_j * P_incl(j) = sum_j terms_j * p_j + E * sum_j
-  // terms_j with p_j the local prefix and E the lanes before (any fp64
-  // summation order is covered by the interval's slack)
-  const int per = (nrc + 31) / 32;
-  const int j_begin = min(nrc, lane * per), j_end = min(nrc, j_begin + per);
-  double lsum = 0.0, lmom = 0.0, lterms = 0.0;
-  for (int jb = j_begin; jb < j_end; jb += 2) {
-    float2 mm[2];
-    float4 cc[2][4];
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {  // two chunks' records in flight
-      const int j = jb + u;
-      const size_t rec = (size_t)g * nrc + j;
-      mm[u] = make_float2(INFINITY, -INFINITY);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) cc[u][q] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (j < j_end) {
-        mm[u] = __ldcg(A.ws.cminmax + rec);
-        if (kSens) {
-          const float4* src = reinterpret_cast<const float4*>(A.ws.ccol + rec * 16);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) cc[u][q] = __ldcg(src + q);
-        }
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int j = jb + u;
-      if (j >= j_end) break;
-      mn = fminf(mn, mm[u].x);
-      mx = fmaxf(mx, mm[u].y);
-      if (kSens) {
-        // products are exact in fp64; four partial sums shorten the chain
-        double part[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float cv[4] = {cc[u][q].x, cc[u][q].y, cc[u][q].z, cc[u][q].w};
-          double t = 0.0;
-#pragma unroll
-          for (int e = 0; e < 4; ++e) t = fma((double)cv[e], (double)rc16[4 * q + e], t);
-          part[q] = t;
-        }
-        double v = (part[0] + part[1]) + (part[2] + part[3]);
-        if (!isfinite(v)) {  // a NaN / inf column sum: flag it, sum the finite ones
-          v = 0.0;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float cv[4] = {cc[u][q].x, cc[u][q].y, cc[u][q].z, cc[u][q].w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              any_nan |= isnan(cv[e]);
-              any_inf |= isinf(cv[e]);
-              if (isfinite(cv[e])) v += (double)cv[e] * (double)rc16[4 * q + e];
-            }
-          }
-        }
-        A.ws.cpred[(size_t)g * nrc + j] = v;
-        const double terms = 16.0 * (double)min64(kChunkRows, M - (int64_t)j * kChunkRows);
-        lsum += v;
-        lmom += terms * lsum;
-        lterms += terms;
-      }
-    }
-  }
-  if (kSens) {
-    double incl = lsum;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const double y = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += y;
-    }
-    mom = lmom + (incl - lsum) * lterms;
-    carry = __shfl_sync(0xffffffffu, incl, 31);
   }
   mn = warp_min(mn);
   mx = warp_max(mx);
@@ -1544,9 +1556,7 @@ __device__ __noinline__ void ct_assemble(const QArgs& A, int ct, int warp, int l
   if (kSens) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mom += __shfl_xor_sync(0xffffffffu, mom, o);
-    const uint32_t flags = (__any_sync(0xffffffffu, any_nan) ? kGrpNaN : 0u) |
-                           (__any_sync(0xffffffffu, any_inf) ? kGrpInf : 0u) |
-                           (__any_sync(0xffffffffu, loose) ? kGrpLoose : 0u);
+    flags = __reduce_or_sync(0xffffffffu, flags);
     if (lane == 0) {
       A.ws.gpred[g] = carry;
       A.ws.gmom[g] = mom;
@@ -1561,38 +1571,37 @@ __device__ __noinline__ void ct_assemble(const QArgs& A, int ct, int warp, int l
   group_params_warp(A.ws.params, A.ws.gscale, A.ws.greg, g, mn, mx, lane);
 }
 
-__device__ __noinline__ void select_all(const QArgs& A, uint8_t* scratch) {
-  select_from_intervals<kStatsThreads>(A, scratch, kTileBytes);
+__device__ __noinline__ void select_all(const QArgs& A, uint8_t* scratch, size_t bytes) {
+  select_from_intervals<kStatsThreads>(A, scratch, bytes);
 }
 
-// stats: persistent CTAs streaming the tiles, one warp per group of the
-// current tile: per (group, row chunk) min / max and the per-column sums of
-// w*w (the sensitivity prediction before the division by h).
+// stats: persistent CTAs, each streaming its contiguous range of tiles
+// (column-major) through a TMA ring, one warp per group of the current tile.
+// Per tile: the per-column sums of w*w (kept for the exact sums of pending
+// groups); per segment, in registers: min / max and the prediction sums
+// (lane = column: RN(1/h) * column sum, in fp64).  At a segment's end its
+// record is written; the CTA completing a column tile combines its groups,
+// and the CTA completing the last column tile selects the 4-bit groups
+// (torch_ops.cu:149-179) and splits the encode tiles.
 template <bool kSens>
 __global__ void __launch_bounds__(kStatsThreads, 2)
-    stats_kernel(const __grid_constant__ CUtensorMap tmap, const QArgs A, int use_tma) {
+    stats_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ QArgs A,
+                 int use_tma) {
   extern __shared__ uint8_t dsm_raw[];
   // 1024-byte aligned for the 128-byte swizzle; offset arithmetic on the
   // shared array keeps the pointer in the shared space (plain LDS)
   uint8_t* dsm = dsm_raw + ((1024u - (smem_u32(dsm_raw) & 1023u)) & 1023u);
   __shared__ uint64_t full[kStages];
+  __shared__ int s_flag, s_select;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t M = A.M, K = A.K;
   const int nrc = A.nrc, nct = A.nct;
   const int ntiles = nct * nrc;  // below 2^31 (checked on the host)
   const int G = (int)gridDim.x;
-  // tile t = rc * nct + ct; t advances by G: (rc, ct) by (G / nct, G % nct)
-  const int drc = G / nct, dct = G - drc * nct;
-  auto advance = [&](int& rc, int& ct) {
-    rc += drc;
-    ct += dct;
-    if (ct >= nct) {
-      ct -= nct;
-      ++rc;
-    }
-  };
-  int t_ahead = (int)blockIdx.x;  // thread 0: the next tile to load
-  int rc_ahead = t_ahead / nct, ct_ahead = t_ahead - rc_ahead * nct;
+  const int u_begin = stats_start((int)blockIdx.x, ntiles, G);
+  const int u_end = stats_start((int)blockIdx.x + 1, ntiles, G);
+  int u_ahead = u_begin;  // thread 0: the next tile to load
+  int ct_ahead = u_begin / nrc, rc_ahead = u_begin - ct_ahead * nrc;
   auto issue = [&](int s) {
     uint8_t* dst = dsm + (size_t)s * kTileBytes;
     fence_proxy_async_smem();
@@ -1600,32 +1609,69 @@ __global__ void __launch_bounds__(kStatsThreads, 2)
     tma_load_2d(dst, &tmap, &full[s], ct_ahead * kTileCols, rc_ahead * kChunkRows);
     tma_load_2d(dst + kBoxBytes, &tmap, &full[s], ct_ahead * kTileCols + 64,
                 rc_ahead * kChunkRows);
-    t_ahead += G;
-    advance(rc_ahead, ct_ahead);
+    ++u_ahead;
+    if (++rc_ahead == nrc) {
+      rc_ahead = 0;
+      ++ct_ahead;
+    }
   };
+  if (tid == 0) s_select = 0;
   if (tid == 0 && use_tma) {
     for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
     fence_mbar_init();
-    for (int s = 0; s < kStages && t_ahead < ntiles; ++s) issue(s);
+    for (int s = 0; s < kStages && u_ahead < u_end; ++s) issue(s);
   }
   __syncthreads();
   bool failed = false;
   uint32_t bad = 0;  // thread 0: stages whose wait ran out
   int st = 0;
   uint32_t ph = 0;  // phase parity of stage st
-  int rc = (int)blockIdx.x / nct, ct = (int)blockIdx.x - rc * nct;
-  for (int t = (int)blockIdx.x; t < ntiles; t += G, advance(rc, ct)) {
+  // the open segment of this warp's group: min / max, and per lane the
+  // prediction sum and moment of its column (even lanes; odd lanes hold 0)
+  __half2 smn = __float2half2_rn(INFINITY), smx = __float2half2_rn(-INFINITY);
+  double ssum = 0.0, smom = 0.0, rcl = 0.0;
+  bool snan = false, sinf = false, sloose = false;
+  uint32_t srows = 0;
+  int seg_rc0 = 0;
+  // lane l ends the column-sum butterfly with column 8 b4 + 4 b3 + 2 b2 + b1
+  const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4, b1 = lane & 2;
+  const int col = (b4 ? 8 : 0) + (b3 ? 4 : 0) + (b2 ? 2 : 0) + (b1 ? 1 : 0);
+  const bool even = !(lane & 1);
+  int ct = u_begin / nrc, rc = u_begin - ct * nrc;
+  for (int u = u_begin; u < u_end; ++u) {
     uint8_t* buf = dsm + (size_t)st * kTileBytes;
     const int64_t row0 = (int64_t)rc * kChunkRows;
     const int gi = warp;
     const int64_t g = (int64_t)ct * kTileGroups + gi;
     const int64_t c0 = g * kGroup1;
+    const bool seg_first = u == u_begin || rc == 0;
+    const bool seg_last = u == u_end - 1 || rc == nrc - 1;
+    const int rows = (int)min64(kChunkRows, M - row0);
+    if (seg_first) {
+      smn = __float2half2_rn(INFINITY);
+      smx = __float2half2_rn(-INFINITY);
+      ssum = smom = 0.0;
+      snan = sinf = sloose = false;
+      srows = 0;
+      seg_rc0 = rc;
+      if (kSens) {
+        float r = 1.0f;
+        if (g < A.ng && c0 + col < K) {
+          const float h = __ldg(A.hess + c0 + col);
+          if (h > 1e-8f) {
+            r = __frcp_rn(h);
+            sloose = !(h >= 0x1p-60f && h <= 0x1p60f);
+          }
+        }
+        rcl = even ? (double)r : 0.0;
+      }
+    }
     if (use_tma) {
       const bool ok = mbar_wait(&full[st], ph);
       failed |= !ok;
       if (tid == 0 && !ok) bad |= 1u << st;
     } else {
-      tile_fill(A.W, M, K, buf, t, nct, 0x7E00);
+      tile_fill(A.W, M, K, buf, (int64_t)rc * nct + ct, nct, 0x7E00);
       __syncthreads();
     }
     if (g < A.ng) {
@@ -1633,7 +1679,7 @@ __global__ void __launch_bounds__(kStatsThreads, 2)
       const uint32_t cmask = gs >= 16 ? 0xFFFFu : ((1u << gs) - 1u);
       const bool edge = (row0 + kChunkRows > M) || gs < kGroup1;
       const size_t rec = (size_t)g * nrc + rc;
-      __half2 hmn = __float2half2_rn(INFINITY), hmx = __float2half2_rn(-INFINITY);
+      __half2 hmn = smn, hmx = smx;
       float acc[16];
 #pragma unroll
       for (int c = 0; c < 16; ++c) acc[c] = 0.0f;
@@ -1669,17 +1715,13 @@ __global__ void __launch_bounds__(kStatsThreads, 2)
           }
         }
       }
-      float mn = fminf(__half2float(__low2half(hmn)), __half2float(__high2half(hmn)));
-      float mx = fmaxf(__half2float(__low2half(hmx)), __half2float(__high2half(hmx)));
-      mn = warp_min(mn);
-      mx = warp_max(mx);
-      if (lane == 0) A.ws.cminmax[rec] = make_float2(mn, mx);
+      smn = hmn;
+      smx = hmx;
+      srows += (uint32_t)rows;
       if (kSens) {
         // per-column sums over the chunk's rows by a transposing butterfly:
-        // each step halves the columns a lane holds; lane l ends with column
-        // 8 b4 + 4 b3 + 2 b2 + b1 (bits of l)
+        // each step halves the columns a lane holds
         float a8[8], a4[4], a2[2];
-        const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4, b1 = lane & 2;
 #pragma unroll
         for (int j = 0; j < 8; ++j)
           a8[j] = __fadd_rn(b4 ? acc[8 + j] : acc[j],
@@ -1694,19 +1736,67 @@ __global__ void __launch_bounds__(kStatsThreads, 2)
                             __shfl_xor_sync(0xffffffffu, b2 ? a4[j] : a4[2 + j], 4));
         float a1 = __fadd_rn(b1 ? a2[1] : a2[0], __shfl_xor_sync(0xffffffffu, b1 ? a2[0] : a2[1], 2));
         a1 = __fadd_rn(a1, __shfl_xor_sync(0xffffffffu, a1, 1));
-        const int col = (b4 ? 8 : 0) + (b3 ? 4 : 0) + (b2 ? 2 : 0) + (b1 ? 1 : 0);
-        if (!(lane & 1)) A.ws.ccol[rec * 16 + col] = a1;
+        if (even) A.ws.ccol[rec * 16 + col] = a1;
+        // the chunk's prediction, lane by lane (exact products); a NaN / inf
+        // column sum is flagged and left out
+        snan |= isnan(a1);
+        sinf |= isinf(a1);
+        ssum += isfinite(a1) ? (double)a1 * rcl : 0.0;
+        smom = fma(16.0 * (double)rows, ssum, smom);
+      }
+      if (seg_last) {
+        float mn = fminf(__half2float(__low2half(smn)), __half2float(__high2half(smn)));
+        float mx = fmaxf(__half2float(__low2half(smx)), __half2float(__high2half(smx)));
+        mn = warp_min(mn);
+        mx = warp_max(mx);
+        double sum = ssum, mom = smom;
+        uint32_t flags = 0;
+        if (kSens) {
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            mom += __shfl_xor_sync(0xffffffffu, mom, o);
+          }
+          flags = (__any_sync(0xffffffffu, snan) ? kGrpNaN : 0u) |
+                  (__any_sync(0xffffffffu, sinf) ? kGrpInf : 0u) |
+                  (__any_sync(0xffffffffu, sloose) ? kGrpLoose : 0u);
+        }
+        if (lane == 0) {
+          SegRec* dst = A.ws.seg + ((size_t)(blockIdx.x + ct) * kTileGroups + gi);
+          reinterpret_cast<double2*>(dst)[0] = make_double2(sum, mom);
+          reinterpret_cast<uint4*>(dst)[1] =
+              make_uint4(__float_as_uint(mn), __float_as_uint(mx), srows, flags);
+        }
       }
     }
     // zero this tile's share of the per-row outlier counts
     if (ct == 0)
       for (int r = tid; r < kChunkRows; r += kStatsThreads)
         if (row0 + r < M) A.ws.row_counts[row0 + r] = 0;
+    if (seg_last) __threadfence();
     __syncthreads();  // the stage is free
-    if (tid == 0 && use_tma && t_ahead < ntiles) issue(st);
+    if (tid == 0 && use_tma && u_ahead < u_end) issue(st);
     if (++st == kStages) {
       st = 0;
       ph ^= 1u;
+    }
+    if (seg_last) {
+      // the column tile's chunks done so far; the CTA completing it combines
+      const uint32_t len = (uint32_t)(rc - seg_rc0 + 1);
+      if (tid == 0) s_flag = atomicAdd(&A.ws.ct_count[ct], len) + len == (uint32_t)nrc;
+      __syncthreads();
+      if (s_flag) {
+        __threadfence();
+        ct_combine<kSens>(A, ct, warp, lane);
+        __threadfence();
+        __syncthreads();
+        // the last column tile can only complete at this CTA's last tile
+        if (tid == 0) s_select = atomicAdd(&A.ws.hdr->ticket_ct, 1u) == (uint32_t)nct - 1u;
+      }
+    }
+    if (++rc == nrc) {
+      rc = 0;
+      ++ct;
     }
   }
   grid_launch_dependents();
@@ -1714,30 +1804,15 @@ __global__ void __launch_bounds__(kStatsThreads, 2)
   if (tid == 0) {
     if (failed) atomicOr(&A.ws.hdr->status, kStatusTimeout);
     // loads whose wait ran out may still be in flight: let them land (the
-    // stage's last issued phase, bounded)
+    // stage's last issued phase, bounded) before the ring is reused
     for (int s = 0; s < kStages; ++s)
       if (bad & (1u << s)) (void)mbar_wait(&full[s], 0u), (void)mbar_wait(&full[s], 1u);
   }
-}
-
-// assemble: one CTA per column tile, one warp per group: totals, flags,
-// min / max and parameters from the chunk records; the last CTA selects.
-template <bool kSens>
-__global__ void __launch_bounds__(kStatsThreads) assemble_kernel(const QArgs A) {
-  extern __shared__ uint8_t dsm_raw[];
-  uint8_t* scratch = dsm_raw + ((16u - (smem_u32(dsm_raw) & 15u)) & 15u);
-  __shared__ int s_flag;
-  grid_launch_dependents();  // exact / encode may start loading W
-  grid_dependency_wait();    // the chunk records are complete
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  ct_assemble<kSens>(A, blockIdx.x, warp, lane);
-  __threadfence();
   __syncthreads();
-  if (tid == 0) s_flag = atomicAdd(&A.ws.hdr->ticket_ct, 1u) == gridDim.x - 1u;
-  __syncthreads();
-  if (!s_flag) return;
-  __threadfence();
-  select_all(A, scratch);
+  if (s_select) {
+    __threadfence();
+    select_all(A, dsm, (size_t)kStages * kTileBytes);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -1971,8 +2046,8 @@ __device__ __noinline__ void tables_grid(const QArgs& a) {
 // Encode is launched only when this kernel is done: its CTAs are large
 // (two fill an SM) and, resident early, would hold the SMs that other work
 // on other streams can use meanwhile.
-__global__ void __launch_bounds__(256) exact_kernel(const QArgs a) {
-  grid_dependency_wait();  // stats, assemble and the selection complete
+__global__ void __launch_bounds__(256) exact_kernel(const __grid_constant__ QArgs a) {
+  grid_dependency_wait();  // stats and the selection complete
   if (*reinterpret_cast<const volatile uint32_t*>(&a.ws.hdr->n_pend) == 0)
     tables_grid(a);
   else
@@ -2201,7 +2276,10 @@ __global__ void __launch_bounds__(256, 2)
   if (tid < 2) item_next[tid] = 0;  // visible after the context's barriers
   grid_dependency_wait();  // the selection, parameters, 2nd-order table and ranges are final
   post_prologue(a);
-  const int64_t S0 = a.ws.enc_start[blockIdx.x], S1 = a.ws.enc_start[blockIdx.x + 1];
+  // the tile range, clamped into the matrix whatever the split wrote
+  const int64_t ntiles_all = (int64_t)a.nct * nrc;
+  const int64_t S0 = max64(0, min64(ntiles_all, a.ws.enc_start[blockIdx.x]));
+  const int64_t S1 = max64(S0, min64(ntiles_all, a.ws.enc_start[blockIdx.x + 1]));
   const int64_t ntile_cta = S1 - S0;
   Seq ahead{(int)(S0 / nrc), (int)(S0 % nrc)};  // thread 0: the next tile to load
   if (tid == 0 && use_tma)
@@ -2576,18 +2654,11 @@ extern "C" mb_status mb_quantize(const void* weights_fp16, int64_t M, int64_t K,
     int per_sm = 1;
     MB_CUDA_TRY(blocks_per_sm_once(kern, kStatsThreads, kStatsSmem, occ[sens ? 1 : 0], 64,
                                    &per_sm));
-    const int64_t grid =
-        std::max<int64_t>(1, std::min<int64_t>(ntiles, (int64_t)sms * std::max(per_sm, 1)));
+    // at most one CTA per tile (no empty tile range) and the records' cap
+    const int64_t grid = std::max<int64_t>(
+        1, std::min<int64_t>(stats_grid_cap(ntiles), (int64_t)sms * std::max(per_sm, 1)));
     kern<<<(unsigned)grid, kStatsThreads, kStatsSmem, stream>>>(tmap, qa, tma ? 1 : 0);
     MB_LAUNCH_CHECK("stats_kernel");
-  }
-  {
-    auto kern = sens ? assemble_kernel<true> : assemble_kernel<false>;
-    static std::atomic<uint64_t> attr_done[2] = {{0}, {0}};
-    MB_CUDA_TRY(set_smem_limit_once(kern, kTileBytes + 16, attr_done[sens ? 1 : 0]));
-    if (mb_status st = launch_pdl(kern, dim3((unsigned)nct), dim3(kStatsThreads),
-                                  (size_t)kTileBytes + 16, stream, qa))
-      return st;
   }
   if (mb_status st = launch_pdl(exact_kernel, dim3(kExactCtas), dim3(256), 0, stream, qa))
     return st;
