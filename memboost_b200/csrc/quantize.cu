@@ -69,7 +69,7 @@ constexpr uint32_t kGrpNaN = 1u, kGrpInf = 2u, kGrpLoose = 4u;  // per-group pre
 constexpr double kEps24 = 5.9604644775390625e-08;  // 2^-24
 constexpr int kExactCtas = 148;                    // CTAs of the exact-sum kernel
 constexpr int kMaxEncGrid = 4096;                  // encode CTAs (persistent grid) at most
-constexpr int kMaxStatsGrid = 4096;                // stats CTAs (persistent grid) at most
+constexpr int kMaxStatsGrid = 1024;                // stats CTAs (persistent grid) at most
 
 // The stats grid never exceeds the tile count or kMaxStatsGrid (the segment
 // records are sized by it).
@@ -1149,6 +1149,63 @@ __device__ void kth_largest2(int n, int ka, KeyA a, int kb, KeyB b, uint32_t* hi
   sync_nt<NT>();
 }
 
+// hist[bin] += 1 for the lanes with `on`: the first active lane's bin takes
+// one shared-memory atomic for all lanes sharing it (in the early passes
+// nearly every key falls in one bin), the other lanes add one each.
+__device__ __forceinline__ void hist_add_lead(uint32_t* hist, uint32_t bin, bool on, int lane) {
+  const unsigned act = __ballot_sync(0xffffffffu, on);
+  if (act == 0u) return;
+  const int leader = __ffs(act) - 1;
+  const uint32_t lb = __shfl_sync(0xffffffffu, bin, leader);
+  const unsigned same = __ballot_sync(0xffffffffu, on && bin == lb);
+  if (lane == leader) atomicAdd(&hist[lb], (uint32_t)__popc(same));
+  if (on && bin != lb) atomicAdd(&hist[bin], 1u);
+}
+
+// kth_largest2 over keys held in registers: thread tid holds keys
+// tid + i NT (i < KPT) of both sets; n <= KPT NT.  The histograms are double
+// buffered (hist: 1024 words), so a pass takes two block barriers: count
+// (and zero the next pass's histograms), then pick.  s4 keeps the results.
+template <int NT, int KPT>
+__device__ void kth_largest2_reg(const uint32_t (&x)[KPT], const uint32_t (&y)[KPT], int n,
+                                 int ka, int kb, uint32_t* hist, uint32_t* s4, uint32_t& Ta,
+                                 uint32_t& Tb) {
+  const int tid = threadIdx.x % NT, lane = threadIdx.x & 31, warp = tid >> 5;
+  for (int i = tid; i < 512; i += NT) hist[i] = 0;
+  if (tid == 0) {
+    s4[0] = 0;
+    s4[1] = (uint32_t)ka;
+    s4[2] = 0;
+    s4[3] = (uint32_t)kb;
+  }
+  sync_nt<NT>();
+  uint32_t mask = 0;
+  int cur = 0;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    uint32_t* h = hist + cur * 512;
+    uint32_t* hn = hist + (cur ^ 1) * 512;
+    const uint32_t pa = s4[0], pb = s4[2];
+#pragma unroll
+    for (int i = 0; i < KPT; ++i) {
+      if (i * NT < n) {  // uniform: whole warps take part
+        const bool v = tid + i * NT < n;
+        hist_add_lead(h, (x[i] >> shift) & 255u, v && (x[i] & mask) == pa, lane);
+        hist_add_lead(h + 256, (y[i] >> shift) & 255u, v && (y[i] & mask) == pb, lane);
+      }
+    }
+    // the previous pass's histograms were last read before its final barrier
+    for (int i = tid; i < 512; i += NT) hn[i] = 0;
+    sync_nt<NT>();
+    if (warp == 0) radix_pick(h, s4, pa, shift, lane);
+    if (warp == (NT > 32 ? 1 : 0)) radix_pick(h + 256, s4 + 2, pb, shift, lane);
+    mask |= 0xFFu << shift;
+    cur ^= 1;
+    sync_nt<NT>();
+  }
+  Ta = s4[0];
+  Tb = s4[2];
+}
+
 // Sortable key of a non-negative float or NaN (NaN above +inf, as the bit
 // patterns of the reference's comparisons would order them).
 __device__ __forceinline__ uint32_t sens_key(float s) {
@@ -1161,12 +1218,23 @@ __device__ __forceinline__ uint32_t sens_key(float s) {
 // about 1.35 and of an irregular group about 4.5, and a tile's write-out
 // about 16 (units of 1/10 below).  CTA b gets the tiles [S_b, S_b+1) (in
 // column-major order) where the weighted prefix reaches b / G of the total.
+// floor(x / d) for 0 <= x < 2^53 and d > 0 without a 64-bit division.
+__device__ __forceinline__ int64_t floor_div_small(int64_t x, int64_t d) {
+  int64_t q = (int64_t)((double)x / (double)d);
+  if (q * d > x)
+    --q;
+  else if ((q + 1) * d <= x)
+    ++q;
+  return q;
+}
+
 __device__ __forceinline__ int64_t enc_uniform_start(int64_t b, int64_t ntiles, int G) {
   return b * ntiles / G;
 }
 
 template <int NT>
-__device__ void enc_partition(const QArgs& a, const uint32_t* s_cost /* nct, or null */) {
+__device__ void enc_partition(const QArgs& a, const uint32_t* s_cost /* nct, or null */,
+                              long long* s_pref /* nct + 1 */) {
   const int tid = threadIdx.x % NT, lane = threadIdx.x & 31, warp = tid >> 5;
   constexpr int NWARP = NT / 32;
   __shared__ long long s_part[NWARP];
@@ -1174,10 +1242,11 @@ __device__ void enc_partition(const QArgs& a, const uint32_t* s_cost /* nct, or 
   const int64_t ntiles = (int64_t)nct * nrc;
   if (G <= 0 || G > kMaxEncGrid) return;
   int32_t* S = a.ws.enc_start;
-  if (ntiles < 2 * (int64_t)G || s_cost == nullptr) {
+  if (ntiles < 2 * (int64_t)G || s_cost == nullptr || s_pref == nullptr) {
     for (int b = tid; b <= G; b += NT) S[b] = (int32_t)enc_uniform_start(b, ntiles, G);
     return;
   }
+  // s_pref[ct] = weighted work of the column tiles before ct (exclusive scan)
   const int per = (nct + NT - 1) / NT;
   const int c0 = min(nct, tid * per), c1 = min(nct, c0 + per);
   long long local = 0;
@@ -1190,23 +1259,31 @@ __device__ void enc_partition(const QArgs& a, const uint32_t* s_cost /* nct, or 
   }
   if (lane == 31) s_part[warp] = incl;
   sync_nt<NT>();
-  long long P = incl - local, total = 0;
-  for (int w = 0; w < NWARP; ++w) {
-    if (w < warp) P += s_part[w];
-    total += s_part[w];
-  }
-  // CTA b starts where the weighted prefix reaches b * total / G (integers:
-  // P * G <= b * total < Pn * G selects the column tile)
+  long long P = incl - local;
+  for (int w = 0; w < warp; ++w) P += s_part[w];
   for (int ct = c0; ct < c1; ++ct) {
-    const long long c = s_cost[ct];
-    const long long Pn = P + c * nrc;
-    long long b = (P * G + total - 1) / total;
-    if (b < 1) b = 1;
-    for (; b < G && b * total < Pn * G; ++b) {
-      const long long num = b * total - P * G, den = (long long)G * c;
-      S[b] = (int32_t)((int64_t)ct * nrc + (num + den - 1) / den);
+    s_pref[ct] = P;
+    P += (long long)s_cost[ct] * nrc;
+  }
+  if (c1 == nct && c0 < c1) s_pref[nct] = P;
+  sync_nt<NT>();
+  const long long total = s_pref[nct];
+  // CTA b starts in the column tile with s_pref[ct] G <= b total <
+  // s_pref[ct + 1] G (the prefix grows strictly: every tile costs > 0), at
+  // row chunk ceil((b total - s_pref[ct] G) / (G cost)) of it; the products
+  // stay below 2^53 (M K < 2^31)
+  for (int b = 1 + tid; b < G; b += NT) {
+    const long long bt = (long long)b * total;
+    int lo = 0, hi = nct - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (s_pref[mid] * G <= bt)
+        lo = mid;
+      else
+        hi = mid - 1;
     }
-    P = Pn;
+    const long long num = bt - s_pref[lo] * G, den = (long long)G * s_cost[lo];
+    S[b] = (int32_t)((int64_t)lo * nrc + floor_div_small(num + den - 1, den));
   }
   if (tid == 0) {
     S[0] = 0;
@@ -1232,7 +1309,10 @@ __device__ void finalize_tables(const QArgs& a, float* s1, size_t s1_bytes, uint
   const bool s1_in_smem = (size_t)ng * sizeof(float) <= s1_bytes;
   // encode work of each column tile, after s1 (for the tile split)
   uint32_t* s_cost = reinterpret_cast<uint32_t*>(s1 + ng);
-  const bool cost_in_smem = s1_in_smem && (size_t)(ng + nct) * sizeof(float) <= s1_bytes;
+  const size_t pref_off = ((size_t)(ng + nct) * sizeof(float) + 7) & ~(size_t)7;
+  long long* s_pref = reinterpret_cast<long long*>(reinterpret_cast<uint8_t*>(s1) + pref_off);
+  const bool cost_in_smem =
+      s1_in_smem && pref_off + (size_t)(nct + 1) * sizeof(long long) <= s1_bytes;
   if (tid == 0) *s_irr = 0;
   if (cost_in_smem)
     for (int ct = tid; ct < nct; ct += NT) s_cost[ct] = 160;
@@ -1308,7 +1388,7 @@ __device__ void finalize_tables(const QArgs& a, float* s1, size_t s1_bytes, uint
       a.ws.hdr->n_pend = 0;
     }
   }
-  enc_partition<NT>(a, cost_in_smem ? s_cost : nullptr);
+  enc_partition<NT>(a, cost_in_smem ? s_cost : nullptr, cost_in_smem ? s_pref : nullptr);
 }
 
 // Interval of a group's fp32 serial sum as sortable keys (lo rounded down,
@@ -1334,44 +1414,93 @@ __device__ __forceinline__ uint2 sens_interval_of(uint32_t f, double P, double m
 // if its upper bound is below the n4-th largest lower bound (n4 groups surely
 // exceed it).  The rest are pending; if all or none of them must be 4-bit
 // the selection is complete, otherwise their exact sums decide.
+constexpr int kSelKPT = 8;  // keys per thread held in registers by the selection
+
+// Encode work of a group (units of 1/10; a column tile's write-out is 160).
+__device__ __forceinline__ uint32_t enc_group_cost(int pr, uint8_t greg) {
+  return !((greg >> pr) & 1) ? 180u : pr ? 54u : 20u;
+}
+
 template <int NT>
 __device__ void select_from_intervals(const QArgs& a, uint8_t* scratch, size_t scratch_bytes) {
-  const int ng = a.ng, n4 = a.n4;
+  const int ng = a.ng, n4 = a.n4, nct = a.nct;
   const int tid = threadIdx.x % NT, lane = threadIdx.x & 31, warp = tid >> 5;
   constexpr int NWARP = NT / 32;
-  __shared__ uint32_t hist[512];
+  __shared__ uint32_t hist[1024];
   __shared__ uint32_t s4[4];
   __shared__ uint32_t s_wsum[NWARP];
   __shared__ uint32_t s_cnt[2];
+  // scratch: the keys (only when they do not fit in registers and do fit
+  // here), then the column tiles' encode costs and their prefix
+  const bool reg_keys = ng <= kSelKPT * NT;
+  const bool keys_in_smem = !reg_keys && (size_t)ng * 8 <= scratch_bytes;
+  const size_t cost_off = keys_in_smem ? (size_t)ng * 8 : 0;
+  const size_t pref_off = (cost_off + (size_t)nct * 4 + 7) & ~(size_t)7;
+  const bool cost_in_smem = pref_off + (size_t)(nct + 1) * 8 <= scratch_bytes;
   uint2* keys = reinterpret_cast<uint2*>(scratch);
-  const bool keys_in_smem = (size_t)ng * 8 <= scratch_bytes;
-  auto lo_of = [&](int g) -> uint32_t { return keys_in_smem ? keys[g].x : __ldcg(a.ws.gkey + g).x; };
-  auto hi_of = [&](int g) -> uint32_t { return keys_in_smem ? keys[g].y : __ldcg(a.ws.gkey + g).y; };
+  uint32_t* s_cost = reinterpret_cast<uint32_t*>(scratch + cost_off);
+  long long* s_pref = reinterpret_cast<long long*>(scratch + pref_off);
+  auto key_of = [&](int g) -> uint2 { return keys_in_smem ? keys[g] : __ldcg(a.ws.gkey + g); };
+  if (cost_in_smem)
+    for (int ct = tid; ct < nct; ct += NT) s_cost[ct] = 160;
+  if (tid == 0) s_cnt[0] = s_cnt[1] = 0;
+  // adds the encode cost of group g (precision pr) to its column tile; the
+  // groups of a column tile are 8 consecutive indices, and with NT a multiple
+  // of 8 they sit in 8 consecutive lanes (all lanes call it)
+  auto add_cost = [&](int g, bool on, int pr, uint8_t greg) {
+    uint32_t c = on ? enc_group_cost(pr, greg) : 0u;
+    c += __shfl_xor_sync(0xffffffffu, c, 1);
+    c += __shfl_xor_sync(0xffffffffu, c, 2);
+    c += __shfl_xor_sync(0xffffffffu, c, 4);
+    if ((lane & 7) == 0 && c != 0u && g < ng) atomicAdd(&s_cost[g / kTileGroups], c);
+  };
   int pending = 0;
   if (a.select && n4 > 0) {
-    if (keys_in_smem)
-      for (int g = tid; g < ng; g += NT) keys[g] = __ldcg(a.ws.gkey + g);
-    if (tid == 0) s_cnt[0] = s_cnt[1] = 0;
-    sync_nt<NT>();
     const bool all_in = n4 >= ng;
     uint32_t Alo = 0, Bhi = 0;
-    if (all_in)
-      kth_largest2<NT>(ng, n4, lo_of, n4, hi_of, hist, s4, Alo, Bhi);
-    else
-      kth_largest2<NT>(ng, n4, lo_of, n4 + 1, hi_of, hist, s4, Alo, Bhi);
+    uint32_t kx[kSelKPT], ky[kSelKPT];
+    uint8_t kg[kSelKPT];
+    if (reg_keys) {
+#pragma unroll
+      for (int i = 0; i < kSelKPT; ++i) {
+        const int g = tid + i * NT;
+        const uint2 k = g < ng ? __ldcg(a.ws.gkey + g) : make_uint2(0u, 0u);
+        kx[i] = k.x;
+        ky[i] = k.y;
+        kg[i] = g < ng ? a.ws.greg[g] : (uint8_t)0;
+      }
+      kth_largest2_reg<NT, kSelKPT>(kx, ky, ng, n4, all_in ? n4 : n4 + 1, hist, s4, Alo, Bhi);
+    } else {
+      if (keys_in_smem)
+        for (int g = tid; g < ng; g += NT) keys[g] = __ldcg(a.ws.gkey + g);
+      sync_nt<NT>();
+      auto lo_of = [&](int g) -> uint32_t { return key_of(g).x; };
+      auto hi_of = [&](int g) -> uint32_t { return key_of(g).y; };
+      kth_largest2<NT>(ng, n4, lo_of, all_in ? n4 : n4 + 1, hi_of, hist, s4, Alo, Bhi);
+    }
+    // certainly 4-bit (1), certainly 2-bit (0) or pending (2); the decided
+    // groups' encode costs go to their column tiles now
     uint32_t c_in = 0, c_pend = 0;
-    for (int g = tid; g < ng; g += NT) {
-      const uint32_t l = lo_of(g), h = hi_of(g);
-      uint8_t p;
-      if (all_in || l > Bhi)
-        p = 1;
-      else if (h < Alo)
-        p = 0;
-      else
-        p = 2;
-      c_in += p == 1;
-      c_pend += p == 2;
-      a.ws.prec[g] = p;
+    auto classify = [&](int g, uint32_t l, uint32_t h, uint8_t greg, bool on) {
+      uint8_t p = 0;
+      if (on) {
+        p = (all_in || l > Bhi) ? 1 : (h < Alo ? 0 : 2);
+        c_in += p == 1;
+        c_pend += p == 2;
+        a.ws.prec[g] = p;
+      }
+      if (cost_in_smem) add_cost(g, on && p != 2, p, greg);
+    };
+    if (reg_keys) {
+#pragma unroll
+      for (int i = 0; i < kSelKPT; ++i)
+        if (i * NT < ng) classify(tid + i * NT, kx[i], ky[i], kg[i], tid + i * NT < ng);
+    } else {
+      for (int g0 = 0; g0 < ng; g0 += NT) {  // whole warps (add_cost shuffles)
+        const int g = g0 + tid;
+        const uint2 k = g < ng ? key_of(g) : make_uint2(0u, 0u);
+        classify(g, k.x, k.y, g < ng ? a.ws.greg[g] : (uint8_t)0, g < ng);
+      }
     }
     c_in = __reduce_add_sync(0xffffffffu, c_in);
     c_pend = __reduce_add_sync(0xffffffffu, c_pend);
@@ -1383,33 +1512,31 @@ __device__ void select_from_intervals(const QArgs& a, uint8_t* scratch, size_t s
     const int need = n4 - (int)s_cnt[0], np = (int)s_cnt[1];
     if (np > 0 && (need <= 0 || need >= np)) {
       // all pending groups take the same precision
-      for (int g = tid; g < ng; g += NT)
-        if (a.ws.prec[g] == 2) a.ws.prec[g] = need > 0 ? 1 : 0;
+      const uint8_t to = need > 0 ? 1 : 0;
+      for (int g0 = 0; g0 < ng; g0 += NT) {
+        const int g = g0 + tid;
+        const bool pend = g < ng && a.ws.prec[g] == 2;
+        if (pend) a.ws.prec[g] = to;
+        if (cost_in_smem) add_cost(g, pend, to, pend ? a.ws.greg[g] : (uint8_t)0);
+      }
+      sync_nt<NT>();
     } else if (np > 0) {
       pending = 1;
       if (tid == 0) a.ws.hdr->need = (uint32_t)need;
     }
   } else {
-    for (int g = tid; g < ng; g += NT) a.ws.prec[g] = 0;
-  }
-  sync_nt<NT>();
-  if (!pending) {
-    // every precision is known: the column tiles' encode work and the tile
-    // split here; group_precision, any_irregular and the 2nd-order table are
-    // written by the CTAs of the next kernel in parallel (tables_grid)
-    uint32_t* s_cost = reinterpret_cast<uint32_t*>(scratch);  // the keys are done with
-    const bool cost_in_smem = (size_t)a.nct * sizeof(uint32_t) <= scratch_bytes;
-    if (cost_in_smem) {
-      for (int ct = tid; ct < a.nct; ct += NT) s_cost[ct] = 160;
-      sync_nt<NT>();
-      for (int g = tid; g < ng; g += NT) {
-        const int pr = a.ws.prec[g];
-        const bool reg = (a.ws.greg[g] >> pr) & 1;
-        atomicAdd(&s_cost[g / kTileGroups], !reg ? 180u : pr ? 54u : 20u);
-      }
-      sync_nt<NT>();
+    for (int g0 = 0; g0 < ng; g0 += NT) {
+      const int g = g0 + tid;
+      if (g < ng) a.ws.prec[g] = 0;
+      if (cost_in_smem) add_cost(g, g < ng, 0, g < ng ? a.ws.greg[g] : (uint8_t)0);
     }
-    enc_partition<NT>(a, cost_in_smem ? s_cost : nullptr);
+    sync_nt<NT>();
+  }
+  if (!pending) {
+    // every precision is known: the tile split here; group_precision,
+    // any_irregular and the 2nd-order table are written by the CTAs of the
+    // next kernel in parallel (tables_grid)
+    enc_partition<NT>(a, cost_in_smem ? s_cost : nullptr, cost_in_smem ? s_pref : nullptr);
     if (tid == 0) {
       a.ws.hdr->n_dec = (uint32_t)ng;
       a.ws.hdr->n_pend = 0;
@@ -1490,15 +1617,6 @@ __device__ __forceinline__ void tile_fill(const __half* W, int64_t M, int64_t K,
 // CTA b takes the tiles [U_b, U_b+1), U_b = floor(b * ntiles / G), G <= ntiles
 // (so no range is empty).  A CTA's tiles of one column tile form a segment,
 // identified by b + ct (both grow along u, so the ids are distinct).
-// floor(x / d) for 0 <= x < 2^53 and d > 0 without a 64-bit division.
-__device__ __forceinline__ int64_t floor_div_small(int64_t x, int64_t d) {
-  int64_t q = (int64_t)((double)x / (double)d);
-  if (q * d > x)
-    --q;
-  else if ((q + 1) * d <= x)
-    ++q;
-  return q;
-}
 __device__ __forceinline__ int stats_start(int b, int ntiles, int G) {
   return (int)floor_div_small((int64_t)b * ntiles, G);
 }
