@@ -46,7 +46,7 @@ UNIT = "GB/s"
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--steps", type=int, default=1000)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--e2e-steps", type=int, default=5)
@@ -83,18 +83,35 @@ def max_over_ranks(ws, x: float) -> float:
 
 
 _SAMPLER = r"""
-import sys, time, pynvml
-pynvml.nvmlInit()
-h = pynvml.nvmlDeviceGetHandleByUUID(sys.argv[1])
-mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
-print("ready", flush=True)
-while True:
+import sys, time
+try:
+    import pynvml
+    pynvml.nvmlInit()
     try:
-        t = time.time()
+        h = pynvml.nvmlDeviceGetHandleByUUID(sys.argv[1])
+    except Exception:
+        h = pynvml.nvmlDeviceGetHandleByIndex(int(sys.argv[3]))
+    mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+except Exception as e:
+    print("error", type(e).__name__, str(e).replace(chr(10), " ")[:120], flush=True)
+    sys.exit(0)
+print("ready", flush=True)
+def reasons():
+    for f in ("nvmlDeviceGetCurrentClocksEventReasons", "nvmlDeviceGetCurrentClocksThrottleReasons"):
+        try:
+            return getattr(pynvml, f)(h)
+        except Exception:
+            pass
+    return 0
+while True:
+    t = time.time()
+    try:
         sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
-        rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
-        pw = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
-        print(t, sm, mx, rs, pw, flush=True)
+        try:
+            pw = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
+        except Exception:
+            pw = -1.0
+        print(t, sm, mx, reasons(), pw, flush=True)
     except Exception:
         pass
     time.sleep(float(sys.argv[2]))
@@ -117,19 +134,28 @@ class ClockSampler:
     def __init__(self, device_index: int):
         self.samples = []
         self.proc = None
+        self.why = ""
         try:
             import subprocess
 
             import torch
             uuid = "GPU-" + str(torch.cuda.get_device_properties(device_index).uuid)
+            # NVML index of this device: CUDA_VISIBLE_DEVICES may renumber
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+            ids = [x.strip() for x in vis.split(",") if x.strip()]
+            nvml_index = int(ids[device_index]) if device_index < len(ids) and \
+                ids[device_index].isdigit() else device_index
             self.proc = subprocess.Popen([sys.executable, "-c", _SAMPLER, uuid,
-                                          str(self.PERIOD_S)],
+                                          str(self.PERIOD_S), str(nvml_index)],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
                                          text=True)
-            if self.proc.stdout.readline().strip() != "ready":
+            first = self.proc.stdout.readline().strip()
+            if first != "ready":
+                self.why = first or "sampler exited"
                 self.proc.kill()
                 self.proc = None
-        except Exception:
+        except Exception as e:
+            self.why = f"{type(e).__name__}: {e}"[:120]
             self.proc = None
 
     def __enter__(self):
@@ -168,7 +194,8 @@ class ClockSampler:
 
     def summary(self) -> dict:
         if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"],
+                    "why": self.why or "no sample"}
         reasons = sorted({n for (_, _, r, _) in self.samples for n, bit in self.REASONS.items()
                           if r & bit})
         return {"sm_mhz": statistics.median(s[0] for s in self.samples),

@@ -60,6 +60,15 @@ constexpr int kStages = 3;     // stats tile ring per CTA (two CTAs per SM)
 constexpr int kEncStages = 2;  // encode tile ring (its staging buffers take the rest)
 constexpr int kStatsSmem = kStages * kTileBytes + 1024;   // + alignment slack
 constexpr int kEncSmem = kEncStages * kTileBytes + 1024;
+// encode CTA size: 8 warps, two CTAs per SM.  The items are taken from a
+// shared counter, so any warp count works; 10 or 12 warps (96 / 80
+// registers a thread) measured 3% / 13% slower on the 7B MLP pair.
+constexpr int kEncThreads = 256;
+static_assert(kEncThreads % 32 == 0 && kEncThreads >= 256, "encode needs >= 8 warps");
+// full-tile write-out: threads [0, 256) store the packed words; the per-row
+// arrays go to threads [256, kEncThreads) (or [0, 128) with 256 threads)
+constexpr int kRowWriter0 = kEncThreads > 256 ? 256 : 0;
+constexpr int kRowWriters = kEncThreads > 256 ? kEncThreads - 256 : kChunkRows;
 
 // exact sums of pending groups
 constexpr int kMaxItems = 8;             // program items per (group, chunk)
@@ -2201,7 +2210,7 @@ __device__ __forceinline__ void post_prologue(const QArgs& a) {
 __device__ __forceinline__ void post_rowptr_scan(const QArgs& a) {
   if (a.ws.hdr->any_irregular == 0) return;
   __shared__ int s_last;
-  __shared__ long long part[256];
+  __shared__ long long part[kEncThreads];
   const int tid = threadIdx.x;
   const int64_t M = a.M;
   __threadfence();
@@ -2284,7 +2293,7 @@ __device__ __forceinline__ void enc_build_ctx(const QArgs& a, EncCtx& cx, int ct
   int kind = kEncKindNone, pr = 0, gs = 0;
   uint16_t sh = 0;
   int8_t z = 0;
-  if (g < ng) {
+  if (warp < kTileGroups && g < ng) {
     pr = a.ws.prec[g];
     const GroupParams& p = a.ws.params[2 * g + pr];
     if (lane < 15) t = (uint32_t)p.thresh[lane] * 0x00010001u;
@@ -2293,8 +2302,8 @@ __device__ __forceinline__ void enc_build_ctx(const QArgs& a, EncCtx& cx, int ct
     sh = (uint16_t)p.scale_h;
     z = (int8_t)p.zero;
   }
-  if (lane < 16) (&cx.thr[warp][0].x)[lane] = t;
-  if (lane == 0) {
+  if (warp < kTileGroups && lane < 16) (&cx.thr[warp][0].x)[lane] = t;
+  if (warp < kTileGroups && lane == 0) {
     cx.kind[warp] = (uint8_t)kind;
     cx.gs[warp] = (uint8_t)gs;
     cx.pr[warp] = (uint8_t)pr;
@@ -2356,7 +2365,7 @@ __device__ __forceinline__ uint8_t sq_direct(const QArgs& a, float s1f, int64_t 
   return (uint8_t)max(0, min(15, q2));
 }
 
-__global__ void __launch_bounds__(256, 2)
+__global__ void __launch_bounds__(kEncThreads, 2)
     encode_kernel(const __grid_constant__ CUtensorMap tmap, const QArgs a, int use_tma,
                   int vec_out) {
   extern __shared__ uint8_t dsm_raw[];
@@ -2409,14 +2418,14 @@ __global__ void __launch_bounds__(256, 2)
   const int rp = P256 / ng;  // a power of two, at most 256
   const int64_t row_full_end = a.cl.nfull * kGroup2;
   const int64_t full_rows = row_full_end / ng;  // rows whose scales lie in full 2nd-order chunks
-  // write-out offsets of this thread in a full tile (elements / words from
-  // the tile's first output): packed_2bit row tid/2, half tid%2; packed_4bit
-  // rows tid/4 and tid/4 + 64, quarter tid%4; the per-row arrays row tid
+  // write-out offsets of thread tid < 256 in a full tile (elements / words
+  // from the tile's first output): packed_2bit row tid/2, half tid%2;
+  // packed_4bit rows tid/4 and tid/4 + 64, quarter tid%4 (the per-row arrays
+  // go to the threads from kRowWriter0)
   const int wo_r2 = tid >> 1, wo_h2 = tid & 1;
   const int64_t wo_o2 = (int64_t)wo_r2 * ng + 4 * wo_h2;
   const int wo_r4 = tid >> 2, wo_q4 = tid & 3;
   const int64_t wo_o4 = 2 * (int64_t)wo_r4 * ng + 4 * wo_q4;
-  const int64_t wo_or = (int64_t)tid * ng;
   bool failed = false;
   uint32_t bad = 0;  // thread 0: stages whose wait ran out
   int cur_ct = -1;
@@ -2513,22 +2522,26 @@ __global__ void __launch_bounds__(256, 2)
     const int64_t obase = row0 * ng + gb;  // flat index of (row0, gb)
     if (vec_out && gb + kTileGroups <= ng && nr == kChunkRows && row0 + kChunkRows <= full_rows) {
       // a full tile: fixed trip counts, per-thread offsets from the prologue
-      const uint4 x2 = make_uint4(cb.p2[wo_h2 * 4][wo_r2], cb.p2[wo_h2 * 4 + 1][wo_r2],
-                                  cb.p2[wo_h2 * 4 + 2][wo_r2], cb.p2[wo_h2 * 4 + 3][wo_r2]);
-      *reinterpret_cast<uint4*>(a.packed2 + obase + wo_o2) = x2;
+      if (tid < 256) {
+        const uint4 x2 = make_uint4(cb.p2[wo_h2 * 4][wo_r2], cb.p2[wo_h2 * 4 + 1][wo_r2],
+                                    cb.p2[wo_h2 * 4 + 2][wo_r2], cb.p2[wo_h2 * 4 + 3][wo_r2]);
+        *reinterpret_cast<uint4*>(a.packed2 + obase + wo_o2) = x2;
 #pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        const int r = wo_r4 + 64 * k;
-        const uint2 x = cb.p4[2 * wo_q4][r], y = cb.p4[2 * wo_q4 + 1][r];
-        *reinterpret_cast<uint4*>(a.packed4 + 2 * obase + wo_o4 + (int64_t)k * 128 * ng) =
-            make_uint4(x.x, x.y, y.x, y.y);
+        for (int k = 0; k < 2; ++k) {
+          const int r = wo_r4 + 64 * k;
+          const uint2 x = cb.p4[2 * wo_q4][r], y = cb.p4[2 * wo_q4 + 1][r];
+          *reinterpret_cast<uint4*>(a.packed4 + 2 * obase + wo_o4 + (int64_t)k * 128 * ng) =
+              make_uint4(x.x, x.y, y.x, y.y);
+        }
       }
-      if (tid < kChunkRows) {
-        const int64_t o = obase + wo_or;
-        *reinterpret_cast<uint4*>(a.scales1 + o) = cx.shv;
-        *reinterpret_cast<uint2*>(a.zeros1 + o) = cx.zv;
-        *reinterpret_cast<uint2*>(a.sq + o) =
-            *reinterpret_cast<const uint2*>(&cx.sqrow[(rc * kChunkRows + tid) & (rp - 1)][0]);
+      if (tid >= kRowWriter0 && tid < kRowWriter0 + kRowWriters) {
+        for (int r = tid - kRowWriter0; r < kChunkRows; r += kRowWriters) {
+          const int64_t o = obase + (int64_t)r * ng;
+          *reinterpret_cast<uint4*>(a.scales1 + o) = cx.shv;
+          *reinterpret_cast<uint2*>(a.zeros1 + o) = cx.zv;
+          *reinterpret_cast<uint2*>(a.sq + o) =
+              *reinterpret_cast<const uint2*>(&cx.sqrow[(rc * kChunkRows + r) & (rp - 1)][0]);
+        }
       }
     } else if (vec_out && gb + kTileGroups <= ng) {
       for (int k = tid; k < nr * 2; k += blockDim.x) {
@@ -2761,7 +2774,7 @@ extern "C" mb_status mb_quantize(const void* weights_fp16, int64_t M, int64_t K,
   {
     static std::atomic<int> occ[64];
     int per_sm = 1;
-    MB_CUDA_TRY(blocks_per_sm_once(encode_kernel, 256, kEncSmem, occ, 64, &per_sm));
+    MB_CUDA_TRY(blocks_per_sm_once(encode_kernel, kEncThreads, kEncSmem, occ, 64, &per_sm));
     enc_grid = std::max<int64_t>(
         1, std::min<int64_t>({ntiles, (int64_t)sms * std::max(per_sm, 1), (int64_t)kMaxEncGrid}));
   }
@@ -2786,7 +2799,7 @@ extern "C" mb_status mb_quantize(const void* weights_fp16, int64_t M, int64_t K,
     };
     const int vec_out = (ng % 8 == 0) && al(packed_2bit, 16) && al(packed_4bit, 16) &&
                         al(scales_1st_fp16, 16) && al(zeros_1st, 8) && al(scales_1st_quant, 8);
-    if (mb_status st = launch_pdl(encode_kernel, dim3((unsigned)enc_grid), dim3(256), kEncSmem,
+    if (mb_status st = launch_pdl(encode_kernel, dim3((unsigned)enc_grid), dim3(kEncThreads), kEncSmem,
                                   stream, tmap, qa, tma ? 1 : 0, vec_out))
       return st;
   }
