@@ -457,8 +457,11 @@ def run_reference_arm(args, ws, rank, local):
     for w, h, c in zip(wn, hn, cases):
         oracle.quantize(w, c.ratio_4bit, h, nthreads=0)
     t_one = time.perf_counter() - t_one
-    # bounded sample per step: whole pair if a step is short, else row slices
-    frac = min(1.0, 6.0 / max(t_one, 1e-6))
+    # bounded sample per step: whole pair if a step is short, else row slices;
+    # the timed steps together take about a minute (6 s a step at most), the
+    # warm-up steps likewise
+    per_step_s = min(6.0, 60.0 / max(1, args.steps))
+    frac = min(1.0, per_step_s / max(t_one, 1e-6))
     rows = [max(256, int(w.shape[0] * frac)) for w in wn]
     sample = [np.ascontiguousarray(w[:r]) for w, r in zip(wn, rows)] if frac < 1 else wn
     step_bytes = sum(2 * s.size for s in sample)
