@@ -272,12 +272,14 @@ def run_ours(args, ws, rank, local):
     # two sets of plans: step k + 1 is enqueued before step k is finished
     # (its outlier count read and CSR extracted), so the GPU does not idle
     # while the host works; every step's outputs are complete inside the
-    # timed region.  The two matrices are independent and run on streams of
-    # their own, so one's latency-bound selection overlaps the other's
-    # streaming kernels.
-    streams = [torch.cuda.Stream(dev) for _ in W]
-    plan_sets = [[_C.QuantizePlan(*w.shape, dev, stream=st) for w, st in zip(W, streams)]
-                 for _ in range(2)]
+    # timed region.  Every plan has a stream of its own (two matrices x two
+    # sets): the matrices are independent, so one call's latency-bound
+    # selection tail overlaps other calls' streaming kernels, including the
+    # next step's, which would otherwise queue behind it on a shared stream.
+    stream_sets = [[torch.cuda.Stream(dev) for _ in W] for _ in range(2)]
+    streams = [st for ss in stream_sets for st in ss]
+    plan_sets = [[_C.QuantizePlan(*w.shape, dev, stream=st) for w, st in zip(W, ss)]
+                 for ss in stream_sets]
     fp16_bytes = sum(2 * w.numel() for w in W)
     nnz_seen = []
 
@@ -427,7 +429,8 @@ def run_ours(args, ws, rank, local):
                                        "pipelined step, DRAM read+write per call)",
                      "kernel": "quantize calls of a step: stats (+group parameters and "
                                "selection), exact/tables, encode (+row pointers) -- 3 kernels "
-                               "chained with PDL per matrix, the two matrices on two streams; "
+                               "chained with PDL per matrix, every plan on a stream of its own "
+                               "(2 matrices x 2 step sets); "
                                "device time per step",
                      "algorithmic_bytes_per_call": alg,
                      "call_ms": [round(d, 4) for d in dur]},
