@@ -269,16 +269,13 @@ __device__ __forceinline__ uint32_t row_word(const Row16& v, int k) {
 
 __device__ __forceinline__ __half2 as_h2(uint32_t w) { return *reinterpret_cast<__half2*>(&w); }
 
-// Run r (0..127) of tile group gi from a tile in shared memory: two 64-column
-// TMA boxes written with the 128-byte swizzle (16-byte chunk c of row r sits
-// at chunk c ^ (r & 7)), so a warp's 32 runs hit distinct banks.
-__device__ __forceinline__ Row16 tile_run(const uint8_t* buf, int gi, int r) {
+// One 16-byte half (8 columns: h = 0 low, 1 high) of tile group gi's row r
+// (0..127) from a tile in shared memory: two 64-column TMA boxes written with
+// the 128-byte swizzle (16-byte chunk c of row r sits at chunk c ^ (r & 7)),
+// so 8 consecutive rows of one half hit distinct banks.
+__device__ __forceinline__ uint4 tile_half(const uint8_t* buf, int gi, int r, int h) {
   const uint8_t* base = buf + (gi >> 2) * kBoxBytes + r * 128;
-  const int c0 = 2 * (gi & 3), sw = r & 7;
-  Row16 v;
-  v.lo = *reinterpret_cast<const uint4*>(base + ((c0 ^ sw) << 4));
-  v.hi = *reinterpret_cast<const uint4*>(base + (((c0 + 1) ^ sw) << 4));
-  return v;
+  return *reinterpret_cast<const uint4*>(base + (((2 * (gi & 3) + h) ^ (r & 7)) << 4));
 }
 
 // ---------------------------------------------------------------------------
@@ -1760,9 +1757,13 @@ __global__ void __launch_bounds__(kStatsThreads, 2)
   bool snan = false, sinf = false, sloose = false;
   uint32_t srows = 0;
   int seg_rc0 = 0;
-  // lane l ends the column-sum butterfly with column 8 b4 + 4 b3 + 2 b2 + b1
-  const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4, b1 = lane & 2;
-  const int col = (b4 ? 8 : 0) + (b3 ? 4 : 0) + (b2 ? 2 : 0) + (b1 ? 1 : 0);
+  // lane = row rl (of 16) of each 16-row step and half hh of the group's 16
+  // columns (a quarter warp reads 8 rows of one half: 8 distinct swizzle
+  // slots); after the column-sum butterfly lane l holds column
+  // 8 hh + 4 b3 + 2 b2 + b1 (bits of l)
+  const int rl = lane & 15, hh = lane >> 4;
+  const bool b3 = lane & 8, b2 = lane & 4, b1 = lane & 2;
+  const int col = 8 * hh + (b3 ? 4 : 0) + (b2 ? 2 : 0) + (b1 ? 1 : 0);
   const bool even = !(lane & 1);
   int ct = u_begin / nrc, rc = u_begin - ct * nrc;
   for (int u = u_begin; u < u_end; ++u) {
@@ -1807,31 +1808,34 @@ __global__ void __launch_bounds__(kStatsThreads, 2)
       const bool edge = (row0 + kChunkRows > M) || gs < kGroup1;
       const size_t rec = (size_t)g * nrc + rc;
       __half2 hmn = smn, hmx = smx;
-      float acc[16];
+      float acc[8];
 #pragma unroll
-      for (int c = 0; c < 16; ++c) acc[c] = 0.0f;
+      for (int c = 0; c < 8; ++c) acc[c] = 0.0f;
       if (!edge) {  // the whole tile lies inside the matrix (all but the edge tiles)
 #pragma unroll
-        for (int s = 0; s < kSteps; ++s) {
-          const Row16 v = tile_run(buf, gi, s * 32 + lane);
+        for (int s = 0; s < kChunkRows / 16; ++s) {
+          const uint4 q = tile_half(buf, gi, s * 16 + rl, hh);
+          const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const uint32_t w = row_word(v, k);
-            hmn = __hmin2(hmn, as_h2(w));
-            hmx = __hmax2(hmx, as_h2(w));
-            if (kSens) sq_acc2(w, acc[2 * k], acc[2 * k + 1]);
+          for (int k = 0; k < 4; ++k) {
+            hmn = __hmin2(hmn, as_h2(w4[k]));
+            hmx = __hmax2(hmx, as_h2(w4[k]));
+            if (kSens) sq_acc2(w4[k], acc[2 * k], acc[2 * k + 1]);
           }
         }
       } else {
+        // this half's valid columns
+        const uint32_t hmask = (cmask >> (8 * hh)) & 0xFFu;
 #pragma unroll 1
-        for (int s = 0; s < kSteps; ++s) {
-          const int r = s * 32 + lane;
-          const Row16 v = tile_run(buf, gi, r);
-          const uint32_t vmask = row0 + r < M ? cmask : 0u;
+        for (int s = 0; s < kChunkRows / 16; ++s) {
+          const int r = s * 16 + rl;
+          const uint4 q = tile_half(buf, gi, r, hh);
+          const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+          const uint32_t vmask = row0 + r < M ? hmask : 0u;
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
+          for (int k = 0; k < 4; ++k) {
             // outside the matrix: NaN for min / max (ignored), 0 for sums
-            const uint32_t w = row_word(v, k);
+            const uint32_t w = w4[k];
             const uint32_t keep = (((vmask >> (2 * k)) & 1u) ? 0x0000FFFFu : 0u) |
                                   (((vmask >> (2 * k + 1)) & 1u) ? 0xFFFF0000u : 0u);
             const uint32_t ws = w & keep;
@@ -1846,17 +1850,14 @@ __global__ void __launch_bounds__(kStatsThreads, 2)
       smx = hmx;
       srows += (uint32_t)rows;
       if (kSens) {
-        // per-column sums over the chunk's rows by a transposing butterfly:
-        // each step halves the columns a lane holds
-        float a8[8], a4[4], a2[2];
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          a8[j] = __fadd_rn(b4 ? acc[8 + j] : acc[j],
-                            __shfl_xor_sync(0xffffffffu, b4 ? acc[j] : acc[8 + j], 16));
+        // per-column sums over the chunk's rows by a transposing butterfly
+        // over the row bits 3..1 (each step halves the columns a lane
+        // holds), then a plain sum over bit 0
+        float a4[4], a2[2];
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-          a4[j] = __fadd_rn(b3 ? a8[4 + j] : a8[j],
-                            __shfl_xor_sync(0xffffffffu, b3 ? a8[j] : a8[4 + j], 8));
+          a4[j] = __fadd_rn(b3 ? acc[4 + j] : acc[j],
+                            __shfl_xor_sync(0xffffffffu, b3 ? acc[j] : acc[4 + j], 8));
 #pragma unroll
         for (int j = 0; j < 2; ++j)
           a2[j] = __fadd_rn(b2 ? a4[2 + j] : a4[j],
