@@ -137,6 +137,25 @@ mb_status mb_dequantize(const int32_t* packed_2bit, const int32_t* packed_4bit,
                         mb_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * dequantize from the compact scales -- no counterpart in the reference,
+ * which computes scales_1st_quant / scales_2nd / zeros_2nd
+ * (core/quantize.cu:245-280) but never reads them back.  Every group's scale
+ * is rebuilt from its 4-bit code by the reference's dequantize rule one level
+ * up: s = fp16(float(scales_2nd[c]) * (q2 - zeros_2nd[c])), q2 =
+ * scales_1st_quant[r, g], c = (r * ng + g) / 256; then out[r, col] =
+ * fp16(float(s) * (q - zeros_1st[r, g])).  With nnz > 0 the CSR outliers
+ * (row_ptrs [M + 1], col_indices / values [nnz]) are written back as their
+ * exact fp16 values; entries past nnz or outside [0, K) are skipped.
+ * ------------------------------------------------------------------------- */
+mb_status mb_dequantize_2nd(const int32_t* packed_2bit, const int32_t* packed_4bit,
+                            const uint8_t* scales_1st_quant, const void* scales_2nd_fp16,
+                            const int8_t* zeros_2nd, const int8_t* zeros_1st,
+                            const uint8_t* group_precision, const int32_t* outlier_row_ptrs,
+                            const int32_t* outlier_col_indices, const void* outlier_values_fp16,
+                            int64_t nnz, int64_t M, int64_t K, void* out_fp16,
+                            mb_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * pack / unpack -- replace memboost::pack_2bit_op, unpack_2bit_op,
  * pack_4bit_op, unpack_4bit_op (core/torch_ops.h:10-15,
  * core/torch_ops.cu:20-102; bound in core/bindings.cpp:9-22).

@@ -41,6 +41,8 @@ _lib.mb_quantize_flags.argtypes = [_P, ctypes.c_size_t, _I64, _I64,
                                    ctypes.POINTER(ctypes.c_uint32), _P]
 _lib.mb_dequantize.restype = ctypes.c_int
 _lib.mb_dequantize.argtypes = [_P, _P, _P, _P, _P, _I64, _I64, _P, _P]
+_lib.mb_dequantize_2nd.restype = ctypes.c_int
+_lib.mb_dequantize_2nd.argtypes = [_P] * 10 + [_I64, _I64, _I64, _P, _P]
 for _n in ("mb_pack_2bit", "mb_pack_4bit"):
     getattr(_lib, _n).restype = ctypes.c_int
     getattr(_lib, _n).argtypes = [_P, _I64, _P, _P]
@@ -260,6 +262,57 @@ def dequantize(packed_2bit: torch.Tensor, packed_4bit: torch.Tensor, scales_1st:
         if out is None:
             out = torch.empty((M, K), dtype=torch.float16, device=dev)
         _check(_lib.mb_dequantize(*[_ptr(a) for a in args], M, K, _ptr(out), _stream(dev)))
+    return out
+
+
+
+def dequantize_2nd(packed_2bit: torch.Tensor, packed_4bit: torch.Tensor,
+                   scales_1st_quant: torch.Tensor, scales_2nd: torch.Tensor,
+                   zeros_2nd: torch.Tensor, zeros_1st: torch.Tensor,
+                   group_precision: torch.Tensor, M: int, K: int,
+                   outlier_row_ptrs: torch.Tensor | None = None,
+                   outlier_col_indices: torch.Tensor | None = None,
+                   outlier_values: torch.Tensor | None = None,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    """fp16 [M, K] with each group's scale rebuilt from its 4-bit 2nd-order
+    code (``mb_dequantize_2nd``); the CSR outliers are written back when
+    given (no counterpart in the reference)."""
+    if not packed_2bit.is_cuda:
+        raise RuntimeError("packed_2bit must be on CUDA")
+    M, K = int(M), int(K)
+    if M <= 0 or K <= 0:
+        raise RuntimeError("M and K must be positive")
+    dev = packed_2bit.device
+    ng = (K + GROUP_SIZE_1ST - 1) // GROUP_SIZE_1ST
+    ng2 = (M * ng + GROUP_SIZE_2ND - 1) // GROUP_SIZE_2ND
+    expect = [(packed_2bit, torch.int32, M * ng, "packed_2bit"),
+              (packed_4bit, torch.int32, 2 * M * ng, "packed_4bit"),
+              (scales_1st_quant, torch.uint8, M * ng, "scales_1st_quant"),
+              (scales_2nd, torch.float16, ng2, "scales_2nd"),
+              (zeros_2nd, torch.int8, ng2, "zeros_2nd"),
+              (zeros_1st, torch.int8, M * ng, "zeros_1st"),
+              (group_precision, torch.uint8, ng, "group_precision")]
+    nnz = 0 if outlier_values is None else int(outlier_values.numel())
+    if nnz > 0:
+        if outlier_row_ptrs is None or outlier_col_indices is None:
+            raise RuntimeError("outlier_row_ptrs and outlier_col_indices are needed with "
+                               "outlier_values")
+        expect += [(outlier_row_ptrs, torch.int32, M + 1, "outlier_row_ptrs"),
+                   (outlier_col_indices, torch.int32, nnz, "outlier_col_indices"),
+                   (outlier_values, torch.float16, nnz, "outlier_values")]
+    for t, dt, n, name in expect:
+        if t.device != dev:
+            raise RuntimeError(f"{name} must be on the same CUDA device as packed_2bit")
+        if t.dtype != dt:
+            raise RuntimeError(f"{name} must be {str(dt).replace('torch.', '')}")
+        if t.numel() < n:
+            raise RuntimeError(f"{name} too small for M={M}, K={K}")
+    with torch.cuda.device(dev):
+        args = [t.contiguous() for t, *_ in expect]
+        if out is None:
+            out = torch.empty((M, K), dtype=torch.float16, device=dev)
+        ptrs = [_ptr(a) for a in args] + [None] * (10 - len(args))
+        _check(_lib.mb_dequantize_2nd(*ptrs, nnz, M, K, _ptr(out), _stream(dev)))
     return out
 
 

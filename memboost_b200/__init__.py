@@ -8,7 +8,8 @@ GROUP_SIZE_1ST / GROUP_SIZE_2ND) with bit-identical results.
 __version__ = "0.1.0"
 
 from .formats import GROUP_SIZE_1ST, GROUP_SIZE_2ND, QuantizedTensor
-from .ops import dequantize, pack_2bit, pack_4bit, quantize, unpack_2bit, unpack_4bit
+from .ops import (dequantize, dequantize_2nd_order, pack_2bit, pack_4bit, quantize, unpack_2bit,
+                  unpack_4bit)
 
 __all__ = [
     "QuantizedTensor",
@@ -20,4 +21,5 @@ __all__ = [
     "unpack_4bit",
     "quantize",
     "dequantize",
+    "dequantize_2nd_order",
 ]

@@ -59,3 +59,19 @@ def dequantize(qtensor: QuantizedTensor, out: Optional[torch.Tensor] = None) -> 
     the reference); they remain in the CSR fields."""
     return _C.dequantize(qtensor.packed_2bit, qtensor.packed_4bit, qtensor.scales_1st,
                          qtensor.zeros_1st, qtensor.group_precision, qtensor.M, qtensor.K, out)
+
+
+def dequantize_2nd_order(qtensor: QuantizedTensor, add_outliers: bool = True,
+                         out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """fp16 [M, K] as a consumer of the compact format sees it: each group's
+    scale is rebuilt from its 4-bit code ``scales_1st_quant`` with the
+    256-group chunk's ``scales_2nd`` / ``zeros_2nd``
+    (``s = scales_2nd * (q2 - zeros_2nd)`` in fp16), then ``w = s * (q -
+    zero)``; with ``add_outliers`` the CSR outliers are written back.  The
+    reference computes these fields but has no function that reads them."""
+    nnz = int(qtensor.outlier_values.numel()) if add_outliers else 0
+    return _C.dequantize_2nd(
+        qtensor.packed_2bit, qtensor.packed_4bit, qtensor.scales_1st_quant, qtensor.scales_2nd,
+        qtensor.zeros_2nd, qtensor.zeros_1st, qtensor.group_precision, qtensor.M, qtensor.K,
+        qtensor.outlier_row_ptrs if nnz else None, qtensor.outlier_col_indices if nnz else None,
+        qtensor.outlier_values if nnz else None, out)

@@ -141,6 +141,57 @@ def dequantize(q: dict, nthreads: int = 0) -> np.ndarray:
     return out
 
 
+def dequantize_2nd(q: dict, add_outliers: bool = True) -> np.ndarray:
+    """Dequantize from the compact scales (numpy; the reference has no such
+    function -- it computes scales_1st_quant / scales_2nd / zeros_2nd in
+    core/quantize.cu:245-280 and never reads them back).  Each group's scale
+    is rebuilt by the reference's dequantize rule (core/quantize.cu:386-444)
+    one level up, then the weights are decoded with it:
+        s = fp16(f32(scales_2nd[c]) * (f32(q2) - f32(zeros_2nd[c]))),
+            q2 = scales_1st_quant[r, g], c = (r * ng + g) // 256
+        w = fp16(f32(s) * (f32(q) - f32(zeros_1st[r, g])))
+    (fp32 subtraction and product each rounded); CSR outliers written back."""
+    return decode_with_scales(q, rebuilt_scales(q), add_outliers)
+
+
+def rebuilt_scales(q: dict) -> np.ndarray:
+    """fp16 [M, ng]: each group's scale from its 4-bit 2nd-order code."""
+    M, K = int(q["M"]), int(q["K"])
+    ng = num_groups(K)
+    c = np.arange(M * ng, dtype=np.int64) // GROUP_SIZE_2ND
+    s2 = np.asarray(q["scales_2nd"]).reshape(-1).astype(np.float32)[c]
+    z2 = np.asarray(q["zeros_2nd"]).reshape(-1).astype(np.float32)[c]
+    q2 = np.asarray(q["scales_1st_quant"]).reshape(-1).astype(np.float32)
+    s = (s2 * (q2 - z2).astype(np.float32)).astype(np.float32).astype(np.float16)
+    return s.reshape(M, ng)
+
+
+def decode_with_scales(q: dict, scales: np.ndarray, add_outliers: bool = False) -> np.ndarray:
+    """fp16 [M, K] from the codes and zeros of q with the given fp16 [M, ng]
+    scales (with q's scales_1st this is the reference dequantize)."""
+    M, K = int(q["M"]), int(q["K"])
+    ng = num_groups(K)
+    s = np.asarray(scales, dtype=np.float16).reshape(M, ng).astype(np.float32)
+    z1 = np.asarray(q["zeros_1st"]).reshape(M, ng).astype(np.float32)
+    gp = np.asarray(q["group_precision"]).reshape(-1)[:ng] != 0
+    p2 = np.asarray(q["packed_2bit"]).reshape(M, ng).astype(np.int64) & 0xFFFFFFFF
+    p4 = np.asarray(q["packed_4bit"]).reshape(M, ng, 2).astype(np.int64) & 0xFFFFFFFF
+    i = np.arange(16)
+    code2 = (p2[:, :, None] >> (2 * i)) & 0x3
+    code4 = (np.where(i < 8, p4[:, :, 0:1], p4[:, :, 1:2]) >> (4 * (i & 7))) & 0xF
+    code = np.where(gp[None, :, None], code4, code2).astype(np.float32)
+    w = (s[:, :, None] * (code - z1[:, :, None]).astype(np.float32)).astype(np.float32)
+    out = w.astype(np.float16).reshape(M, ng * 16)[:, :K].copy()
+    if add_outliers:
+        rp = np.asarray(q["outlier_row_ptrs"]).reshape(-1)
+        cols = np.asarray(q["outlier_col_indices"]).reshape(-1)
+        vals = np.asarray(q["outlier_values"]).reshape(-1).astype(np.float16)
+        if vals.size:
+            rows = np.repeat(np.arange(M), np.diff(rp[:M + 1]))
+            out[rows, cols] = vals
+    return out
+
+
 def group_stats(w: np.ndarray, nthreads: int = 0):
     w = np.ascontiguousarray(w, dtype=np.float16)
     M, K = w.shape
