@@ -7,6 +7,7 @@ GROUP_SIZE_1ST / GROUP_SIZE_2ND) with bit-identical results.
 """
 __version__ = "0.1.0"
 
+from .checkpoint import load_quantized, save_quantized
 from .formats import GROUP_SIZE_1ST, GROUP_SIZE_2ND, QuantizedTensor
 from .ops import (dequantize, dequantize_2nd_order, pack_2bit, pack_4bit, quantize, unpack_2bit,
                   unpack_4bit)
@@ -22,4 +23,6 @@ __all__ = [
     "quantize",
     "dequantize",
     "dequantize_2nd_order",
+    "save_quantized",
+    "load_quantized",
 ]

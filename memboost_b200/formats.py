@@ -26,6 +26,9 @@ import torch
 GROUP_SIZE_1ST = 16   # columns per 1st-order group (memboost/formats.py:7)
 GROUP_SIZE_2ND = 256  # scales per 2nd-order group  (memboost/formats.py:8)
 
+# compact_state_dict(): packed arrays hold only each group's own words
+PACKED_LAYOUT_KEY = "packed_layout"
+
 _TENSOR_FIELDS = (
     "packed_2bit", "packed_4bit", "scales_1st", "zeros_1st", "scales_2nd", "zeros_2nd",
     "scales_1st_quant", "group_precision", "outlier_values", "outlier_col_indices",
@@ -132,6 +135,40 @@ class QuantizedTensor:
         d["K"] = torch.tensor(self.K)
         return d
 
+    def compact_state_dict(self) -> dict:
+        """state_dict() without the packed words of the other precision:
+        ``packed_2bit`` keeps the words of the 2-bit groups ([M, n2]) and
+        ``packed_4bit`` the two words of each 4-bit group ([M, 2 n4]), both in
+        group order, marked by ``packed_layout`` = 1.  The packed bytes are
+        the ones ``total_bytes`` counts; the omitted words are zero by
+        construction, so ``from_state_dict`` restores the arrays exactly."""
+        M, ng = self.M, self.num_groups
+        four = self.group_precision[:ng].to(torch.bool)
+        idx2 = torch.nonzero(~four).flatten()
+        idx4 = torch.nonzero(four).flatten()
+        d = self.state_dict()
+        d["packed_2bit"] = self.packed_2bit.reshape(M, ng).index_select(1, idx2).contiguous()
+        d["packed_4bit"] = (self.packed_4bit.reshape(M, ng, 2).index_select(1, idx4)
+                            .reshape(M, 2 * idx4.numel()).contiguous())
+        d[PACKED_LAYOUT_KEY] = torch.tensor(1)
+        return d
+
     @classmethod
     def from_state_dict(cls, d: dict) -> "QuantizedTensor":
-        return cls(**{f: d[f] for f in _TENSOR_FIELDS}, M=int(d["M"].item()), K=int(d["K"].item()))
+        """From ``state_dict()`` (the reference's keys) or
+        ``compact_state_dict()``."""
+        M, K = int(d["M"].item()), int(d["K"].item())
+        fields = {f: d[f] for f in _TENSOR_FIELDS}
+        if PACKED_LAYOUT_KEY in d and int(d[PACKED_LAYOUT_KEY].item()) == 1:
+            ng = (K + GROUP_SIZE_1ST - 1) // GROUP_SIZE_1ST
+            four = fields["group_precision"][:ng].to(torch.bool)
+            idx2 = torch.nonzero(~four).flatten()
+            idx4 = torch.nonzero(four).flatten()
+            dev = fields["packed_2bit"].device
+            p2 = torch.zeros((M, ng), dtype=torch.int32, device=dev)
+            p4 = torch.zeros((M, ng, 2), dtype=torch.int32, device=dev)
+            p2[:, idx2.to(dev)] = fields["packed_2bit"].reshape(M, idx2.numel())
+            p4[:, idx4.to(dev)] = fields["packed_4bit"].reshape(M, idx4.numel(), 2)
+            fields["packed_2bit"] = p2
+            fields["packed_4bit"] = p4.reshape(M, 2 * ng)
+        return cls(**fields, M=M, K=K)
