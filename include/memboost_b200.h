@@ -156,6 +156,21 @@ mb_status mb_dequantize_2nd(const int32_t* packed_2bit, const int32_t* packed_4b
                             mb_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * quantized GEMV -- no counterpart in the reference (it has no matmul over
+ * its format).  y[r] = sum_c W[r, c] * x[c] in fp32 (y: M floats, x: K fp16),
+ * W the reference dequantization of the codes (as mb_dequantize, per-element
+ * fp16 rounding) with each CSR outlier's exact value in place of its code's.
+ * outlier_row_ptrs [M + 1] is always read; col_indices / values [nnz] when
+ * nnz > 0 (entries past nnz or outside [0, K) are skipped).
+ * ------------------------------------------------------------------------- */
+mb_status mb_qgemv(const int32_t* packed_2bit, const int32_t* packed_4bit,
+                   const void* scales_1st_fp16, const int8_t* zeros_1st,
+                   const uint8_t* group_precision, const int32_t* outlier_row_ptrs,
+                   const int32_t* outlier_col_indices, const void* outlier_values_fp16,
+                   int64_t nnz, int64_t M, int64_t K, const void* x_fp16, float* y,
+                   mb_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * pack / unpack -- replace memboost::pack_2bit_op, unpack_2bit_op,
  * pack_4bit_op, unpack_4bit_op (core/torch_ops.h:10-15,
  * core/torch_ops.cu:20-102; bound in core/bindings.cpp:9-22).

@@ -41,6 +41,8 @@ _lib.mb_quantize_flags.argtypes = [_P, ctypes.c_size_t, _I64, _I64,
                                    ctypes.POINTER(ctypes.c_uint32), _P]
 _lib.mb_dequantize.restype = ctypes.c_int
 _lib.mb_dequantize.argtypes = [_P, _P, _P, _P, _P, _I64, _I64, _P, _P]
+_lib.mb_qgemv.restype = ctypes.c_int
+_lib.mb_qgemv.argtypes = [_P] * 8 + [_I64, _I64, _I64, _P, _P, _P]
 _lib.mb_dequantize_2nd.restype = ctypes.c_int
 _lib.mb_dequantize_2nd.argtypes = [_P] * 10 + [_I64, _I64, _I64, _P, _P]
 for _n in ("mb_pack_2bit", "mb_pack_4bit"):
@@ -313,6 +315,49 @@ def dequantize_2nd(packed_2bit: torch.Tensor, packed_4bit: torch.Tensor,
             out = torch.empty((M, K), dtype=torch.float16, device=dev)
         ptrs = [_ptr(a) for a in args] + [None] * (10 - len(args))
         _check(_lib.mb_dequantize_2nd(*ptrs, nnz, M, K, _ptr(out), _stream(dev)))
+    return out
+
+
+
+def qgemv(packed_2bit: torch.Tensor, packed_4bit: torch.Tensor, scales_1st: torch.Tensor,
+          zeros_1st: torch.Tensor, group_precision: torch.Tensor, outlier_row_ptrs: torch.Tensor,
+          outlier_col_indices: torch.Tensor, outlier_values: torch.Tensor, M: int, K: int,
+          x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """fp32 [M] = W x from the packed format (``mb_qgemv``); outliers with
+    their exact values (pass empty CSR values to leave them out)."""
+    if not packed_2bit.is_cuda:
+        raise RuntimeError("packed_2bit must be on CUDA")
+    M, K = int(M), int(K)
+    if M <= 0 or K <= 0:
+        raise RuntimeError("M and K must be positive")
+    dev = packed_2bit.device
+    ng = (K + GROUP_SIZE_1ST - 1) // GROUP_SIZE_1ST
+    nnz = int(outlier_values.numel())
+    expect = [(packed_2bit, torch.int32, M * ng, "packed_2bit"),
+              (packed_4bit, torch.int32, 2 * M * ng, "packed_4bit"),
+              (scales_1st, torch.float16, M * ng, "scales_1st"),
+              (zeros_1st, torch.int8, M * ng, "zeros_1st"),
+              (group_precision, torch.uint8, ng, "group_precision"),
+              (outlier_row_ptrs, torch.int32, M + 1, "outlier_row_ptrs"),
+              (outlier_col_indices, torch.int32, nnz, "outlier_col_indices"),
+              (outlier_values, torch.float16, nnz, "outlier_values"),
+              (x, torch.float16, K, "x")]
+    for t, dt, n, name in expect:
+        if t.device != dev:
+            raise RuntimeError(f"{name} must be on the same CUDA device as packed_2bit")
+        if t.dtype != dt:
+            raise RuntimeError(f"{name} must be {str(dt).replace('torch.', '')}")
+        if t.numel() < n:
+            raise RuntimeError(f"{name} too small for M={M}, K={K}")
+    with torch.cuda.device(dev):
+        args = [t.contiguous() for t, *_ in expect]
+        if out is None:
+            out = torch.empty((M,), dtype=torch.float32, device=dev)
+        elif out.dtype != torch.float32 or out.numel() < M or not out.is_contiguous():
+            raise RuntimeError("out must be a contiguous float32 tensor of at least M values")
+        p = [_ptr(a) for a in args]
+        _check(_lib.mb_qgemv(*p[:6], p[6] if nnz else None, p[7] if nnz else None, nnz, M, K,
+                             p[8], _ptr(out), _stream(dev)))
     return out
 
 

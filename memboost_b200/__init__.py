@@ -9,8 +9,8 @@ __version__ = "0.1.0"
 
 from .checkpoint import load_quantized, save_quantized
 from .formats import GROUP_SIZE_1ST, GROUP_SIZE_2ND, QuantizedTensor
-from .ops import (dequantize, dequantize_2nd_order, pack_2bit, pack_4bit, quantize, unpack_2bit,
-                  unpack_4bit)
+from .ops import (dequantize, dequantize_2nd_order, pack_2bit, pack_4bit, qgemv, quantize,
+                  unpack_2bit, unpack_4bit)
 
 __all__ = [
     "QuantizedTensor",
@@ -25,4 +25,5 @@ __all__ = [
     "dequantize_2nd_order",
     "save_quantized",
     "load_quantized",
+    "qgemv",
 ]

@@ -75,3 +75,16 @@ def dequantize_2nd_order(qtensor: QuantizedTensor, add_outliers: bool = True,
         qtensor.zeros_2nd, qtensor.zeros_1st, qtensor.group_precision, qtensor.M, qtensor.K,
         qtensor.outlier_row_ptrs if nnz else None, qtensor.outlier_col_indices if nnz else None,
         qtensor.outlier_values if nnz else None, out)
+
+
+def qgemv(qtensor: QuantizedTensor, x: torch.Tensor, add_outliers: bool = True,
+          out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """fp32 [M] = W x straight from the packed format: W as ``dequantize``
+    gives it, and with ``add_outliers`` every outlier's exact value in place
+    of its code's.  The matrix is never expanded in memory.  The reference
+    has no matmul over its format."""
+    vals = qtensor.outlier_values if add_outliers else qtensor.outlier_values[:0]
+    cols = qtensor.outlier_col_indices if add_outliers else qtensor.outlier_col_indices[:0]
+    return _C.qgemv(qtensor.packed_2bit, qtensor.packed_4bit, qtensor.scales_1st,
+                    qtensor.zeros_1st, qtensor.group_precision, qtensor.outlier_row_ptrs, cols,
+                    vals, qtensor.M, qtensor.K, x.reshape(-1), out)
