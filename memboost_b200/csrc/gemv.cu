@@ -10,6 +10,14 @@
 // One warp per row, lanes over the row's 16-column groups; then the row's
 // outliers replace their codes' contributions (exact value minus decoded
 // value, times x); a warp sum gives y[r].
+//
+// The weights are decoded two at a time in fp16 with the reference's result:
+// q - zero is an integer of at most 143 in magnitude (exact in fp16, formed
+// as (1024 + q) - (1024 + zero) from bit patterns), and scale * (q - zero)
+// has at most 19 significant bits, so it is exact in fp32 and the
+// reference's fp32 product rounded to fp16 equals one fp16 multiply.  Each
+// product w * x is exact in fp32 and added with a single rounding
+// (fma.rn.f32.f16), as fmaf on the converted values would.
 #include "mb_common.cuh"
 
 namespace mb {
@@ -36,6 +44,33 @@ __device__ __forceinline__ void load_group(const int32_t* __restrict__ packed2,
   }
 }
 
+// acc += lo(w) * lo(x) + hi(w) * hi(x) (two fp32 FMAs, fp16 operands)
+__device__ __forceinline__ void fma2_f16(uint32_t w, uint32_t x, float& acc) {
+  asm("{\n\t.reg .b16 wl, wh, xl, xh;\n\t"
+      "mov.b32 {wl, wh}, %1;\n\tmov.b32 {xl, xh}, %2;\n\t"
+      "fma.rn.f32.f16 %0, wl, xl, %0;\n\tfma.rn.f32.f16 %0, wh, xh, %0;\n\t}"
+      : "+f"(acc)
+      : "r"(w), "r"(x));
+}
+
+// Weights 2k and 2k + 1 of a group as fp16 pairs: codes from the packed
+// word(s) as 1024 + q, minus 1024 + zero (zh2), times the scale (sh2).
+__device__ __forceinline__ uint32_t decode_pair(uint32_t wa, uint32_t wb, bool four, int k,
+                                                __half2 zh2, __half2 sh2) {
+  uint32_t t, c;
+  if (four) {
+    t = (k < 4 ? wa : wb) >> (8 * (k & 3));
+    c = (t & 0xFu) | ((t << 12) & 0xF0000u);
+  } else {
+    t = wa >> (4 * k);
+    c = (t & 0x3u) | ((t << 14) & 0x30000u);
+  }
+  const uint32_t h = 0x64006400u | c;
+  const __half2 d = __hsub2(*reinterpret_cast<const __half2*>(&h), zh2);
+  const __half2 w = __hmul2(d, sh2);
+  return *reinterpret_cast<const uint32_t*>(&w);
+}
+
 __global__ void __launch_bounds__(256)
     qgemv_kernel(const int32_t* __restrict__ packed2, const int32_t* __restrict__ packed4,
                  const __half* __restrict__ scales1, const int8_t* __restrict__ zeros1,
@@ -52,27 +87,33 @@ __global__ void __launch_bounds__(256)
     const bool four = gp[g] != 0;
     uint32_t wa, wb;
     load_group(packed2, packed4, four, si, wa, wb);
-    const float scale = __half2float(scales1[si]);
-    const float zf = (float)(int)zeros1[si];
+    const __half sc = scales1[si];
+    const __half2 sh2 = __halves2half2(sc, sc);
+    const __half zh = __int2half_rn(1024 + (int)zeros1[si]);  // exact: 896 .. 1151
+    const __half2 zh2 = __halves2half2(zh, zh);
     const int64_t c0 = (int64_t)g * kGroup1;
     const int gs = (int)min64(kGroup1, K - c0);
-    float xv[16];
+    uint32_t xw[8];
     if (x_vec && gs == kGroup1) {
       const uint4 a = reinterpret_cast<const uint4*>(x + c0)[0];
       const uint4 b = reinterpret_cast<const uint4*>(x + c0)[1];
-      const uint32_t h[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+      xw[0] = a.x; xw[1] = a.y; xw[2] = a.z; xw[3] = a.w;
+      xw[4] = b.x; xw[5] = b.y; xw[6] = b.z; xw[7] = b.w;
+    } else {  // a partial group or an unaligned x: x = 0 past K
+      const uint16_t* xs = reinterpret_cast<const uint16_t*>(x) + c0;
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        xv[2 * k] = __half2float(__ushort_as_half((uint16_t)(h[k] & 0xFFFFu)));
-        xv[2 * k + 1] = __half2float(__ushort_as_half((uint16_t)(h[k] >> 16)));
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 16; ++i) xv[i] = i < gs ? __half2float(x[c0 + i]) : 0.0f;
+      for (int k = 0; k < 8; ++k)
+        xw[k] = (2 * k < gs ? (uint32_t)xs[2 * k] : 0u) |
+                (2 * k + 1 < gs ? (uint32_t)xs[2 * k + 1] << 16 : 0u);
     }
 #pragma unroll
-    for (int i = 0; i < 16; ++i)
-      if (i < gs) acc = fmaf(decode_one(wa, wb, four, scale, zf, i), xv[i], acc);
+    for (int k = 0; k < 8; ++k) {
+      uint32_t w = decode_pair(wa, wb, four, k, zh2, sh2);
+      // weights past K: 0 (a non-finite weight times x = 0 would give NaN)
+      if (2 * k >= gs) w &= 0xFFFF0000u;
+      if (2 * k + 1 >= gs) w &= 0x0000FFFFu;
+      fma2_f16(w, xw[k], acc);
+    }
   }
   // the row's outliers: their exact values in place of the decoded ones
   const int64_t j0 = max64(0, row_ptrs[r]), j1 = min64(nnz, row_ptrs[r + 1]);
