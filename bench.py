@@ -1,33 +1,45 @@
 #!/usr/bin/env python
-"""Benchmark: memboost quantize throughput on B200 (FP16 GB/s ingested).
+"""Benchmark: memboost quantize throughput on B200 (FP16 GB/s quantized).
 
-One step = quantize the Llama-7B MLP-shaped pair (11008x4096 and 4096x11008
-fp16, N(0, 0.02^2) with 0.05% Student-t(3) outliers, lognormal(0, 1.5)
-hessian_diag, ratio_4bit 0.1) -- synthetic, seeded, generated on the CPU.
-At N GPUs every rank quantizes its own copy (weak scaling, no collective on
-the data path); rank 0 prints one JSON line.
+One step = quantize the whole Llama-2-7B-shaped model: 32 layers x {q, k, v,
+o 4096x4096, gate / up 11008x4096, down 4096x11008}, 224 matrices, 12.95 GB
+of fp16, N(0, 0.02^2) weights, lognormal(0, 1.5) hessian_diag per matrix,
+ratio_4bit 0.1 -- synthetic and seeded (no checkpoint exists here), drawn on
+the GPU.  At N GPUs the 224 matrices are split over the ranks by size
+(longest-processing-time first, memboost_b200.shard.lpt_partition): strong
+scaling, no collective on the data path; the step time is the max over
+ranks.  Rank 0 prints one JSON line.
 
-  value      device-resident throughput: inputs already in HBM, the
-             QuantizePlan path (launch both matrices, read their outlier
-             counts, CSR extract); step k + 1 is enqueued before step k is
-             finished, so host work overlaps the GPU
+  value      device-resident throughput: every matrix of this rank's share
+             quantized by one CUDA-graph replay of its launches
+             (memboost_b200._C.QuantizeBatch: stats, tables, encode and the
+             CSR extraction chained on the device, 4 graph branches); step
+             k + 1 is enqueued before step k's outlier counts are read
   e2e        the public memboost_b200.quantize() call per matrix with host
              buffers: pinned H2D copy of the weights and hessian, quantize,
              D2H of every output tensor, inside the timed region
-  roofline   algorithmic bytes of a step's quantize calls (3.0 B per weight
-             plus hessian, 2nd-order, CSR and precision bytes) / the device
-             time per step, against MEASURED_PEAKS.json; traffic = DRAM bytes
-             per call from the committed ncu summary
+  roofline   algorithmic bytes of the step's quantize calls (3.0 B per weight
+             plus hessian, 2nd-order, CSR and precision bytes) / device time
+             per step, against MEASURED_PEAKS.json
   cpu_baseline  the CPU oracle (C++ restatement of the reference algorithm)
-             on all host cores, on the same matrices
+             on all host cores, on row slices of the model's first layer
+  sub-records (one GPU only): mlp_pair (the Llama-7B MLP pair 11008x4096 +
+             4096x11008 with Student-t outliers, every plan on a stream of its
+             own), single_4096 (4096x4096 quantize + dequantize, hessian
+             ones), gptq_layer (one Llama-7B layer's GPTQ on 262144
+             calibration tokens: s/layer and the tensor-core Hessian's
+             TFLOP/s)
 
 --impl reference times the reference algorithm on the host cores (the
-oracle port) for the same workload and, when the reference's own extension
-is built in oracle/_ref, its CUDA kernels on this GPU.
+oracle port, rank 0 only) on row slices of the same model, and -- as context
+-- the reference's own CUDA kernels (oracle/_ref, built from its sources) on
+the model's first layer, and its GPTQ layer loop restated in torch ops on
+the GPU.  That arm loads nothing of memboost_b200's native library.
 """
 from __future__ import annotations
 
 import argparse
+import importlib.util
 import json
 import os
 import statistics
@@ -39,19 +51,41 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-METRIC = "FP16 GB/s quantized (Llama-7B MLP pair 11008x4096 + 4096x11008)"
+METRIC = "FP16 GB/s quantized (whole Llama-2-7B-shaped model, 224 matrices)"
 UNIT = "GB/s"
+WORKLOAD = ("llama2_7b model: 32 layers x {q,k,v,o 4096x4096, gate/up 11008x4096, "
+            "down 4096x11008} fp16 N(0,0.02^2), 224 matrices, 12.95 GB; hessian_diag "
+            "lognormal(0,1.5) per matrix; ratio_4bit 0.1; 16-col groups; matrices split over "
+            "ranks by size (LPT)")
+
+# DRAM read + write per quantize call of a 4096x11008 / 11008x4096 matrix
+# (ncu, one pipelined step of the MLP pair, L2 kept between kernels), as
+# summarised in profiles/quantize_mlp7b_launches.md: the measured traffic the
+# roofline's algorithmic bytes are compared with.
+TRAFFIC_PER_CALL_MLP7B = 197_200_000
 
 
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=1000)
+    p.add_argument("--steps", type=int, default=100)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    p.add_argument("--e2e-steps", type=int, default=5)
+    p.add_argument("--e2e-steps", type=int, default=2)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-sub", action="store_true", help="skip the one-GPU sub-records")
+    p.add_argument("--layers", type=int, default=32, help="model layers (32 = the config)")
     return p.parse_args()
+
+
+def load_workloads():
+    """memboost_b200/workloads.py loaded by path: importing the package would
+    load its native library, which the reference arm must not."""
+    spec = importlib.util.spec_from_file_location(
+        "mb_workloads", os.path.join(ROOT, "memboost_b200", "workloads.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
 
 
 def dist_setup():
@@ -78,8 +112,11 @@ def barrier(ws):
 def max_over_ranks(ws, x: float) -> float:
     if ws == 1:
         return x
-    from memboost_b200 import shard
-    return shard.max_over_ranks(x)
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
 
 
 _SAMPLER = r"""
@@ -95,7 +132,6 @@ try:
 except Exception as e:
     print("error", type(e).__name__, str(e).replace(chr(10), " ")[:120], flush=True)
     sys.exit(0)
-print("ready", flush=True)
 def reasons():
     for f in ("nvmlDeviceGetCurrentClocksEventReasons", "nvmlDeviceGetCurrentClocksThrottleReasons"):
         try:
@@ -103,6 +139,7 @@ def reasons():
         except Exception:
             pass
     return 0
+first = True
 while True:
     t = time.time()
     try:
@@ -112,6 +149,9 @@ while True:
         except Exception:
             pw = -1.0
         print(t, sm, mx, reasons(), pw, flush=True)
+        if first:
+            print("ready", flush=True)
+            first = False
     except Exception:
         pass
     time.sleep(float(sys.argv[2]))
@@ -120,11 +160,12 @@ while True:
 
 class ClockSampler:
     """Samples this GPU's SM clock, throttle reasons and power through NVML
-    every ~5 ms (read-only queries) from a separate process, and reports the
-    samples taken inside the timed window (``mark_start`` / ``mark_end``;
-    the nearest one if the window is shorter than the period).  NVML queries
-    slow the launching process down measurably at millisecond periods, hence
-    the longer one."""
+    every ~5 ms (read-only queries) from a separate process, started before
+    the warm-up and ready once its first sample is in.  Reports the samples
+    taken inside the timed window (``mark_start`` / ``mark_end``), or the
+    nearest ones if the window is shorter than the period.  NVML queries slow
+    the launching process down measurably at millisecond periods, hence the
+    longer one."""
 
     PERIOD_S = 0.005
 
@@ -135,6 +176,9 @@ class ClockSampler:
         self.samples = []
         self.proc = None
         self.why = ""
+        self.in_window = 0
+        self.lines = []
+        self.t_start = self.t_end = time.time()
         try:
             import subprocess
 
@@ -149,18 +193,20 @@ class ClockSampler:
                                           str(self.PERIOD_S), str(nvml_index)],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
                                          text=True)
-            first = self.proc.stdout.readline().strip()
-            if first != "ready":
-                self.why = first or "sampler exited"
-                self.proc.kill()
-                self.proc = None
+            # the first sample, then "ready"
+            for _ in range(3):
+                line = self.proc.stdout.readline().strip()
+                if line == "ready":
+                    break
+                if not line or line.startswith("error"):
+                    self.why = line or "sampler exited"
+                    self.proc.kill()
+                    self.proc = None
+                    break
+                self.lines.append(line)
         except Exception as e:
             self.why = f"{type(e).__name__}: {e}"[:120]
             self.proc = None
-
-    def __enter__(self):
-        self.t_start = self.t_end = time.time()
-        return self
 
     def mark_start(self):
         self.t_start = time.time()
@@ -168,18 +214,19 @@ class ClockSampler:
     def mark_end(self):
         self.t_end = time.time()
 
-    def __exit__(self, *exc):
+    def stop(self):
         if self.proc is None:
             return
-        time.sleep(2 * self.PERIOD_S)  # a sample after the window, for short windows
+        time.sleep(3 * self.PERIOD_S)  # samples after the window, for short windows
         self.proc.terminate()
         try:
             out, _ = self.proc.communicate(timeout=5)
         except Exception:
             self.proc.kill()
             out, _ = self.proc.communicate()
+        self.proc = None
         allsamp = []
-        for line in out.splitlines():
+        for line in self.lines + out.splitlines():
             try:
                 t, sm, mx, rs, pw = line.split()
                 allsamp.append((float(t), int(sm), int(mx), int(rs), float(pw)))
@@ -187,23 +234,25 @@ class ClockSampler:
                 pass
         inside = [x for x in allsamp if self.t_start <= x[0] <= self.t_end]
         self.in_window = len(inside)
-        if not inside and allsamp:  # window shorter than the period: the nearest sample
+        if not inside and allsamp:  # window shorter than the period: the nearest samples
             mid = 0.5 * (self.t_start + self.t_end)
-            inside = [min(allsamp, key=lambda x: abs(x[0] - mid))]
+            inside = sorted(allsamp, key=lambda x: abs(x[0] - mid))[:3]
         self.samples = [x[1:] for x in inside]
+        if not self.samples and not self.why:
+            self.why = "sampler returned no samples"
 
     def summary(self) -> dict:
         if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"],
-                    "why": self.why or "no sample"}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [],
+                    "unsampled_why": self.why or "no sample"}
         reasons = sorted({n for (_, _, r, _) in self.samples for n, bit in self.REASONS.items()
                           if r & bit})
         return {"sm_mhz": statistics.median(s[0] for s in self.samples),
                 "sm_max_mhz": max(s[1] for s in self.samples),
                 "power_w_max": round(max(s[3] for s in self.samples), 1),
                 "samples": len(self.samples), "samples_in_window": self.in_window,
-                "source": "NVML every ~5 ms from a separate process, samples inside the "
-                          "timed window (else the nearest)",
+                "source": "NVML every ~5 ms from a separate process started before the "
+                          "warm-up; samples inside the timed window (else the 3 nearest)",
                 "reasons": reasons}
 
 
@@ -211,21 +260,9 @@ def peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
         d = json.load(open(path))
-        return float(d["hbm_gbs"]), "measured"
-    return 6650.0, "fallback"
-
-
-def profiled_traffic():
-    """DRAM bytes (read + write) of one quantize call of the benchmark pair,
-    from the committed ncu summary (a number, not a measurement of this run)."""
-    path = os.path.join(ROOT, "profiles", "quantize_mlp7b_launches.md")
-    try:
-        for line in open(path):
-            if line.startswith("traffic_bytes_per_call:"):
-                return int(line.split(":", 1)[1])
-    except OSError:
-        pass
-    return None
+        return d, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, \
+        "fallback"
 
 
 def algorithmic_bytes(M: int, K: int, nnz: int, selecting: bool) -> int:
@@ -240,285 +277,555 @@ def algorithmic_bytes(M: int, K: int, nnz: int, selecting: bool) -> int:
             + 6 * nnz + 4 * (M + 1) + ng)
 
 
-def cpu_baseline(cases, min_seconds=10.0):
-    from oracle import oracle
-    oracle.build()
-    n, t0 = 0, time.perf_counter()
-    nbytes = 0
+def dequant_bytes(M: int, K: int, n4: int) -> int:
+    """Compulsory HBM bytes of one dequantize: the selected code words
+    (4 B per 2-bit and 8 B per 4-bit (row, group)), fp16 scale and int8 zero
+    per (row, group), group precision, and the fp16 output."""
+    ng = (K + 15) // 16
+    return M * (4 * (ng - n4) + 8 * n4) + M * ng * 3 + ng + 2 * M * K
+
+
+def model_shapes(layers: int, wl):
+    return [(name, M, K, wl.llama7b_model_seed(i))
+            for i, (name, M, K) in enumerate(wl.llama7b_shapes(layers))]
+
+
+def cpu_sample(wl, layers_shapes, device, min_rows: int = 256, frac: float = 1.0 / 16):
+    """Row slices (about ``frac`` of the rows) of the first layer's seven
+    matrices of the model workload, drawn on ``device`` with the model's seeds
+    and copied to host memory: the CPU arms' bounded sample."""
+    out = []
+    for name, M, K, seed in layers_shapes[:7]:
+        c = wl.llama7b_matrix(name, M, K, seed, device=device)
+        r = max(min_rows, int(M * frac))
+        out.append((name, c.weights[:r].cpu().numpy(), c.hessian_diag.cpu().numpy(),
+                    c.ratio_4bit))
+    return out
+
+
+def time_oracle(oracle, sample, seconds: float):
+    """Repeats the oracle over the sample for about ``seconds``; GB/s of fp16."""
+    n, nbytes, t0 = 0, 0, time.perf_counter()
     while True:
-        for c in cases:
-            oracle.quantize(c.weights.numpy(), c.ratio_4bit, c.hessian_diag.numpy(), nthreads=0)
-            nbytes += 2 * c.weights.numel()
+        for _, w, h, r in sample:
+            oracle.quantize(w, r, h, nthreads=0)
+            nbytes += 2 * w.size
         n += 1
         el = time.perf_counter() - t0
-        if el >= min_seconds or n >= 50:
-            break
-    return {"value": round(nbytes / el / 1e9, 4), "unit": UNIT, "cores": os.cpu_count(),
-            "kind": "port",
-            "sample": f"oracle/mb_oracle.cpp on {os.cpu_count()} host threads, {n} x the "
-                      f"full pair ({'+'.join(c.name for c in cases)}), {el:.1f} s"}
+        if el >= seconds or n >= 200:
+            return nbytes / el / 1e9, n, el
 
+
+def cpu_baseline(wl, shapes, device, seconds=12.0):
+    from oracle import oracle
+    oracle.build()
+    sample = cpu_sample(wl, shapes, device)
+    v, n, el = time_oracle(oracle, sample, seconds)
+    rows = {name: w.shape[0] for name, w, _, _ in sample}
+    return {"value": round(v, 4), "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+            "sample": f"oracle/mb_oracle.cpp (C++ restatement of the reference algorithm) on "
+                      f"{os.cpu_count()} host threads, {n} passes over row slices of layer 0 "
+                      f"({rows}), {el:.1f} s"}
+
+
+# ---------------------------------------------------------------------------
+# the main line: the whole model, sharded by matrix
+# ---------------------------------------------------------------------------
 
 def run_ours(args, ws, rank, local):
     import torch
 
     import memboost_b200 as mb
-    from memboost_b200 import _C, workloads
+    from memboost_b200 import _C, shard
+    from memboost_b200 import workloads as wl
 
     dev = torch.device("cuda", local)
-    cases = workloads.mlp_7b()
-    W = [c.weights.to(dev) for c in cases]
-    H = [c.hessian_diag.to(dev) for c in cases]
-    # two sets of plans: step k + 1 is enqueued before step k is finished
-    # (its outlier count read and CSR extracted), so the GPU does not idle
-    # while the host works; every step's outputs are complete inside the
-    # timed region.  Every plan has a stream of its own (two matrices x two
-    # sets): the matrices are independent, so one call's latency-bound
-    # selection tail overlaps other calls' streaming kernels, including the
-    # next step's, which would otherwise queue behind it on a shared stream.
-    stream_sets = [[torch.cuda.Stream(dev) for _ in W] for _ in range(2)]
-    streams = [st for ss in stream_sets for st in ss]
-    plan_sets = [[_C.QuantizePlan(*w.shape, dev, stream=st) for w, st in zip(W, ss)]
-                 for ss in stream_sets]
-    fp16_bytes = sum(2 * w.numel() for w in W)
-    nnz_seen = []
+    clk = ClockSampler(local)
+    shapes = model_shapes(args.layers, wl)
+    mine = shard.lpt_partition([M * K for _, M, K, _ in shapes], ws)[rank]
+    cases = [wl.llama7b_matrix(shapes[i][0], shapes[i][1], shapes[i][2], shapes[i][3],
+                               device=dev) for i in mine]
+    batch = _C.QuantizeBatch([c.weights for c in cases], [c.ratio_4bit for c in cases],
+                             [c.hessian_diag for c in cases], dev, branches=4)
+    del cases
+    fp16_bytes = sum(2 * M * K for (M, K) in batch.shapes)
+    batch.capture()
 
-    def launch_step(k, ev=None):
-        for i, (p, w, h, c) in enumerate(zip(plan_sets[k % 2], W, H, cases)):
-            if ev is not None:
-                p.record_on(ev[i][0])
-            p.launch(w, c.ratio_4bit, h)
-            if ev is not None:
-                p.record_on(ev[i][1])
+    ev = [torch.cuda.Event() for _ in range(2)]
+    last = {}
 
-    def finish_step(k):
-        res = [p.finish() for p in plan_sets[k % 2]]
-        nnz_seen.append([int(r[8].numel()) for r in res])
-
-    def run_steps(n, events=None):
+    def run_steps(n):
         for k in range(n):
-            launch_step(k, None if events is None else events[k])
+            batch.launch()
+            ev[k % 2].record()
             if k > 0:
-                finish_step(k - 1)
-        finish_step(n - 1)
+                ev[(k - 1) % 2].synchronize()
+                last["nnz"] = batch.nnz_host.tolist()
+        ev[(n - 1) % 2].synchronize()
+        res = batch.finish()
+        last["nnz"] = [int(r[8].numel()) for r in res]
 
     run_steps(max(args.warmup, 3))
     torch.cuda.synchronize()
-    per_call = [[] for _ in W]
-    events = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in W]
-              for _ in range(min(args.steps, 5))]
     barrier(ws)
     torch.cuda.synchronize()
-    with ClockSampler(local) as clk:
-        t0 = torch.cuda.Event(enable_timing=True)
-        t1 = torch.cuda.Event(enable_timing=True)
-        clk.mark_start()
-        t0.record()
-        for st in streams:  # the plans' streams start after t0 ...
-            st.wait_event(t0)
-        run_steps(args.steps)
-        for st in streams:  # ... and t1 follows all of their work
-            torch.cuda.current_stream(dev).wait_stream(st)
-        t1.record()
-        torch.cuda.synchronize()
-        clk.mark_end()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    clk.mark_start()
+    t0.record()
+    run_steps(args.steps)
+    t1.record()
+    torch.cuda.synchronize()
+    clk.mark_end()
     barrier(ws)
     ms_local = t0.elapsed_time(t1)
     ms = max_over_ranks(ws, ms_local)
-    # per-call durations (informational), in an untimed pass of their own:
-    # the events between launches cost host time
-    n_ev = min(args.steps, 5)
-    run_steps(n_ev, events)
-    torch.cuda.synchronize()
-    for k in range(n_ev):
-        for i in range(len(W)):
-            per_call[i].append(events[k][i][0].elapsed_time(events[k][i][1]))
-    value = fp16_bytes * args.steps * ws / (ms / 1e3) / 1e9
+    total_fp16 = sum(2 * M * K for _, M, K, _ in shapes)  # every rank's share together
+    value = total_fp16 * args.steps / (ms / 1e3) / 1e9
 
-    # roofline of the quantize path: the algorithmic bytes of a step's calls
-    # over the device time per step (the two calls overlap on their streams;
-    # call_ms, each call from its first to its last kernel, is informational)
-    peak, peak_kind = peaks()
-    nnz = nnz_seen[-1]
-    alg = [algorithmic_bytes(*w.shape, n, True) for w, n in zip(W, nnz)]
-    dur = [statistics.mean(x) for x in per_call]
-    achieved = sum(alg) / (ms / args.steps / 1e3) / 1e9
-    # stats (+selection), exact (tables), encode per matrix; extract when the
-    # matrix has outliers
-    launches_per_step = sum(3 + (1 if n > 0 else 0) for n in nnz)
+    pk, peak_kind = peaks()
+    hbm = float(pk["hbm_gbs"])
+    nnz = last["nnz"]
+    alg_local = sum(algorithmic_bytes(M, K, n, True) for (M, K), n in zip(batch.shapes, nnz))
+    alg_all = alg_local
+    if ws > 1:
+        import torch.distributed as dist
+        t = torch.tensor([float(alg_local)], dtype=torch.float64, device=dev)
+        dist.all_reduce(t)
+        alg_all = float(t.item())
+    achieved = alg_all / (ms / args.steps / 1e3) / 1e9  # whole job
+    achieved_rank = alg_local / (ms_local / args.steps / 1e3) / 1e9
+    launches_per_step = 4 * len(batch.shapes)  # stats, exact, encode, extract per matrix
 
-    # e2e: public API, host buffers, copies in the timed region.  Each matrix
-    # has a stream of its own: its upload, quantize() (which reads the
-    # outlier count, waiting for that stream only) and the download of every
-    # output into pinned host buffers; one matrix's download overlaps the
-    # other's upload (the link is full duplex).  The step's outputs are all
-    # on the host when the step's final synchronisation returns.
+    # e2e: the public API per matrix, host buffers, copies in the timed region
     e2e = None
     if args.e2e_steps > 0:
-        hw = [c.weights.pin_memory() for c in cases]
-        hh = [c.hessian_diag.pin_memory() for c in cases]
-        h2d = sum(t.numel() * t.element_size() for t in hw + hh)
-        e_streams = [torch.cuda.Stream(dev) for _ in cases]
-        host_out = [dict() for _ in cases]  # pinned destinations, by state_dict key
-        d2h_holder = {}
-
-        def e2e_step(sync=True):
-            # both uploads first: the link stays busy while quantize() waits
-            # for a matrix's outlier count
-            dev_in = []
-            for wh, hhh, st in zip(hw, hh, e_streams):
-                with torch.cuda.stream(st):
-                    dev_in.append((wh.to(dev, non_blocking=True),
-                                   hhh.to(dev, non_blocking=True)))
-            for i, ((wd, hd), c, st) in enumerate(zip(dev_in, cases, e_streams)):
-                with torch.cuda.stream(st):
-                    qt = mb.quantize(wd, c.ratio_4bit, hd)
-                    for k, v in qt.state_dict().items():
-                        if not (isinstance(v, torch.Tensor) and v.is_cuda):
-                            continue
-                        dst = host_out[i].get(k)
-                        if dst is None or dst.shape != v.shape:
-                            dst = torch.empty(v.shape, dtype=v.dtype).pin_memory()
-                            host_out[i][k] = dst
-                        dst.copy_(v, non_blocking=True)
-                    wd.record_stream(st)
-            if sync:
-                torch.cuda.synchronize()
-            d2h_holder["bytes"] = sum(v.numel() * v.element_size() for d in host_out
-                                      for v in d.values())
-
-        for _ in range(2):
-            e2e_step()
-        barrier(ws)
-        torch.cuda.synchronize()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for st in e_streams:
-            st.wait_event(e0)
-        for k in range(args.e2e_steps):
-            # step k's downloads overlap step k+1's uploads; the final
-            # synchronisation completes every step
-            e2e_step(sync=k == args.e2e_steps - 1)
-        for st in e_streams:
-            torch.cuda.current_stream(dev).wait_stream(st)
-        e1.record()
-        torch.cuda.synchronize()
-        ems = max_over_ranks(ws, e0.elapsed_time(e1))
-        e2e = {"value": round(fp16_bytes * args.e2e_steps * ws / (ems / 1e3) / 1e9, 3),
-               "unit": UNIT, "h2d_bytes_per_step": h2d,
-               "d2h_bytes_per_step": d2h_holder["bytes"], "steps": args.e2e_steps,
-               "ms_per_step": round(ems / args.e2e_steps, 3),
-               "path": "memboost_b200.quantize() per matrix (C ABI), pinned host buffers, "
-                       "one stream per matrix"}
+        e2e = run_e2e(args, ws, dev, batch, fp16_bytes, total_fp16)
+    clk.stop()
 
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16->u8/i32",
-        "data": "synthetic (seeded N(0,0.02^2) + Student-t(3) outliers, lognormal hessian)",
-        "config": {"workload": "mlp_7b pair: 11008x4096 + 4096x11008 fp16, ratio_4bit 0.1, "
-                               "hessian_diag lognormal(0,1.5), 16-col groups",
-                   "per_rank_fp16_bytes": fp16_bytes,
-                   "l2": "per-step inputs 180 MB > 126 MB L2; not flushed",
-                   "parallelism": f"{ws} independent ranks (weak scaling)"},
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
-                     "unit": "GB/s", "frac": round(achieved / peak, 4),
-                     "peak_kind": peak_kind, "traffic": profiled_traffic(),
-                     "traffic_source": "profiles/quantize_mlp7b_launches.md (ncu, one "
-                                       "pipelined step, DRAM read+write per call)",
-                     "kernel": "quantize calls of a step: stats (+group parameters and "
-                               "selection), exact/tables, encode (+row pointers) -- 3 kernels "
-                               "chained with PDL per matrix, every plan on a stream of its own "
-                               "(2 matrices x 2 step sets); "
-                               "device time per step",
-                     "algorithmic_bytes_per_call": alg,
-                     "call_ms": [round(d, 4) for d in dur]},
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "fp16->u8/i32",
+        "data": "synthetic (seeded N(0,0.02^2) weights, lognormal(0,1.5) hessian, drawn on the "
+                "GPU; no checkpoint)",
+        "config": {"workload": WORKLOAD, "layers": args.layers, "matrices": len(shapes),
+                   "fp16_bytes": total_fp16, "rank0_matrices": len(batch.shapes),
+                   "rank0_fp16_bytes": fp16_bytes,
+                   "l2": "per-step inputs 12.95 GB (1.6 GB per rank at 8) > 126 MB L2; "
+                         "not flushed",
+                   "parallelism": f"{ws} ranks, matrices split by size (LPT), no collective on "
+                                  "the data path"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved / ws, 1), "peak": hbm,
+                     "unit": "GB/s", "frac": round(achieved / ws / hbm, 4),
+                     "peak_kind": peak_kind, "of": f"{peak_kind} hbm_gbs per GPU",
+                     "traffic": TRAFFIC_PER_CALL_MLP7B,
+                     "traffic_what": "DRAM read+write of one 4096x11008 quantize call (ncu, "
+                                     "profiles/quantize_mlp7b_launches.md) against "
+                                     f"{algorithmic_bytes(4096, 11008, 0, True)} algorithmic "
+                                     "bytes",
+                     "kernel": "the quantize calls of a step (stats, exact/tables, encode, "
+                               "extract per matrix, chained with PDL, 4 graph branches): "
+                               "algorithmic bytes of the whole job per GPU / device time per "
+                               "step (max over ranks)",
+                     "algorithmic_bytes_per_step": int(alg_all),
+                     "rank0_achieved": round(achieved_rank, 1)},
         "gpu_launches": launches_per_step * args.steps,
-        "nnz": nnz,
+        "gpu_launches_what": "rank 0: 4 kernels per matrix per step",
+        "nnz_rank0": int(sum(nnz)),
         "clocks": clk.summary(),
     }
     if e2e:
         line["e2e"] = e2e
-    return line, cases
+    return line, shapes, wl
 
 
-def run_reference_arm(args, ws, rank, local):
-    """Reference algorithm on the host cores (oracle port) + the reference's
-    own CUDA kernels on this GPU when built in oracle/_ref."""
+def run_e2e(args, ws, dev, batch, fp16_bytes, total_fp16):
+    """memboost_b200.quantize() per matrix of this rank's share with host
+    buffers: upload (pinned), quantize, download of every output into pinned
+    buffers, all inside the timed region; two streams alternate so one
+    matrix's download overlaps the next one's upload."""
     import torch
 
-    from memboost_b200 import workloads
-    from oracle import oracle
+    import memboost_b200 as mb
+    hw = [w.cpu().pin_memory() for w in batch.weights]
+    hh = [h.cpu().pin_memory() if h is not None else None for h in batch.hess]
+    h2d = sum(t.numel() * t.element_size() for t in hw) + \
+        sum(t.numel() * t.element_size() for t in hh if t is not None)
+    streams = [torch.cuda.Stream(dev) for _ in range(2)]
+    host_out = [dict() for _ in hw]
+    d2h = {"b": 0}
 
+    def step():
+        nb = 0
+        for i, (w, h) in enumerate(zip(hw, hh)):
+            st = streams[i % 2]
+            with torch.cuda.stream(st):
+                wd = w.to(dev, non_blocking=True)
+                hd = h.to(dev, non_blocking=True) if h is not None else None
+                qt = mb.quantize(wd, batch.ratios[i], hd)
+                for k, v in qt.state_dict().items():
+                    if not (isinstance(v, torch.Tensor) and v.is_cuda):
+                        continue
+                    dst = host_out[i].get(k)
+                    if dst is None or dst.shape != v.shape:
+                        dst = torch.empty(v.shape, dtype=v.dtype).pin_memory()
+                        host_out[i][k] = dst
+                    dst.copy_(v, non_blocking=True)
+                    nb += v.numel() * v.element_size()
+                wd.record_stream(st)
+        d2h["b"] = nb
+
+    step()
+    torch.cuda.synchronize()
+    barrier(ws)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for st in streams:
+        st.wait_event(e0)
+    for _ in range(args.e2e_steps):
+        step()
+    for st in streams:
+        torch.cuda.current_stream(dev).wait_stream(st)
+    e1.record()
+    torch.cuda.synchronize()
+    ems = max_over_ranks(ws, e0.elapsed_time(e1))
+    return {"value": round(total_fp16 * args.e2e_steps / (ems / 1e3) / 1e9, 3), "unit": UNIT,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h["b"],
+            "per": "rank 0 (every rank moves its own share)", "steps": args.e2e_steps,
+            "ms_per_step": round(ems / args.e2e_steps, 3),
+            "path": "memboost_b200.quantize() per matrix (C ABI), pinned host buffers, "
+                    "2 alternating streams"}
+
+
+# ---------------------------------------------------------------------------
+# one-GPU sub-records
+# ---------------------------------------------------------------------------
+
+def sub_mlp_pair(steps=1000, warmup=5):
+    """Config 2: the Llama-7B MLP pair, QuantizePlan per matrix, every plan on
+    a stream of its own (two matrices x two step sets), step k + 1 enqueued
+    before step k is finished."""
+    import torch
+
+    from memboost_b200 import _C
+    from memboost_b200 import workloads as wl
+    dev = torch.device("cuda", torch.cuda.current_device())
+    cases = wl.mlp_7b()
+    W = [c.weights.to(dev) for c in cases]
+    H = [c.hessian_diag.to(dev) for c in cases]
+    stream_sets = [[torch.cuda.Stream(dev) for _ in W] for _ in range(2)]
+    streams = [st for ss in stream_sets for st in ss]
+    plan_sets = [[_C.QuantizePlan(*w.shape, dev, stream=st) for w, st in zip(W, ss)]
+                 for ss in stream_sets]
+    nnz_seen = []
+
+    def run_steps(n):
+        for k in range(n):
+            for p, w, h, c in zip(plan_sets[k % 2], W, H, cases):
+                p.launch(w, c.ratio_4bit, h)
+            if k > 0:
+                nnz_seen.append([int(r[8].numel()) for r in
+                                 (p.finish() for p in plan_sets[(k - 1) % 2])])
+        nnz_seen.append([int(r[8].numel()) for r in (p.finish() for p in plan_sets[(n - 1) % 2])])
+
+    run_steps(warmup)
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for st in streams:
+        st.wait_event(t0)
+    run_steps(steps)
+    for st in streams:
+        torch.cuda.current_stream(dev).wait_stream(st)
+    t1.record()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    fp16 = sum(2 * w.numel() for w in W)
+    alg = [algorithmic_bytes(*w.shape, n, True) for w, n in zip(W, nnz_seen[-1])]
+    pk, kind = peaks()
+    ach = sum(alg) / (ms / steps / 1e3) / 1e9
+    return {"workload": "mlp_7b pair: 11008x4096 + 4096x11008 fp16, 0.05% Student-t(3) "
+                        "outliers, lognormal(0,1.5) hessian, ratio 0.1",
+            "value": round(fp16 * steps / (ms / 1e3) / 1e9, 2), "unit": UNIT, "steps": steps,
+            "ms_per_step": round(ms / steps, 4),
+            "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": pk["hbm_gbs"],
+                         "frac": round(ach / pk["hbm_gbs"], 4), "of": f"{kind} hbm_gbs",
+                         "traffic": TRAFFIC_PER_CALL_MLP7B,
+                         "algorithmic_bytes_per_call": alg},
+            "gpu_launches": 3 * len(W) * steps}
+
+
+def sub_single_4096(steps=200, warmup=5):
+    """Config 1: 4096x4096 (0.1% x10 outliers, hessian ones, ratio 0.1):
+    quantize then dequantize per step, device-resident, and dequantize
+    alone with its roofline."""
+    import torch
+
+    from memboost_b200 import _C
+    from memboost_b200 import workloads as wl
+    dev = torch.device("cuda", torch.cuda.current_device())
+    c = wl.single_4096()
+    batch = _C.QuantizeBatch([c.weights], [c.ratio_4bit], [c.hessian_diag], dev, branches=1)
+    batch.capture()
+    M, K = batch.shapes[0]
+    out = torch.empty((M, K), dtype=torch.float16, device=dev)
+
+    def step():
+        batch.launch()
+        r = batch.finish()[0]
+        _C.dequantize(r[0], r[1], r[2], r[3], r[7], M, K, out)
+        return r
+
+    for _ in range(warmup):
+        r = step()
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        r = step()
+    t1.record()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / steps
+    nnz = int(r[8].numel())
+    # dequantize alone, inputs rotated over 8 copies (larger than L2 together)
+    copies = [[t.clone() for t in (r[0], r[1], r[2], r[3], r[7])] for _ in range(8)]
+    outs = [torch.empty((M, K), dtype=torch.float16, device=dev) for _ in range(8)]
+    for i in range(16):
+        a = copies[i % 8]
+        _C.dequantize(a[0], a[1], a[2], a[3], a[4], M, K, outs[i % 8])
+    torch.cuda.synchronize()
+    d0 = torch.cuda.Event(enable_timing=True)
+    d1 = torch.cuda.Event(enable_timing=True)
+    n = 400
+    d0.record()
+    for i in range(n):
+        a = copies[i % 8]
+        _C.dequantize(a[0], a[1], a[2], a[3], a[4], M, K, outs[i % 8])
+    d1.record()
+    torch.cuda.synchronize()
+    dms = d0.elapsed_time(d1) / n
+    n4 = int(r[7].sum())
+    db = dequant_bytes(M, K, n4)
+    pk, kind = peaks()
+    qb = algorithmic_bytes(M, K, nnz, True)
+    return {"workload": "single 4096x4096 fp16 N(0,0.02^2) seed 0, 0.1% x10 outliers, "
+                        "hessian ones, ratio 0.1: quantize (graph replay) + dequantize",
+            "value": round(2 * M * K / (ms / 1e3) / 1e9, 2), "unit": UNIT,
+            "ms_per_step": round(ms, 4), "nnz": nnz, "steps": steps,
+            "quantize_plus_dequantize_bytes": qb + db,
+            "dequantize": {"ms": round(dms, 4),
+                           "value": round(2 * M * K / (dms / 1e3) / 1e9, 1), "unit": UNIT,
+                           "roofline": {"bound": "hbm", "algorithmic_bytes": db,
+                                        "achieved": round(db / (dms / 1e3) / 1e9, 1),
+                                        "peak": pk["hbm_gbs"],
+                                        "frac": round(db / (dms / 1e3) / 1e9 / pk["hbm_gbs"], 4),
+                                        "of": f"{kind} hbm_gbs",
+                                        "l2": "8 rotated input/output sets (8 x 41 MB)"}}}
+
+
+def sub_gptq(tokens=262144, reps=2):
+    """Config 4: one Llama-7B layer's GPTQ (4 tcgen05 Hessians over `tokens`
+    calibration tokens, 4 inverses, 7 GPTQ updates, 7 quantize calls), s per
+    layer; and the Hessians alone in TFLOP/s of N*K*(K+1)."""
+    import torch
+
+    from memboost_b200 import gptq
+    from memboost_b200 import workloads as wl
+    dev = torch.device("cuda", torch.cuda.current_device())
+    weights, inputs = wl.gptq_layer(tokens=tokens, device=dev)
+    torch.cuda.synchronize()
+    gptq.quantize_layer(weights, inputs)  # warm-up
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(reps):
+        gptq.quantize_layer(weights, inputs)
+    t1.record()
+    torch.cuda.synchronize()
+    s_layer = t0.elapsed_time(t1) / 1e3 / reps
+    hres = {}
+    flops_all, ms_all = 0.0, 0.0
+    for key, x in inputs.items():
+        K = x.shape[1]
+        H = torch.empty((K, K), dtype=torch.float32, device=dev)
+        gptq.hessian(x, alpha=1.0 / x.shape[0], out=H)
+        torch.cuda.synchronize()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        n = 3
+        a.record()
+        for _ in range(n):
+            gptq.hessian(x, alpha=1.0 / x.shape[0], out=H)
+        b.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / n
+        fl = float(x.shape[0]) * K * (K + 1)
+        flops_all += fl
+        ms_all += ms
+        hres[key] = {"K": K, "ms": round(ms, 3), "tflops": round(fl / (ms / 1e3) / 1e12, 1)}
+    pk, kind = peaks()
+    tf = flops_all / (ms_all / 1e3) / 1e12
+    return {"workload": f"GPTQ of one Llama-7B layer: calibration X {tokens} tokens bf16 "
+                        "(Student-t(4)/sqrt(4096), 1% channels x20) for K=4096 (3 inputs) and "
+                        "11008 (down_proj); H=X^T X fp32; block 128; ratio 0.1",
+            "s_per_layer": round(s_layer, 4), "reps": reps,
+            "hessian": {"per_input": hres, "tflops": round(tf, 1),
+                        "flops_per_layer": flops_all, "ms_per_layer": round(ms_all, 3),
+                        "roofline": {"bound": "tensor", "achieved": round(tf, 1),
+                                     "peak": pk.get("bf16_tflops"), "unit": "TFLOP/s",
+                                     "frac": round(tf / float(pk.get("bf16_tflops", 1590.0)), 4),
+                                     "of": f"{kind} bf16_tflops (burst: kernels timed alone)",
+                                     "flops": "N*K*(K+1) per Hessian (symmetric)"}}}
+
+
+# ---------------------------------------------------------------------------
+# reference arm
+# ---------------------------------------------------------------------------
+
+def run_reference_arm(args, ws, rank, local):
+    """The reference algorithm on the host cores (oracle port of
+    core/quantize.cu + core/torch_ops.cu), on row slices of the same model;
+    as context the reference's own CUDA kernels (oracle/_ref) on layer 0 and
+    its GPTQ layer loop (models/llama.py:234-294 restated in torch ops) on
+    this GPU.  Nothing of memboost_b200's native library is loaded."""
+    import torch
+
+    from oracle import oracle
+    wl = load_workloads()
     oracle.build()
-    cases = workloads.mlp_7b()
-    fp16 = sum(2 * c.weights.numel() for c in cases)
-    wn = [c.weights.numpy() for c in cases]
-    hn = [c.hessian_diag.numpy() for c in cases]
+    dev = torch.device("cuda", local)
+    shapes = model_shapes(args.layers, wl)
+    total_fp16 = sum(2 * M * K for _, M, K, _ in shapes)
+    full = cpu_sample(wl, shapes, dev, frac=1.0)
     t_one = time.perf_counter()
-    for w, h, c in zip(wn, hn, cases):
-        oracle.quantize(w, c.ratio_4bit, h, nthreads=0)
-    t_one = time.perf_counter() - t_one
-    # bounded sample per step: whole pair if a step is short, else row slices;
-    # the timed steps together take about a minute (6 s a step at most), the
-    # warm-up steps likewise
+    for _, w, h, r in full:
+        oracle.quantize(w[:256], r, h, nthreads=0)
+    t_row = (time.perf_counter() - t_one) / 256 / len(full)
+    # bounded sample per step: the timed steps together take about a minute
     per_step_s = min(6.0, 60.0 / max(1, args.steps))
-    frac = min(1.0, per_step_s / max(t_one, 1e-6))
-    rows = [max(256, int(w.shape[0] * frac)) for w in wn]
-    sample = [np.ascontiguousarray(w[:r]) for w, r in zip(wn, rows)] if frac < 1 else wn
-    step_bytes = sum(2 * s.size for s in sample)
+    rows = max(64, int(per_step_s / max(t_row, 1e-9)))
+    sample = [(n, np.ascontiguousarray(w[:min(rows, w.shape[0])]), h, r) for n, w, h, r in full]
+    step_bytes = sum(2 * w.size for _, w, _, _ in sample)
     for _ in range(args.warmup):
-        for s, h, c in zip(sample, hn, cases):
-            oracle.quantize(s, c.ratio_4bit, h, nthreads=0)
+        for _, w, h, r in sample:
+            oracle.quantize(w, r, h, nthreads=0)
     a = time.perf_counter()
     for _ in range(args.steps):
-        for s, h, c in zip(sample, hn, cases):
-            oracle.quantize(s, c.ratio_4bit, h, nthreads=0)
+        for _, w, h, r in sample:
+            oracle.quantize(w, r, h, nthreads=0)
     el = time.perf_counter() - a
     value = step_bytes * args.steps / el / 1e9
+    rows_of = {n: w.shape[0] for n, w, _, _ in sample}
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT,
         "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(el / args.steps * 1e3, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "fp16->u8/i32", "data": "synthetic",
-        "config": {"workload": "mlp_7b pair: 11008x4096 + 4096x11008 fp16, ratio_4bit 0.1",
-                   "per_step_sample_rows": rows},
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp16->u8/i32",
+        "data": "synthetic (seeded N(0,0.02^2) weights, lognormal(0,1.5) hessian, drawn on the "
+                "GPU; no checkpoint)",
+        "config": {"workload": WORKLOAD, "layers": args.layers, "matrices": len(shapes),
+                   "fp16_bytes": total_fp16, "per_step_sample_rows": rows_of},
         "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": os.cpu_count(),
                          "kind": "port",
-                         "sample": f"oracle/mb_oracle.cpp (reference algorithm) on "
-                                   f"{os.cpu_count()} host threads, rows {rows} of the pair"},
+                         "sample": f"oracle/mb_oracle.cpp (the reference algorithm restated "
+                                   f"in C++) on {os.cpu_count()} host threads, rows {rows_of} "
+                                   f"of layer 0 of the model per step"},
         "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
-    # the reference's own CUDA kernels, built from its sources, on this GPU
+    # context: the reference's own CUDA kernels, built from its sources, on layer 0
     try:
         from oracle import build_ref
         ref = build_ref.load()
-        dev = torch.device("cuda", local)
-        W = [c.weights.to(dev) for c in cases]
-        H = [c.hessian_diag.to(dev) for c in cases]
-        for _ in range(3):
-            for w, h, c in zip(W, H, cases):
-                ref.quantize(w, c.ratio_4bit, h)
+        cases = [wl.llama7b_matrix(n, M, K, s, device=dev) for n, M, K, s in shapes[:7]]
+        for _ in range(2):
+            for c in cases:
+                ref.quantize(c.weights, c.ratio_4bit, c.hessian_diag)
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        n = max(3, min(args.steps, 10))
+        n = 3
         e0.record()
         for _ in range(n):
-            for w, h, c in zip(W, H, cases):
-                ref.quantize(w, c.ratio_4bit, h)
+            for c in cases:
+                ref.quantize(c.weights, c.ratio_4bit, c.hessian_diag)
         e1.record()
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1)
+        fp16 = sum(2 * c.weights.numel() for c in cases)
         line["reference_cuda_b200"] = {
             "value": round(fp16 * n / (ms / 1e3) / 1e9, 3), "unit": UNIT,
-            "ms_per_step": round(ms / n, 3),
+            "ms_per_layer": round(ms / n, 3),
             "what": "reference core/*.cu compiled for sm_100a (oracle/build_ref.py), "
-                    "_C.quantize on the same pair, CUDA events, device-resident inputs"}
+                    "_C.quantize on layer 0's seven matrices, CUDA events, device-resident"}
+        del cases
     except Exception as e:  # not built here
         line["reference_cuda_b200"] = {"unavailable": str(e)[:200]}
+    if not args.no_sub:
+        try:
+            line["reference_gptq_layer"] = reference_gptq_layer(wl, dev)
+        except Exception as e:
+            line["reference_gptq_layer"] = {"unavailable": str(e)[:200]}
     return line
+
+
+def reference_gptq_layer(wl, dev, tokens=262144):
+    """The reference's per-layer GPTQ on this GPU in its own torch terms: H
+    accumulated as fp32 x^T x per 2048-token sample (models/llama.py:523-528),
+    the damped Cholesky inverse (llama.py:177-203, torch.linalg), group
+    precision by torch sum + topk (llama.py:209-231) and the column loop of
+    gptq_quantize (llama.py:234-294, restated op for op in oracle/gptq_torch);
+    the final memboost.quantize calls are left out (timed with our arm)."""
+    import torch
+
+    from oracle import gptq_torch
+    weights, inputs = wl.gptq_layer(tokens=tokens, device=dev)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        inv = {}
+        for key, x in inputs.items():
+            K = x.shape[1]
+            H = torch.zeros((K, K), dtype=torch.float32, device=dev)
+            for s0 in range(0, x.shape[0], 2048):
+                xf = x[s0:s0 + 2048].float()
+                H.add_(xf.T @ xf)
+            H.div_(x.shape[0])
+            d = H.diagonal()
+            d.add_(max((0.01 * d.abs().max()).item(), 1e-6))
+            Hinv = torch.cholesky_inverse(torch.linalg.cholesky(H))
+            h_diag = Hinv.diag().clone()
+            Hinv.diagonal().add_(1e-8)
+            inv[key] = (h_diag, torch.linalg.cholesky(Hinv, upper=True))
+        t_h = time.perf_counter() - t0
+        groups = {"self_attn.q_proj": "attn", "self_attn.k_proj": "attn",
+                  "self_attn.v_proj": "attn", "self_attn.o_proj": "o", "mlp.gate_proj": "mlp",
+                  "mlp.up_proj": "mlp", "mlp.down_proj": "down"}
+        for name, W in weights.items():
+            h_diag, hc = inv[groups[name]]
+            M, K = W.shape
+            ng = K // 16
+            sens = (W.pow(2) * (1.0 / h_diag.clamp(min=1e-8)).unsqueeze(0)).view(M, ng, 16).sum(
+                dim=(0, 2))
+            gp = torch.zeros(ng, dtype=torch.uint8, device=dev)
+            gp[sens.topk(int(0.1 * ng)).indices] = 1
+            gptq_torch.gptq_quantize(W, hc, gp)
+        torch.cuda.synchronize()
+        total = time.perf_counter() - t0
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    return {"s_per_layer": round(total, 3), "hessians_and_inverses_s": round(t_h, 3),
+            "what": "reference GPTQ steps of models/llama.py in torch on this GPU (fp32 "
+                    "Hessian per 2048-token sample, cholesky inverse, column loop); "
+                    "memboost.quantize calls not included"}
 
 
 def main():
@@ -528,10 +835,17 @@ def main():
         if rank == 0:
             print(json.dumps(run_reference_arm(args, ws, rank, local)), flush=True)
         return
-    line, cases = run_ours(args, ws, rank, local)
+    line, shapes, wl = run_ours(args, ws, rank, local)
+    if ws == 1 and not args.no_sub:
+        import torch
+        torch.cuda.empty_cache()
+        line["mlp_pair"] = sub_mlp_pair()
+        line["single_4096"] = sub_single_4096()
+        line["gptq_layer"] = sub_gptq()
     if rank == 0:
         if ws == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(cases)
+            import torch
+            line["cpu_baseline"] = cpu_baseline(wl, shapes, torch.device("cuda", local))
         print(json.dumps(line), flush=True)
     if ws > 1:
         import torch.distributed as dist

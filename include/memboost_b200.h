@@ -87,12 +87,51 @@ mb_status mb_quantize_extract_outliers(const void* weights_fp16, int64_t M, int6
                                        int32_t* outlier_col_indices, const void* workspace,
                                        size_t workspace_bytes, mb_stream_t stream);
 
+/* Both phases of quantize in one enqueue, with no host round trip --
+ * core/torch_ops.cu:105-264 (quantize_op including extract_outliers,
+ * :231-248).  Same inputs and outputs as mb_quantize, plus caller-sized CSR
+ * arrays with room for outlier_capacity outliers: the extraction kernel is
+ * chained to the quantize kernels on `stream` and reads the outlier count on
+ * the device.  After the stream reaches this point, *nnz_device holds the
+ * count; if it exceeds outlier_capacity the CSR values / columns were not
+ * written and flag bit 3 (mb_quantize_flags) is set -- call
+ * mb_quantize_extract_outliers with larger arrays (same workspace).  No host
+ * synchronisation and no allocation inside: a sequence of these calls can
+ * be recorded once and replayed (whole-model loops). */
+mb_status mb_quantize_csr(const void* weights_fp16, int64_t M, int64_t K, double ratio_4bit,
+                          const float* hessian_diag, int64_t hessian_numel,
+                          int32_t* packed_2bit, int32_t* packed_4bit, void* scales_1st_fp16,
+                          int8_t* zeros_1st, void* scales_2nd_fp16, int8_t* zeros_2nd,
+                          uint8_t* scales_1st_quant, uint8_t* group_precision,
+                          int32_t* outlier_row_ptrs, int32_t* nnz_device,
+                          void* outlier_values_fp16, int32_t* outlier_col_indices,
+                          int64_t outlier_capacity, void* workspace, size_t workspace_bytes,
+                          mb_stream_t stream);
+
 /* Host-side flags of the last mb_quantize on `workspace` (synchronises the
  * stream).  Bit 0: the 4-bit selection met a tie of equal sensitivities at
  * the selection boundary and broke it by lowest group index (the reference
- * breaks such ties by std::sort's unspecified order). */
+ * breaks such ties by std::sort's unspecified order).  Bit 1: a pipeline
+ * wait inside a kernel ran out (outputs invalid).  Bit 2: a 2nd-order zero
+ * point round(-min / scales_2nd) of some 256-scale chunk lay outside
+ * [-128, 127]; zeros_2nd keeps the reference's int8 cast of it
+ * (core/quantize.cu:267-272), which wraps, so scales rebuilt from
+ * scales_1st_quant / scales_2nd / zeros_2nd (mb_dequantize_2nd) are wrong
+ * for that chunk -- a limit of the reference format.  It happens when a
+ * chunk's 256 scales are tightly clustered (max / min below about 1.12).
+ * Bit 3: mb_quantize_csr found more outliers than its CSR capacity. */
 mb_status mb_quantize_flags(const void* workspace, size_t workspace_bytes, int64_t M, int64_t K,
                             uint32_t* flags, mb_stream_t stream);
+
+/* Diagnostics of the last mb_quantize on `workspace` (synchronises the
+ * stream; no counterpart in the reference).  info[0] = the flags of
+ * mb_quantize_flags; info[1] = groups whose sensitivity interval straddled
+ * the 4-bit selection boundary; info[2] = groups among them whose exact
+ * serial fp32 sensitivity sums (the order of core/quantize.cu:72-98) were
+ * computed to settle the selection; info[3] = 1 if a group of its selected
+ * precision may hold outliers (the per-element reference formula ran). */
+mb_status mb_quantize_info(const void* workspace, size_t workspace_bytes, int64_t M, int64_t K,
+                           uint32_t info[4], mb_stream_t stream);
 
 /* ---------------------------------------------------------------------------
  * quantize without allocation -- no counterpart in the reference.

@@ -39,6 +39,12 @@ _lib.mb_quantize_extract_outliers.argtypes = [_P, _I64, _I64, _P, _P, _P, _P, ct
 _lib.mb_quantize_flags.restype = ctypes.c_int
 _lib.mb_quantize_flags.argtypes = [_P, ctypes.c_size_t, _I64, _I64,
                                    ctypes.POINTER(ctypes.c_uint32), _P]
+_lib.mb_quantize_csr.restype = ctypes.c_int
+_lib.mb_quantize_csr.argtypes = ([_P, _I64, _I64, ctypes.c_double, _P, _I64] + [_P] * 10 +
+                                 [_P, _P, _I64, _P, ctypes.c_size_t, _P])
+_lib.mb_quantize_info.restype = ctypes.c_int
+_lib.mb_quantize_info.argtypes = [_P, ctypes.c_size_t, _I64, _I64,
+                                  ctypes.POINTER(ctypes.c_uint32), _P]
 _lib.mb_dequantize.restype = ctypes.c_int
 _lib.mb_dequantize.argtypes = [_P, _P, _P, _P, _P, _I64, _I64, _P, _P]
 _lib.mb_qgemv.restype = ctypes.c_int
@@ -71,8 +77,14 @@ GPTQ_DIV_RECIPROCAL = 1
 LIB_PATH = _LIB_PATH
 
 # mb_quantize_flags bit 0: a tie of equal sensitivities straddled the 4-bit
-# selection boundary (broken by lowest group index).
+# selection boundary (broken by lowest group index); bit 1: a pipeline wait in
+# a kernel ran out; bit 2: a 2nd-order zero point wrapped in its int8 cast (the
+# reference format's limit: scales rebuilt from the 2nd-order codes are wrong
+# for that chunk).
 FLAG_SELECTION_TIE = 1
+FLAG_TIMEOUT = 2
+FLAG_ZERO2_WRAP = 4
+FLAG_CSR_OVERFLOW = 8
 
 
 def version() -> str:
@@ -171,6 +183,14 @@ class QuantizeWorkspace:
                                       ctypes.byref(f), _stream(self.buf.device)))
         return int(f.value)
 
+    def info(self) -> dict:
+        """Diagnostics of the last quantize on this workspace (mb_quantize_info)."""
+        a = (ctypes.c_uint32 * 4)()
+        _check(_lib.mb_quantize_info(_ptr(self.buf), self.nbytes, self.M, self.K, a,
+                                     _stream(self.buf.device)))
+        return {"flags": int(a[0]), "straddling": int(a[1]), "exact_sums": int(a[2]),
+                "any_irregular": int(a[3])}
+
 
 def quantize(weights: torch.Tensor, ratio_4bit: float = 0.1,
              hessian_diag: torch.Tensor | None = None,
@@ -263,6 +283,10 @@ def dequantize(packed_2bit: torch.Tensor, packed_4bit: torch.Tensor, scales_1st:
         args = [t.contiguous() for t, *_ in expect]
         if out is None:
             out = torch.empty((M, K), dtype=torch.float16, device=dev)
+        elif out.dtype != torch.float16 or out.numel() < M * K or not out.is_contiguous() \
+                or out.device != dev:
+            raise RuntimeError("out must be a contiguous float16 tensor of at least M * K "
+                               "values on packed_2bit's device")
         _check(_lib.mb_dequantize(*[_ptr(a) for a in args], M, K, _ptr(out), _stream(dev)))
     return out
 
@@ -313,6 +337,10 @@ def dequantize_2nd(packed_2bit: torch.Tensor, packed_4bit: torch.Tensor,
         args = [t.contiguous() for t, *_ in expect]
         if out is None:
             out = torch.empty((M, K), dtype=torch.float16, device=dev)
+        elif out.dtype != torch.float16 or out.numel() < M * K or not out.is_contiguous() \
+                or out.device != dev:
+            raise RuntimeError("out must be a contiguous float16 tensor of at least M * K "
+                               "values on packed_2bit's device")
         ptrs = [_ptr(a) for a in args] + [None] * (10 - len(args))
         _check(_lib.mb_dequantize_2nd(*ptrs, nnz, M, K, _ptr(out), _stream(dev)))
     return out
@@ -353,8 +381,10 @@ def qgemv(packed_2bit: torch.Tensor, packed_4bit: torch.Tensor, scales_1st: torc
         args = [t.contiguous() for t, *_ in expect]
         if out is None:
             out = torch.empty((M,), dtype=torch.float32, device=dev)
-        elif out.dtype != torch.float32 or out.numel() < M or not out.is_contiguous():
-            raise RuntimeError("out must be a contiguous float32 tensor of at least M values")
+        elif out.dtype != torch.float32 or out.numel() < M or not out.is_contiguous() \
+                or out.device != dev:
+            raise RuntimeError("out must be a contiguous float32 tensor of at least M values "
+                               "on packed_2bit's device")
         p = [_ptr(a) for a in args]
         _check(_lib.mb_qgemv(*p[:6], p[6] if nnz else None, p[7] if nnz else None, nnz, M, K,
                              p[8], _ptr(out), _stream(dev)))
@@ -503,3 +533,131 @@ def gptq_quantize(W: torch.Tensor, Hinv_cho: torch.Tensor, group_precision: torc
                                      int(scalar_division), _ptr(out), _ptr(ws), ws.numel(),
                                      _stream(dev)))
     return out
+
+
+class QuantizeBatch:
+    """Quantizes a fixed list of matrices -- a model's weights -- with every
+    launch recorded once into a CUDA graph and replayed.
+
+    The batch owns device buffers for the weights (``weights[i]``; refill them
+    in place between replays), hessian diagonals, every output, a workspace
+    per matrix and CSR arrays with room for ``csr_capacity`` outliers each.
+    Each matrix is one ``mb_quantize_csr`` call (stats, tables, encode and the
+    CSR extraction chained on the device, no host round trip); the matrices
+    are spread over ``branches`` parallel graph branches (largest first, each
+    to the least loaded branch), so one matrix's latency-bound selection
+    overlaps another's streaming.  ``launch`` replays the graph on the current
+    stream (a few microseconds of host time for the whole list); ``finish``
+    waits for it and returns the reference's 11-tensor list per matrix, views
+    into the batch's buffers valid until the next ``launch``.  A matrix with
+    more outliers than its capacity is re-extracted into larger arrays in
+    ``finish`` (mb_quantize_extract_outliers).
+    """
+
+    def __init__(self, weights: list, ratios, hessians: list | None = None, device=None,
+                 branches: int = 4, csr_capacity: int | None = None):
+        device = torch.device("cuda", torch.cuda.current_device()) if device is None \
+            else torch.device(device)
+        self.device = device
+        n = len(weights)
+        if isinstance(ratios, (int, float)):
+            ratios = [float(ratios)] * n
+        hessians = [None] * n if hessians is None else list(hessians)
+        e = lambda shape, dt: torch.empty(shape, dtype=dt, device=device)  # noqa: E731
+        with torch.cuda.device(device):
+            self.weights = [w.to(device=device, dtype=torch.float16).contiguous().clone()
+                            for w in weights]
+            self.hess = [None if (h is None or h.numel() == 0 or r <= 0) else
+                         h.to(device=device, dtype=torch.float32).contiguous().clone()
+                         for h, r in zip(hessians, ratios)]
+            self.ratios = [float(r) for r in ratios]
+            self.shapes = [tuple(int(x) for x in w.shape) for w in self.weights]
+            self.out, self.ws, self.row_ptrs, self.vals, self.cols, self.cap = [], [], [], [], [], []
+            for (M, K) in self.shapes:
+                ng = (K + GROUP_SIZE_1ST - 1) // GROUP_SIZE_1ST
+                ng2 = (M * ng + GROUP_SIZE_2ND - 1) // GROUP_SIZE_2ND
+                self.out.append([e((M, ng), torch.int32), e((M, 2 * ng), torch.int32),
+                                 e((M, ng), torch.float16), e((M, ng), torch.int8),
+                                 e((ng2,), torch.float16), e((ng2,), torch.int8),
+                                 e((M, ng), torch.uint8), e((ng,), torch.uint8)])
+                self.ws.append(QuantizeWorkspace(M, K, device))
+                self.row_ptrs.append(e((M + 1,), torch.int32))
+                cap = max(1024, (M * K) // 256) if csr_capacity is None else int(csr_capacity)
+                self.cap.append(cap)
+                self.vals.append(e((max(cap, 1),), torch.float16))
+                self.cols.append(e((max(cap, 1),), torch.int32))
+            self.nnz_dev = torch.zeros((n,), dtype=torch.int32, device=device)
+            self.nnz_host = torch.zeros((n,), dtype=torch.int32).pin_memory()
+        # branches: largest matrices first, each to the least loaded branch
+        nb = max(1, min(int(branches), n))
+        load = [0] * nb
+        self.branch_of = [0] * n
+        for i in sorted(range(n), key=lambda i: -self.shapes[i][0] * self.shapes[i][1]):
+            b = min(range(nb), key=lambda b: load[b])
+            self.branch_of[i] = b
+            load[b] += self.shapes[i][0] * self.shapes[i][1]
+        self.nbranch = nb
+        self.graph = None
+        self.done = torch.cuda.Event()
+
+    def _enqueue(self, i: int, stream) -> None:
+        M, K = self.shapes[i]
+        h = self.hess[i]
+        o = self.out[i]
+        _check(_lib.mb_quantize_csr(
+            _ptr(self.weights[i]), M, K, self.ratios[i], _ptr(h), 0 if h is None else h.numel(),
+            *(_ptr(t) for t in o), _ptr(self.row_ptrs[i]),
+            ctypes.c_void_p(self.nnz_dev.data_ptr() + 4 * i), _ptr(self.vals[i]),
+            _ptr(self.cols[i]), self.cap[i], _ptr(self.ws[i].buf), self.ws[i].nbytes,
+            ctypes.c_void_p(stream.cuda_stream)))
+
+    def _record(self, main) -> None:
+        fork = torch.cuda.Event()
+        fork.record(main)
+        for st in self.streams:
+            st.wait_event(fork)
+        for i in range(len(self.shapes)):
+            self._enqueue(i, self.streams[self.branch_of[i]])
+        for st in self.streams:
+            main.wait_stream(st)
+        self.nnz_host.copy_(self.nnz_dev, non_blocking=True)
+
+    def capture(self) -> None:
+        """Record the graph (once; the first call of every kernel runs eagerly
+        before it, so one-time set-up stays out of the capture)."""
+        with torch.cuda.device(self.device):
+            self.streams = [torch.cuda.Stream(self.device) for _ in range(self.nbranch)]
+            main = torch.cuda.current_stream(self.device)
+            self._record(main)
+            torch.cuda.synchronize(self.device)
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph):
+                self._record(torch.cuda.current_stream(self.device))
+            torch.cuda.synchronize(self.device)
+
+    def launch(self) -> None:
+        if self.graph is None:
+            self.capture()
+        with torch.cuda.device(self.device):
+            self.graph.replay()
+            self.done.record()
+
+    def finish(self) -> list:
+        self.done.synchronize()
+        nnz = self.nnz_host.tolist()
+        res = []
+        for i, (M, K) in enumerate(self.shapes):
+            k = int(nnz[i])
+            if k > self.cap[i]:
+                with torch.cuda.device(self.device):
+                    self.cap[i] = k
+                    self.vals[i] = torch.empty((k,), dtype=torch.float16, device=self.device)
+                    self.cols[i] = torch.empty((k,), dtype=torch.int32, device=self.device)
+                    self.graph = None  # the graph holds the old arrays
+                    _check(_lib.mb_quantize_extract_outliers(
+                        _ptr(self.weights[i]), M, K, _ptr(self.row_ptrs[i]), _ptr(self.vals[i]),
+                        _ptr(self.cols[i]), _ptr(self.ws[i].buf), self.ws[i].nbytes,
+                        _stream(self.device)))
+                    torch.cuda.current_stream(self.device).synchronize()
+            res.append([*self.out[i], self.vals[i][:k], self.cols[i][:k], self.row_ptrs[i]])
+        return res

@@ -47,6 +47,12 @@ namespace {
 constexpr int kFlagRegular = 1;  // threshold path valid; group cannot hold outliers
 constexpr uint32_t kStatusTie = 1u;
 constexpr uint32_t kStatusTimeout = 2u;
+// a 2nd-order zero point round(-min / scale_2nd) fell outside [-128, 127] and
+// wrapped in its int8 cast (the reference's format, quantize.cu:267-272)
+constexpr uint32_t kStatusZero2Wrap = 4u;
+// more outliers than the caller's CSR capacity (mb_quantize_csr): the CSR
+// values / columns were not written
+constexpr uint32_t kStatusCsrOverflow = 8u;
 
 // stats tiles: 128 columns (8 groups) x 128 rows
 constexpr int kTileCols = 128;
@@ -112,7 +118,8 @@ struct __align__(16) Header {
   uint32_t ticket_exact;   // pending groups whose exact sum is assembled
   uint32_t tile_stats;     // next stats tile
   uint32_t tile_encode;    // next encode tile
-  uint32_t pad[5];
+  uint32_t n_straddle;     // groups whose sensitivity interval straddled the boundary
+  uint32_t pad[4];
 };
 static_assert(sizeof(Header) == 64, "Header must stay 64 bytes");
 
@@ -1384,6 +1391,7 @@ __device__ void finalize_tables(const QArgs& a, float* s1, size_t s1_bytes, uint
     float sc2 = __fdiv_rn(__fsub_rn(mx, mn), 15.0f);
     if (sc2 < 1e-10f) sc2 = 1e-10f;
     const int z2 = f2i_rz(roundf(__fdiv_rn(-mn, sc2)));
+    if (z2 < -128 || z2 > 127) atomicOr(&a.ws.hdr->status, kStatusZero2Wrap);
     *e = make_float4(mn, sc2, __int_as_float((int)__half_as_ushort(__float2half_rn(sc2))),
                      __int_as_float((int)(int8_t)z2));
   }
@@ -1516,6 +1524,7 @@ __device__ void select_from_intervals(const QArgs& a, uint8_t* scratch, size_t s
     }
     sync_nt<NT>();
     const int need = n4 - (int)s_cnt[0], np = (int)s_cnt[1];
+    if (tid == 0) a.ws.hdr->n_straddle = (uint32_t)np;
     if (np > 0 && (need <= 0 || need >= np)) {
       // all pending groups take the same precision
       const uint8_t to = need > 0 ? 1 : 0;
@@ -2161,6 +2170,7 @@ __device__ __noinline__ void tables_grid(const QArgs& a) {
       float sc2 = __fdiv_rn(__fsub_rn(mx, mn), 15.0f);
       if (sc2 < 1e-10f) sc2 = 1e-10f;
       const int z2 = f2i_rz(roundf(__fdiv_rn(-mn, sc2)));
+      if (z2 < -128 || z2 > 127) atomicOr(&a.ws.hdr->status, kStatusZero2Wrap);
       a.ws.chunk_tab[partial ? cl.ntab_full : ci] =
           make_float4(mn, sc2, __int_as_float((int)__half_as_ushort(__float2half_rn(sc2))),
                       __int_as_float((int)(int8_t)z2));
@@ -2613,14 +2623,12 @@ __global__ void __launch_bounds__(kEncThreads, 2)
 // extract: one warp per row with outliers; only non-regular groups can hold
 // them.  Lanes 0-15 take the group's 16 columns; the ballot order is the
 // column order.
-__global__ void __launch_bounds__(256)
-    extract_kernel(const __half* __restrict__ W, int64_t M, int64_t K, int ng,
-                   const GroupParams* __restrict__ params, const uint8_t* __restrict__ prec,
-                   const int32_t* __restrict__ row_ptrs, __half* __restrict__ vals,
-                   int32_t* __restrict__ cols, int fma_mode) {
-  const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (r >= M) return;
+__device__ __forceinline__ void extract_row(const __half* __restrict__ W, int64_t r, int64_t K,
+                                            int ng, const GroupParams* __restrict__ params,
+                                            const uint8_t* __restrict__ prec,
+                                            const int32_t* __restrict__ row_ptrs,
+                                            __half* __restrict__ vals, int32_t* __restrict__ cols,
+                                            int fma_mode, int lane) {
   int32_t o = row_ptrs[r];
   const int32_t end = row_ptrs[r + 1];
   if (o == end) return;
@@ -2644,6 +2652,39 @@ __global__ void __launch_bounds__(256)
     }
     o += __popc(bal);
   }
+}
+
+__global__ void __launch_bounds__(256)
+    extract_kernel(const __half* __restrict__ W, int64_t M, int64_t K, int ng,
+                   const GroupParams* __restrict__ params, const uint8_t* __restrict__ prec,
+                   const int32_t* __restrict__ row_ptrs, __half* __restrict__ vals,
+                   int32_t* __restrict__ cols, int fma_mode) {
+  const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (r >= M) return;
+  extract_row(W, r, K, ng, params, prec, row_ptrs, vals, cols, fma_mode, threadIdx.x & 31);
+}
+
+// The CSR extraction chained to encode (programmatic dependent launch): the
+// outlier count is read on the device, so no host round trip sits between
+// the kernels (mb_quantize_csr).  Nothing to do without outliers; more
+// outliers than `capacity` set kStatusCsrOverflow and write nothing.  Warps
+// stride over the rows.
+__global__ void __launch_bounds__(256)
+    extract_cap_kernel(const __half* __restrict__ W, int64_t M, int64_t K, int ng,
+                       const GroupParams* __restrict__ params, const uint8_t* __restrict__ prec,
+                       const int32_t* __restrict__ row_ptrs, const int32_t* nnz,
+                       int64_t capacity, __half* __restrict__ vals, int32_t* __restrict__ cols,
+                       uint32_t* status, int fma_mode) {
+  grid_dependency_wait();  // encode and its row-pointer scan complete
+  const int32_t n = *reinterpret_cast<const volatile int32_t*>(nnz);
+  if (n <= 0) return;
+  if ((int64_t)n > capacity) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(status, kStatusCsrOverflow);
+    return;
+  }
+  const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < M; r += nw)
+    extract_row(W, r, K, ng, params, prec, row_ptrs, vals, cols, fma_mode, threadIdx.x & 31);
 }
 
 mb_status check_common(const void* weights, int64_t M, int64_t K) {
@@ -2829,6 +2870,58 @@ extern "C" mb_status mb_quantize_extract_outliers(const void* weights_fp16, int6
       outlier_row_ptrs, static_cast<__half*>(outlier_values_fp16), outlier_col_indices,
       kOutlierFma);
   MB_LAUNCH_CHECK("extract_kernel");
+  return MB_OK;
+}
+
+extern "C" mb_status mb_quantize_csr(const void* weights_fp16, int64_t M, int64_t K,
+                                     double ratio_4bit, const float* hessian_diag,
+                                     int64_t hessian_numel, int32_t* packed_2bit,
+                                     int32_t* packed_4bit, void* scales_1st_fp16,
+                                     int8_t* zeros_1st, void* scales_2nd_fp16, int8_t* zeros_2nd,
+                                     uint8_t* scales_1st_quant, uint8_t* group_precision,
+                                     int32_t* outlier_row_ptrs, int32_t* nnz_device,
+                                     void* outlier_values_fp16, int32_t* outlier_col_indices,
+                                     int64_t outlier_capacity, void* workspace,
+                                     size_t workspace_bytes, mb_stream_t stream_) {
+  MB_REQUIRE(outlier_capacity >= 0, "outlier_capacity must not be negative");
+  MB_REQUIRE(outlier_capacity == 0 || (outlier_values_fp16 && outlier_col_indices),
+             "CSR pointers must not be null when outlier_capacity > 0");
+  if (mb_status st = mb_quantize(weights_fp16, M, K, ratio_4bit, hessian_diag, hessian_numel,
+                                 packed_2bit, packed_4bit, scales_1st_fp16, zeros_1st,
+                                 scales_2nd_fp16, zeros_2nd, scales_1st_quant, group_precision,
+                                 outlier_row_ptrs, nnz_device, workspace, workspace_bytes,
+                                 stream_))
+    return st;
+  Workspace ws;
+  workspace_layout(M, K, static_cast<char*>(workspace), &ws);
+  const int64_t ng = ceil_div(K, kGroup1);
+  const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(ceil_div(M, 8), 1184));
+  return launch_pdl(extract_cap_kernel, dim3((unsigned)grid), dim3(256), 0,
+                    reinterpret_cast<cudaStream_t>(stream_),
+                    static_cast<const __half*>(weights_fp16), M, K, (int)ng,
+                    (const GroupParams*)ws.params, (const uint8_t*)ws.prec,
+                    (const int32_t*)outlier_row_ptrs, (const int32_t*)nnz_device,
+                    outlier_capacity, static_cast<__half*>(outlier_values_fp16),
+                    outlier_col_indices, &ws.hdr->status, kOutlierFma);
+}
+
+extern "C" mb_status mb_quantize_info(const void* workspace, size_t workspace_bytes, int64_t M,
+                                      int64_t K, uint32_t* info, mb_stream_t stream_) {
+  clear_error();
+  MB_REQUIRE(workspace && info, "null argument");
+  MB_REQUIRE(M > 0 && K > 0, "M and K must be positive");
+  const size_t need = workspace_layout(M, K, nullptr, nullptr);
+  if (workspace_bytes < need) return set_error(MB_ERR_WORKSPACE, "workspace too small");
+  Workspace ws;
+  workspace_layout(M, K, static_cast<char*>(const_cast<void*>(workspace)), &ws);
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  Header h;
+  MB_CUDA_TRY(cudaMemcpyAsync(&h, ws.hdr, sizeof(Header), cudaMemcpyDeviceToHost, stream));
+  MB_CUDA_TRY(cudaStreamSynchronize(stream));
+  info[0] = h.status;
+  info[1] = h.n_straddle;
+  info[2] = h.n_pend;
+  info[3] = h.any_irregular;
   return MB_OK;
 }
 

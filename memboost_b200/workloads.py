@@ -98,9 +98,22 @@ def llama7b_shapes(n_layers: int = 32) -> list[tuple[str, int, int]]:
     return [(f"layers.{l}.{n}", M, K) for l in range(n_layers) for (n, M, K) in LLAMA7B_LAYER]
 
 
-def llama7b_matrix(name: str, M: int, K: int, seed: int) -> MatrixCase:
-    g = torch.Generator().manual_seed(seed)
-    return MatrixCase(name, _normal(M, K, 0.02, g).half(), lognormal(K, 1.5, g), 0.1)
+def llama7b_matrix(name: str, M: int, K: int, seed: int, device=None) -> MatrixCase:
+    """One matrix of the Llama-2-7B-shaped model: N(0, 0.02^2) fp16 weights
+    and a lognormal(0, 1.5) hessian_diag, ratio 0.1.  ``device`` (default the
+    CPU) is where the values are drawn and kept; a CUDA generator gives other
+    (equally distributed) values than the CPU one for the same seed."""
+    device = torch.device("cpu") if device is None else torch.device(device)
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    w = torch.randn((M, K), generator=g, device=device, dtype=torch.float32).mul_(0.02).half()
+    h = torch.randn((K,), generator=g, device=device).mul_(1.5).exp_().float()
+    return MatrixCase(name, w, h, 0.1)
+
+
+def llama7b_model_seed(i: int) -> int:
+    """Seed of matrix i (in llama7b_shapes order) of the whole-model workload."""
+    return 1000 + i
 
 
 def small_case(M: int, K: int, seed: int, kind: str = "normal") -> MatrixCase:

@@ -12,6 +12,7 @@ The module is named ``memboost_ref_C`` and exposes exactly the reference's
 ``memboost._C`` functions (core/bindings.cpp:6-39).
 
 Usage: python oracle/build_ref.py [REFERENCE_ROOT]
+(default: $MEMBOOST_REFERENCE_DIR; reference_dir() below)
 """
 from __future__ import annotations
 
@@ -25,12 +26,24 @@ OUT = os.path.join(HERE, "_ref")
 NAME = "memboost_ref_C"
 
 
+def reference_dir() -> str | None:
+    """The reference checkout this recipe reads: $MEMBOOST_REFERENCE_DIR, else
+    the build container's mount point; None where neither holds core/."""
+    for d in (os.environ.get("MEMBOOST_REFERENCE_DIR"), "/root/reference"):
+        if d and os.path.isdir(os.path.join(d, "core")):
+            return d
+    return None
+
+
 def built_path() -> str | None:
     hits = sorted(glob.glob(os.path.join(OUT, NAME + "*.so")))
     return hits[0] if hits else None
 
 
-def build(ref_root: str = "/root/reference", verbose: bool = False) -> str:
+def build(ref_root: str | None = None, verbose: bool = False) -> str:
+    ref_root = ref_root or reference_dir()
+    if ref_root is None:
+        raise FileNotFoundError("reference checkout not found (set MEMBOOST_REFERENCE_DIR)")
     core = os.path.join(ref_root, "core")
     srcs = [os.path.join(core, f) for f in ("bindings.cpp", "torch_ops.cu", "quantize.cu")]
     for s in srcs:
@@ -79,4 +92,4 @@ def load():
 
 
 if __name__ == "__main__":
-    print(build(sys.argv[1] if len(sys.argv) > 1 else "/root/reference", verbose=True))
+    print(build(sys.argv[1] if len(sys.argv) > 1 else None, verbose=True))

@@ -112,4 +112,5 @@ def main(ref_root: str, out_dir: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference", HERE)
+    from oracle import build_ref
+    main(sys.argv[1] if len(sys.argv) > 1 else build_ref.reference_dir(), HERE)

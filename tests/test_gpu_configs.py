@@ -54,8 +54,43 @@ def test_mlp_7b(ref_module, i):
     _check(workloads.mlp_7b()[i], ref_module)
 
 
-def test_mlp_70b_up(ref_module):
-    _check(workloads.mlp_70b()[0], ref_module)
+@pytest.mark.parametrize("i", [0, 1])
+def test_mlp_70b(ref_module, i):
+    """Both config-5 matrices: 28672x8192 and 8192x28672 (K = 28672: ng =
+    1792, 224 column tiles, the widest K of the configurations)."""
+    _check(workloads.mlp_70b()[i], ref_module)
+
+
+def _info(case):
+    from memboost_b200 import _C
+    w = case.weights.cuda()
+    h = case.hessian_diag.cuda()
+    ws = _C.QuantizeWorkspace(*w.shape, w.device)
+    out = _C.quantize(w, case.ratio_4bit, h, ws)
+    torch.cuda.synchronize()
+    return out, ws.info()
+
+
+def test_exact_sums_run_on_ties(ref_module):
+    """Identical column groups: their sensitivity intervals coincide across
+    the 4-bit boundary, so the exact serial sums of the straddling groups run
+    (and the result still equals the reference kernels')."""
+    case = workloads.small_case(640, 1024, seed=21, kind="ties")
+    out, info = _info(case)
+    assert info["straddling"] > 0 and info["exact_sums"] > 0, info
+    _check(case, ref_module)
+
+
+def test_exact_sums_run_at_config_shape(ref_module):
+    """Config 1 (4096x4096, hessian all ones): the groups' sensitivities lie
+    within a fraction of a percent of each other, so groups straddle the
+    boundary and their exact serial sums decide, bit-exact to the
+    reference's selection."""
+    case = workloads.single_4096()
+    out, info = _info(case)
+    assert info["straddling"] > 0 and info["exact_sums"] > 0, info
+    assert info["flags"] & 2 == 0
+    _check(case, ref_module)
 
 
 def test_llama7b_layer0(ref_module):

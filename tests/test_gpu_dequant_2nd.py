@@ -41,3 +41,23 @@ def test_dequantize_2nd_unaligned_output(oracle):
     torch.cuda.synchronize()
     want = oracle.dequantize_2nd(_fields(qt), add_outliers=True)
     assert np.array_equal(out.cpu().numpy().view(np.uint16), want.view(np.uint16))
+
+
+def test_zero2_wrap_flag():
+    """Clustered scales make the reference's int8 2nd-order zero point wrap;
+    the quantize call reports it (FLAG_ZERO2_WRAP), and the outputs still
+    equal the oracle's (the format is kept).  Ordinary inputs raise no flag."""
+    from memboost_b200 import _C
+    from test_dequant_2nd import clustered_scales_case
+    from oracle import oracle as O
+    w = clustered_scales_case()
+    ws = _C.QuantizeWorkspace(*w.shape, torch.device("cuda"))
+    out = _C.quantize(torch.from_numpy(w).cuda(), 0.0, None, ws)
+    torch.cuda.synchronize()
+    assert ws.flags() & _C.FLAG_ZERO2_WRAP
+    want = O.quantize(w, 0.0, None)
+    assert np.array_equal(out[5].cpu().numpy(), want["zeros_2nd"])
+    mc = workloads.small_case(300, 1040, 12, "shifted")
+    ws2 = _C.QuantizeWorkspace(300, 1040, torch.device("cuda"))
+    _C.quantize(mc.weights.cuda(), 0.1, mc.hessian_diag.cuda(), ws2)
+    assert not ws2.flags() & _C.FLAG_ZERO2_WRAP

@@ -111,6 +111,34 @@ def test_hessian_config_shape(gq):
     assert float(err.max() / exact.abs().max()) < 2.5e-4
 
 
+def test_hessian_config4_length(gq):
+    """The full config-4 calibration length in one launch: 128 x 2048 =
+    262144 tokens x 4096 features, bf16 (8192 pipeline stages per CTA),
+    against fp64 within the fp32 tensor-core accumulation bound, by column
+    blocks of H."""
+    from memboost_b200 import workloads
+    N, K = 262144, 4096
+    x = workloads.calibration_activations(N, K, seed=17, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    H = gq.hessian(x, alpha=1.0 / N, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    xd = x.double()
+    worst, rel = 0.0, 0.0
+    for c0 in range(0, K, 1024):
+        blk = xd[:, c0:c0 + 1024]
+        exact = (blk.T @ xd) / N
+        gabs = (blk.abs().T @ xd.abs()) / N
+        bound = (N // 16 + 16) * 2.0 ** -22 * gabs + 2.0 ** -23 * exact.abs() + 1e-30
+        err = (H[c0:c0 + 1024].double() - exact).abs()
+        worst = max(worst, float((err / bound).max()))
+        rel = max(rel, float(err.max() / exact.abs().max()))
+        del exact, gabs, bound, err
+    assert worst <= 1.0, worst
+    print(f"hessian 262144x4096: max |H - fp64| / max|H| = {rel:.3e}, "
+          f"max err / bound = {worst:.3f}")
+
+
 def test_hessian_rejects_bad_arguments(gq):
     x = torch.zeros(16, 12, dtype=torch.float16, device="cuda")
     with pytest.raises(RuntimeError, match="multiple of 8"):
@@ -180,6 +208,20 @@ def test_gptq_matches_oracle_random(gq, oracle, M, K, ratio, seed):
         assert gptq_torch.equal_up_to_zero_sign(Q, torch.from_numpy(want)), mode
 
 
+def test_gptq_full_size_matches_reference_on_cuda(gq):
+    """A full 4096 x 4096 projection (32 blocks of 128 columns, ratio 0.1)
+    against the reference's column loop run on CUDA tensors, bit for bit."""
+    from memboost_b200 import workloads
+    K, M = 4096, 4096
+    x = workloads.calibration_activations(4 * K, K, seed=31, device="cuda")
+    h_diag, Hc = gq.gptq_inverse(gq.hessian(x, alpha=1.0 / x.shape[0]))
+    W = (torch.randn((M, K), generator=torch.Generator().manual_seed(8)) * 0.02).cuda()
+    gp = gq.compute_group_precision(W, h_diag, 0.1)
+    Q = gq.gptq_quantize(W, Hc, gp)
+    want = gptq_torch.gptq_quantize(W, Hc, gp)
+    assert gptq_torch.equal_up_to_zero_sign(Q, want)
+
+
 def test_gptq_rejects_bad_arguments(gq):
     W = torch.zeros(4, 24, device="cuda")
     with pytest.raises(RuntimeError, match="multiple of 16"):
@@ -217,3 +259,15 @@ def test_quantize_layer_small(gq):
     for name, qt in out.items():
         assert (qt.M, qt.K) == tuple(weights[name].shape)
         assert int(qt.group_precision.sum()) == int(0.1 * (qt.K // 16))
+
+
+def test_quantize_layer_full_shapes(gq):
+    """One Llama-7B layer at full weight shapes (calibration shortened to
+    16384 tokens): every matrix quantized with GPTQ's own 4-bit groups."""
+    from memboost_b200 import workloads
+    weights, inputs = workloads.gptq_layer(tokens=16384, device="cuda")
+    out = gq.quantize_layer(weights, inputs, ratio_4bit=0.1)
+    for name, qt in out.items():
+        M, K = weights[name].shape
+        assert (qt.M, qt.K) == (M, K)
+        assert int(qt.group_precision.sum()) == int(0.1 * (K // 16))

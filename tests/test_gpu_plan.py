@@ -40,3 +40,37 @@ def test_plans_match_quantize(use_streams):
                 a, b = g[k], getattr(q, f)
                 assert a.shape == b.shape, f
                 assert torch.equal(a.cpu(), b.cpu()), f
+
+
+@pytest.mark.parametrize("capacity", [None, 5])
+def test_batch_graph_matches_quantize(capacity):
+    """QuantizeBatch (every matrix's launches recorded once into a CUDA graph,
+    CSR extraction chained on the device) gives the public quantize()
+    outputs bit for bit, replay after replay; with a capacity below the
+    outlier count the batch falls back to a host-sized extraction."""
+    import memboost_b200 as mb
+    from memboost_b200 import _C
+    from memboost_b200 import workloads
+    dev = torch.device("cuda", 0)
+    cases = _cases() + [workloads.small_case(640, 1024, seed=21, kind="ties"),
+                        workloads.small_case(33, 48, seed=9, kind="const")]
+    W = [c.weights.to(dev) for c in cases]
+    H = [c.hessian_diag.to(dev) for c in cases]
+    ratios = [0.1, 0.1, 0.1, 0.25, 0.0]
+    want = [mb.quantize(w, r, h) for w, r, h in zip(W, ratios, H)]
+    batch = _C.QuantizeBatch(W, ratios, H, dev, branches=3, csr_capacity=capacity)
+    for rep in range(3):
+        batch.launch()
+        got = batch.finish()
+        for g, q in zip(got, want):
+            for k, f in enumerate(FIELDS):
+                a, b = g[k], getattr(q, f)
+                assert a.shape == b.shape, (rep, f)
+                assert torch.equal(a.cpu(), b.cpu()), (rep, f)
+    # new weights copied into the batch's buffers are picked up by the replay
+    batch.weights[1].copy_(W[1].flip(0))
+    batch.launch()
+    got = batch.finish()
+    again = mb.quantize(W[1].flip(0).contiguous(), 0.1, H[1])
+    for k, f in enumerate(FIELDS):
+        assert torch.equal(got[1][k].cpu(), getattr(again, f).cpu()), f
