@@ -13,7 +13,7 @@ ranks.  Rank 0 prints one JSON line.
   value      device-resident throughput: every matrix of this rank's share
              quantized by one CUDA-graph replay of its launches
              (memboost_b200._C.QuantizeBatch: stats, tables, encode and the
-             CSR extraction chained on the device, 4 graph branches); step
+             CSR extraction chained on the device, 8 graph branches); step
              k + 1 is enqueued before step k's outlier counts are read
   e2e        the public memboost_b200.quantize() call per matrix with host
              buffers: pinned H2D copy of the weights and hessian, quantize,
@@ -346,7 +346,7 @@ def run_ours(args, ws, rank, local):
     cases = [wl.llama7b_matrix(shapes[i][0], shapes[i][1], shapes[i][2], shapes[i][3],
                                device=dev) for i in mine]
     batch = _C.QuantizeBatch([c.weights for c in cases], [c.ratio_4bit for c in cases],
-                             [c.hessian_diag for c in cases], dev, branches=4)
+                             [c.hessian_diag for c in cases], dev, branches=8)
     del cases
     fp16_bytes = sum(2 * M * K for (M, K) in batch.shapes)
     batch.capture()
@@ -426,7 +426,7 @@ def run_ours(args, ws, rank, local):
                                      f"{algorithmic_bytes(4096, 11008, 0, True)} algorithmic "
                                      "bytes",
                      "kernel": "the quantize calls of a step (stats, exact/tables, encode, "
-                               "extract per matrix, chained with PDL, 4 graph branches): "
+                               "extract per matrix, chained with PDL, 8 graph branches): "
                                "algorithmic bytes of the whole job per GPU / device time per "
                                "step (max over ranks)",
                      "algorithmic_bytes_per_step": int(alg_all),

@@ -95,6 +95,39 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// 2-D tiled TMA store of the box at (x, y) from shared memory (bulk-group
+// completion).  The writes to `src` must be made visible to the async proxy
+// first (fence_proxy_async_smem by every writing thread, then a barrier).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x,
+                                             int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// Wait until at most N of this thread's committed bulk groups still read
+// their shared-memory source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+// Wait until at most N of this thread's committed bulk groups are pending.
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 // Programmatic dependent launch: wait for the preceding grid's memory.
 __device__ __forceinline__ void grid_dependency_wait() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -123,5 +156,13 @@ bool make_tensor_map_2d_f16(CUtensorMap* map, const void* base, uint64_t rows, u
 // out-of-bounds elements read as zero.
 bool make_tensor_map_2d_16bit_sw128(CUtensorMap* map, const void* base, bool bf16, uint64_t rows,
                                     uint64_t cols, uint32_t box_rows, uint32_t box_cols);
+
+// Row-major [rows, cols] matrix of 1-, 2- or 4-byte elements (elem_bytes),
+// box [box_rows, box_cols], swizzle 0 (none), 32, 64 or 128 (bytes).  For TMA
+// stores: elements outside the matrix are not written.  False if the driver
+// rejects it (base 16-byte aligned, cols * elem_bytes a multiple of 16,
+// box_cols * elem_bytes a multiple of 16 and at most the swizzle span).
+bool make_tensor_map_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t rows,
+                        uint64_t cols, uint32_t box_rows, uint32_t box_cols, int swizzle);
 
 }  // namespace mb

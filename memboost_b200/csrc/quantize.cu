@@ -1628,6 +1628,20 @@ __device__ __forceinline__ void tile_fill(const __half* W, int64_t M, int64_t K,
   }
 }
 
+// The same layout for the 128-column tile ct of row chunk rc (columns or rows
+// outside the matrix read as `fill`).
+__device__ __forceinline__ void tile_fill_at(const __half* W, int64_t M, int64_t K, uint8_t* dst,
+                                             int64_t rc, int64_t ct, uint16_t fill) {
+  for (int e = threadIdx.x; e < kChunkRows * kTileCols; e += blockDim.x) {
+    const int r = e / kTileCols, c = e % kTileCols;
+    const int64_t gr = rc * kChunkRows + r, gc = ct * kTileCols + c;
+    const uint16_t v = (gr < M && gc < K) ? __half_as_ushort(W[gr * K + gc]) : fill;
+    const int half = c >> 6, cc = c & 63;
+    *reinterpret_cast<uint16_t*>(dst + half * kBoxBytes + r * 128 +
+                                 (((cc >> 3) ^ (r & 7)) << 4) + (cc & 7) * 2) = v;
+  }
+}
+
 // Tile u of the stats pass is (column tile u / nrc, row chunk u % nrc); stats
 // CTA b takes the tiles [U_b, U_b+1), U_b = floor(b * ntiles / G), G <= ntiles
 // (so no range is empty).  A CTA's tiles of one column tile form a segment,
@@ -2218,10 +2232,11 @@ __device__ __forceinline__ void post_prologue(const QArgs& a) {
 
 // When groups may hold outliers: the last encode CTA to finish turns the
 // per-row counts into row pointers (all threads of every CTA call it).
+template <int NT>
 __device__ __forceinline__ void post_rowptr_scan(const QArgs& a) {
   if (a.ws.hdr->any_irregular == 0) return;
   __shared__ int s_last;
-  __shared__ long long part[kEncThreads];
+  __shared__ long long part[NT];
   const int tid = threadIdx.x;
   const int64_t M = a.M;
   __threadfence();
@@ -2616,7 +2631,360 @@ __global__ void __launch_bounds__(kEncThreads, 2)
     for (int s = 0; s < kEncStages; ++s)
       if (bad & (1u << s)) (void)mbar_wait(&full[s], 0u), (void)mbar_wait(&full[s], 1u);
   }
-  post_rowptr_scan(a);
+  post_rowptr_scan<kEncThreads>(a);
+}
+
+
+// ---------------------------------------------------------------------------
+// encode, wide-tile form: tiles of 128 rows x 256 columns (16 groups), lane =
+// row, outputs written whole by TMA.  Warp w takes the 32 rows
+// [32 (w & 3), 32 (w & 3) + 32) of the tile and four of its groups, the
+// quarter ((w >> 2) + i) & 3 on the CTA's i-th tile, so every warp carries
+// the same mix of 2-bit / 4-bit groups over any four tiles and no work queue
+// is needed.  A lane codes its row's four runs in registers (straight-line
+// code per 2/4-bit pattern of the quarter) and writes the words to a staging
+// tile laid out as the output rows (packed_2bit with the 64-byte swizzle,
+// packed_4bit with the 128-byte swizzle: conflict-free).  One thread then
+// stores the whole tile -- 64 bytes of packed_2bit, 128 of packed_4bit, 32
+// of scales_1st and 16 each of zeros_1st and 2nd-order codes per row -- with
+// five TMA stores, so every output row segment leaves as one write.
+// scales_1st and zeros_1st are the same in every row of a column tile: their
+// 128-row blocks are built once per column tile.  Tile stages are released
+// per warp (a 16-arrival mbarrier).  Needs ng % 16 == 0 and 16-byte aligned
+// outputs; other shapes take encode_kernel.  CTA b takes the tiles
+// [floor(b T / G), floor((b + 1) T / G)) of the T tiles in column-major order.
+// ---------------------------------------------------------------------------
+constexpr int kE3Cols = 256;
+constexpr int kE3Groups = kE3Cols / kGroup1;        // 16
+constexpr int kE3Threads = 512;                     // 16 warps
+constexpr int kE3Stages = 2;
+constexpr int kE3Tile = kChunkRows * kE3Cols * 2;   // 64 KB: four 64-column boxes
+constexpr int kE3P2 = kChunkRows * 64;              // 128 rows x 16 words
+constexpr int kE3P4 = kChunkRows * 128;             // 128 rows x 32 words
+constexpr int kE3Sq = kChunkRows * 16;              // 128 rows x 16 codes
+constexpr int kE3Out = kE3P2 + kE3P4 + kE3Sq;       // one staging buffer: 26 KB
+constexpr int kE3OffOut = kE3Stages * kE3Tile;
+constexpr int kE3OffScale = kE3OffOut + 2 * kE3Out;
+constexpr int kE3OffZero = kE3OffScale + kChunkRows * 32;
+constexpr int kE3Smem = kE3OffZero + kChunkRows * 16 + 1024;  // + alignment slack
+static_assert(kE3OffOut % 1024 == 0 && kE3Out % 1024 == 0 && kE3P2 % 1024 == 0 &&
+                  kE3OffScale % 128 == 0 && kE3OffZero % 128 == 0,
+              "staging alignment");
+
+struct __align__(16) Enc3Ctx {
+  uint4 thr[kE3Groups][4];                    // T_1..T_15 as broadcast half2, +inf pad
+  uint8_t sqrow[kE3Groups][kE3Groups];        // 2nd-order code by (row mod rp, group); rp <= 16
+  uint8_t kind[kE3Groups];
+  uint8_t gs[kE3Groups];
+  uint8_t pr[kE3Groups];
+  int pat[4];  // per quarter: 4-bit mask of the 4-bit groups, or 16 (general path)
+};
+
+struct Enc3Maps {
+  CUtensorMap p2, p4, sc, z, sq;  // packed_2bit (box 128 x 16, 64B swizzle), packed_4bit
+                                  // (128 x 32, 128B swizzle), scales_1st (128 x 16),
+                                  // zeros_1st (128 x 16), scales_1st_quant (128 x 16)
+};
+
+// Codes of one row's four runs of a quarter whose groups are all regular and
+// 16 columns wide; bit q of P: group q of the quarter is 4-bit.  The run of
+// group q lies at chunks 2q, 2q + 1 of the row in its 64-column box.
+template <int P>
+__device__ __forceinline__ void enc3_quarter(const uint8_t* __restrict__ rb, int sw,
+                                             const uint4 (*__restrict__ thr)[4],
+                                             uint32_t (&w2)[4], uint32_t (&w4)[8]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    Row16 v;
+    v.lo = *reinterpret_cast<const uint4*>(rb + (((2 * q) ^ sw) << 4));
+    v.hi = *reinterpret_cast<const uint4*>(rb + (((2 * q + 1) ^ sw) << 4));
+    if ((P >> q) & 1) {
+      uint32_t t[16];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint4 T = thr[q][k];
+        t[4 * k] = T.x;
+        t[4 * k + 1] = T.y;
+        t[4 * k + 2] = T.z;
+        t[4 * k + 3] = T.w;
+      }
+      enc4_run(v, t, w4[2 * q], w4[2 * q + 1]);
+      w2[q] = 0u;
+    } else {
+      const uint4 T = thr[q][0];
+      w2[q] = enc2_run(v, T.x, T.y, T.z);
+      w4[2 * q] = w4[2 * q + 1] = 0u;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kE3Threads, 1)
+    encode3_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ Enc3Maps om,
+                   const __grid_constant__ QArgs a, int use_tma) {
+  extern __shared__ uint8_t dsm_raw[];
+  uint8_t* dsm = dsm_raw + ((1024u - (smem_u32(dsm_raw) & 1023u)) & 1023u);
+  __shared__ uint64_t full[kE3Stages], empty[kE3Stages];
+  __shared__ Enc3Ctx cx;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t M = a.M;
+  const int ng = a.ng, nrc = a.nrc;
+  const int nct3 = ng / kE3Groups;
+  const int slab = warp & 3, qsel = warp >> 2;
+  const int rr = slab * 32 + lane;  // this lane's row in the tile
+  const int sw = rr & 7;            // its 128-byte swizzle phase
+  uint8_t* cscale = dsm + kE3OffScale;
+  uint8_t* czero = dsm + kE3OffZero;
+  if (tid == 0) {
+    for (int s = 0; s < kE3Stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kE3Threads / 32);
+    }
+    fence_mbar_init();
+  }
+  grid_dependency_wait();  // the selection, parameters and 2nd-order table are final
+  post_prologue(a);
+  const int64_t ntiles = (int64_t)nct3 * nrc;
+  const int G = (int)gridDim.x;
+  const int64_t S0 = ntiles * blockIdx.x / G, S1 = ntiles * (blockIdx.x + 1) / G;
+  const int64_t ntile_cta = S1 - S0;
+  int a_ct = (int)(S0 / nrc), a_rc = (int)(S0 % nrc);  // thread 0: the next tile to load
+  auto issue = [&](int s) {
+    uint8_t* dst = dsm + (size_t)s * kE3Tile;
+    mbar_arrive_expect_tx(&full[s], kE3Tile);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      tma_load_2d(dst + j * kBoxBytes, &tmap, &full[s], a_ct * kE3Cols + 64 * j,
+                  a_rc * kChunkRows);
+    if (++a_rc == nrc) {
+      a_rc = 0;
+      ++a_ct;
+    }
+  };
+  __syncthreads();  // barrier initialisation visible
+  if (tid == 0 && use_tma)
+    for (int s = 0; s < kE3Stages && s < ntile_cta; ++s) issue(s);
+  const int P256 = a.cl.period * kGroup2;
+  const int rp = P256 / ng;                              // divides 16 here
+  const int64_t full_rows = a.cl.nfull * kGroup2 / ng;  // rows whose scales lie in full chunks
+  bool failed = false;
+  uint32_t bad = 0;  // thread 0: stages whose wait ran out
+  int cur_ct = -1;
+  int ct = (int)(S0 / nrc), rc = (int)(S0 % nrc);
+  for (int64_t i = 0; i < ntile_cta; ++i) {
+    const int s = (int)(i % kE3Stages);
+    const uint32_t ph = (uint32_t)((i / kE3Stages) & 1);
+    if (ct != cur_ct) {
+      // a new column tile: every warp is done with the old context and the
+      // constant blocks' last TMA stores have read them
+      if (cur_ct >= 0) {
+        if (tid == 0) bulk_wait_read<0>();
+        __syncthreads();
+      }
+      const int64_t g = (int64_t)ct * kE3Groups + warp;  // warp w builds group w
+      uint32_t t = 0x7C007C00u;  // +inf: never reached
+      int kind = kEncKindNone, pr = 0, gs = 0;
+      uint16_t sh = 0;
+      int8_t z = 0;
+      if (g < ng) {
+        pr = a.ws.prec[g];
+        const GroupParams& p = a.ws.params[2 * g + pr];
+        if (lane < 15) t = (uint32_t)p.thresh[lane] * 0x00010001u;
+        kind = (p.flags & kFlagRegular) ? (pr ? kEncKind4 : kEncKind2) : kEncKindIrr;
+        gs = (int)min64(kGroup1, a.K - g * kGroup1);
+        sh = (uint16_t)p.scale_h;
+        z = (int8_t)p.zero;
+      }
+      if (lane < 16) (&cx.thr[warp][0].x)[lane] = t;
+      if (lane == 0) {
+        cx.kind[warp] = (uint8_t)kind;
+        cx.gs[warp] = (uint8_t)gs;
+        cx.pr[warp] = (uint8_t)pr;
+      }
+      for (int r = lane; r < kChunkRows; r += 32) {
+        reinterpret_cast<uint16_t*>(cscale + r * 32)[warp] = sh;
+        reinterpret_cast<int8_t*>(czero + r * 16)[warp] = z;
+      }
+      // 2nd-order codes of group w by row phase (rows in full chunks)
+      if (lane < rp) {
+        uint8_t q = 0;
+        if (g < ng) {
+          const int u = (int)(((int64_t)lane * ng + g) % P256);
+          const float4 ch = a.ws.chunk_tab[min(u >> 8, a.cl.ntab_full)];
+          const float s1f = __half2float(__ushort_as_half(sh));
+          const int q2 = f2i_rz(roundf(__fdiv_rn(__fsub_rn(s1f, ch.x), ch.y)));
+          q = (uint8_t)max(0, min(15, q2));
+        }
+        cx.sqrow[lane][warp] = q;
+      }
+      fence_proxy_async_smem();
+      __syncthreads();
+      if (tid < 4) {
+        int pat = 0;
+        for (int q = 0; q < 4; ++q) {
+          const int gi = 4 * tid + q;
+          const int kd = cx.kind[gi];
+          if (cx.gs[gi] != kGroup1 || (kd != kEncKind2 && kd != kEncKind4)) pat = 16;
+          if (pat < 16 && kd == kEncKind4) pat |= 1 << q;
+        }
+        cx.pat[tid] = pat;
+      }
+      __syncthreads();
+      cur_ct = ct;
+    }
+    uint8_t* buf = dsm + (size_t)s * kE3Tile;
+    if (use_tma) {
+      // after a wait ran out the thread stops waiting (outputs are flagged
+      // invalid), so a failed pipeline ends in bounded time
+      const bool ok = failed || mbar_wait(&full[s], ph);
+      if (!ok) {
+        failed = true;
+        if (tid == 0) bad |= 1u << s;
+      }
+    } else {
+      __syncthreads();  // every warp is done with the stage
+      for (int j = 0; j < 2; ++j)
+        tile_fill_at(a.W, M, a.K, buf + j * kTileBytes, rc, 2 * (int64_t)ct + j, 0);
+      __syncthreads();
+    }
+    const int64_t row0 = (int64_t)rc * kChunkRows;
+    const int qq = (qsel + (int)(i & 3)) & 3;  // this warp's quarter of the tile
+    // codes of this lane's row, groups 4 qq .. 4 qq + 3 (box qq of the tile)
+    const uint8_t* rb = buf + qq * kBoxBytes + rr * 128;
+    uint32_t w2[4], w4[8];
+    uint32_t cnt = 0;
+    const uint4(*thr)[4] = &cx.thr[4 * qq];
+    switch (cx.pat[qq]) {
+#define MB_ENC3_CASE(P) \
+  case P:               \
+    enc3_quarter<P>(rb, sw, thr, w2, w4); \
+    break;
+      MB_ENC3_CASE(0) MB_ENC3_CASE(1) MB_ENC3_CASE(2) MB_ENC3_CASE(3)
+      MB_ENC3_CASE(4) MB_ENC3_CASE(5) MB_ENC3_CASE(6) MB_ENC3_CASE(7)
+      MB_ENC3_CASE(8) MB_ENC3_CASE(9) MB_ENC3_CASE(10) MB_ENC3_CASE(11)
+      MB_ENC3_CASE(12) MB_ENC3_CASE(13) MB_ENC3_CASE(14) MB_ENC3_CASE(15)
+#undef MB_ENC3_CASE
+      default:
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int gi = 4 * qq + q;
+          const int kind = cx.kind[gi];
+          const int lo_off = ((2 * q) ^ sw) << 4, hi_off = ((2 * q + 1) ^ sw) << 4;
+          w2[q] = 0u;
+          w4[2 * q] = w4[2 * q + 1] = 0u;
+          if (kind == kEncKind2) {
+            Row16 v;
+            v.lo = *reinterpret_cast<const uint4*>(rb + lo_off);
+            v.hi = *reinterpret_cast<const uint4*>(rb + hi_off);
+            const uint4 T = cx.thr[gi][0];
+            uint32_t w = enc2_run(v, T.x, T.y, T.z);
+            const int gs = cx.gs[gi];
+            if (gs < kGroup1) w &= (1u << (2 * gs)) - 1u;  // columns past K hold code 0
+            w2[q] = w;
+          } else if (kind == kEncKind4) {
+            Row16 v;
+            v.lo = *reinterpret_cast<const uint4*>(rb + lo_off);
+            v.hi = *reinterpret_cast<const uint4*>(rb + hi_off);
+            uint32_t t[16];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint4 T = cx.thr[gi][k];
+              t[4 * k] = T.x;
+              t[4 * k + 1] = T.y;
+              t[4 * k + 2] = T.z;
+              t[4 * k + 3] = T.w;
+            }
+            uint32_t x, y;
+            enc4_run(v, t, x, y);
+            const int gs = cx.gs[gi];
+            if (gs < kGroup1) {
+              x &= gs >= 8 ? 0xFFFFFFFFu : ((1u << (4 * gs)) - 1u);
+              y &= gs <= 8 ? 0u : ((1u << (4 * (gs - 8))) - 1u);
+            }
+            w4[2 * q] = x;
+            w4[2 * q + 1] = y;
+          } else if (kind == kEncKindIrr) {
+            const int64_t g = (int64_t)ct * kE3Groups + gi;
+            const GroupParams& gp = a.ws.params[2 * g + cx.pr[gi]];
+            const uint3 c = enc_irregular(gp, rb, lo_off, hi_off, cx.gs[gi]);
+            if (cx.pr[gi]) {
+              w4[2 * q] = c.x;
+              w4[2 * q + 1] = c.y;
+            } else {
+              w2[q] = c.x;
+            }
+            cnt += c.z;
+          }
+        }
+    }
+    // the tile's stage is free once every warp has read its part
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    const int64_t row = row0 + rr;
+    if (cnt && row < M) atomicAdd(a.ws.row_counts + row, (int)cnt);
+    // 2nd-order codes of this lane's row
+    uint32_t q4;
+    if (row < full_rows) {
+      q4 = *reinterpret_cast<const uint32_t*>(&cx.sqrow[(int)(row & (rp - 1))][4 * qq]);
+    } else {
+      q4 = 0;
+      if (row < M) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint16_t shb = reinterpret_cast<const uint16_t*>(cscale)[4 * qq + q];
+          q4 |= (uint32_t)sq_direct(a, __half2float(__ushort_as_half(shb)), row,
+                                    (int64_t)ct * kE3Groups + 4 * qq + q)
+                << (8 * q);
+        }
+      }
+    }
+    // staging buffer (i & 1): the stores of two tiles ago have read it
+    const int b = (int)(i & 1);
+    uint8_t* s2 = dsm + kE3OffOut + b * kE3Out;
+    uint8_t* s4 = s2 + kE3P2;
+    uint8_t* ssq = s4 + kE3P4;
+    if (tid == 0) bulk_wait_read<1>();
+    __syncthreads();
+    *reinterpret_cast<uint4*>(s2 + rr * 64 + ((qq ^ ((rr >> 1) & 3)) << 4)) =
+        make_uint4(w2[0], w2[1], w2[2], w2[3]);
+    *reinterpret_cast<uint4*>(s4 + rr * 128 + (((2 * qq) ^ sw) << 4)) =
+        make_uint4(w4[0], w4[1], w4[2], w4[3]);
+    *reinterpret_cast<uint4*>(s4 + rr * 128 + (((2 * qq + 1) ^ sw) << 4)) =
+        make_uint4(w4[4], w4[5], w4[6], w4[7]);
+    *reinterpret_cast<uint32_t*>(ssq + rr * 16 + 4 * qq) = q4;
+    fence_proxy_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+      const int x = ct * kE3Groups, y = (int)row0;
+      tma_store_2d(&om.p2, s2, x, y);
+      tma_store_2d(&om.p4, s4, 2 * x, y);
+      tma_store_2d(&om.sq, ssq, x, y);
+      tma_store_2d(&om.sc, cscale, x, y);
+      tma_store_2d(&om.z, czero, x, y);
+      bulk_commit();
+      // refill this stage once every warp has released it
+      if (use_tma && i + kE3Stages < ntile_cta && !failed) {
+        if (mbar_wait(&empty[s], ph)) {
+          fence_proxy_async_smem();
+          issue(s);
+        } else {
+          failed = true;
+        }
+      }
+    }
+    if (++rc == nrc) {
+      rc = 0;
+      ++ct;
+    }
+  }
+  grid_launch_dependents();
+  if (tid == 0) bulk_wait<0>();  // the CTA's stores are complete
+  failed = __syncthreads_or(failed) != 0;
+  if (tid == 0) {
+    if (failed) atomicOr(&a.ws.hdr->status, kStatusTimeout);
+    for (int s = 0; s < kE3Stages; ++s)
+      if (bad & (1u << s)) (void)mbar_wait(&full[s], 0u), (void)mbar_wait(&full[s], 1u);
+  }
+  post_rowptr_scan<kE3Threads>(a);
 }
 
 
@@ -2820,6 +3188,28 @@ extern "C" mb_status mb_quantize(const void* weights_fp16, int64_t M, int64_t K,
     enc_grid = std::max<int64_t>(
         1, std::min<int64_t>({ntiles, (int64_t)sms * std::max(per_sm, 1), (int64_t)kMaxEncGrid}));
   }
+  // the wide-tile encode with whole-tile TMA stores: ng % 16 == 0 and 16-byte
+  // aligned outputs
+  Enc3Maps omaps;
+  std::memset(&omaps, 0, sizeof(omaps));
+  const auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  const uint64_t um = (uint64_t)M, ung = (uint64_t)ng;
+  const bool enc3 =
+      (ng % kE3Groups == 0) && al16(packed_2bit) && al16(packed_4bit) &&
+      al16(scales_1st_fp16) && al16(zeros_1st) && al16(scales_1st_quant) &&
+      make_tensor_map_2d(&omaps.p2, packed_2bit, 4, um, ung, kChunkRows, 16, 64) &&
+      make_tensor_map_2d(&omaps.p4, packed_4bit, 4, um, 2 * ung, kChunkRows, 32, 128) &&
+      make_tensor_map_2d(&omaps.sc, scales_1st_fp16, 2, um, ung, kChunkRows, 16, 0) &&
+      make_tensor_map_2d(&omaps.z, zeros_1st, 1, um, ung, kChunkRows, 16, 0) &&
+      make_tensor_map_2d(&omaps.sq, scales_1st_quant, 1, um, ung, kChunkRows, 16, 0);
+  int64_t enc3_grid = 1;
+  if (enc3) {
+    static std::atomic<int> occ3[64];
+    int per_sm = 1;
+    MB_CUDA_TRY(blocks_per_sm_once(encode3_kernel, kE3Threads, kE3Smem, occ3, 64, &per_sm));
+    enc3_grid = std::max<int64_t>(
+        1, std::min<int64_t>((ng / kE3Groups) * nrc, (int64_t)sms * std::max(per_sm, 1)));
+  }
   qa.enc_grid = (int)enc_grid;
   {
     auto kern = sens ? stats_kernel<true> : stats_kernel<false>;
@@ -2835,6 +3225,12 @@ extern "C" mb_status mb_quantize(const void* weights_fp16, int64_t M, int64_t K,
   }
   if (mb_status st = launch_pdl(exact_kernel, dim3(kExactCtas), dim3(256), 0, stream, qa))
     return st;
+  if (enc3) {
+    if (mb_status st = launch_pdl(encode3_kernel, dim3((unsigned)enc3_grid), dim3(kE3Threads),
+                                  kE3Smem, stream, tmap, omaps, qa, tma ? 1 : 0))
+      return st;
+    return MB_OK;
+  }
   {
     const auto al = [](const void* p, unsigned m) {
       return (reinterpret_cast<uintptr_t>(p) & (m - 1)) == 0;
