@@ -685,6 +685,89 @@ def sub_gptq(tokens=262144, reps=2):
                                      "flops": "N*K*(K+1) per Hessian (symmetric)"}}}
 
 
+def sub_rowsplit(ws, rank, steps=5, warmup=2):
+    """Config 5: the Llama-70B MLP pair (28672x8192 and 8192x28672, 0.2% x10
+    outliers, lognormal(0, 2) hessian, ratio 0.25) with each matrix's rows
+    split over the ranks (memboost_b200.rowsplit: records all-gathered over
+    NCCL, identical selection on every rank, pending groups settled from
+    gathered column strips, slab encodes, CSR offsets all-gathered); at one
+    GPU the plain quantize of each whole matrix.  All ranks take part; the
+    step time is the max over ranks."""
+    import torch
+
+    from memboost_b200 import _C, rowsplit
+    from memboost_b200 import workloads as wl
+    dev = torch.device("cuda", torch.cuda.current_device())
+    mats = []
+    for i, (M, K) in enumerate(((28672, 8192), (8192, 28672))):
+        g = torch.Generator(device=dev)
+        g.manual_seed(5 + i)
+        w = torch.randn((M, K), generator=g, device=dev) * 0.015
+        idx = torch.randint(0, M * K, (int(round(M * K * 0.002)),), generator=g, device=dev)
+        w.view(-1)[idx] *= 10.0
+        h = torch.randn((K,), generator=g, device=dev).mul_(2.0).exp_()
+        mats.append((w.half(), h))
+        del w
+    comm = rowsplit.DistComm() if ws > 1 else None
+    slabs = []
+    for w, h in mats:
+        b = rowsplit.slab_bounds(w.shape[0], w.shape[1], ws)[rank]
+        slabs.append((w[b[0]:b[1]].contiguous(), h, w.shape[0], w.shape[1]))
+    info = {}
+
+    def step():
+        for j, (ws_, h, M, K) in enumerate(slabs):
+            if comm is None:
+                r = _C.quantize(ws_, 0.25, h)
+                info[j] = (0, 0)
+            else:
+                r = rowsplit.quantize_rows(ws_, M, K, 0.25, h, comm)
+                info[j] = (r.n_pending, r.need)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(ws)
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(ws, t0.elapsed_time(t1)) / steps
+    fp16 = sum(2 * w.numel() for w, _ in mats)
+    return {"workload": "mlp_70b pair: 28672x8192 + 8192x28672 fp16 N(0,0.015^2), 0.2% x10 "
+                        "outliers, lognormal(0,2) hessian, ratio 0.25; rows split over the ranks",
+            "value": round(fp16 / (ms / 1e3) / 1e9, 2), "unit": UNIT, "ms_per_step": round(ms, 3),
+            "n_gpus": ws, "steps": steps,
+            "pending_groups": [info[j][0] for j in range(len(mats))],
+            "path": "memboost_b200.rowsplit.quantize_rows (NCCL all-gathers)" if ws > 1 else
+                    "memboost_b200._C.quantize on each whole matrix"}
+
+
+def sub_gptq_stream(ws, rank, n_layers=2):
+    """Layer-streaming GPTQ of the Llama-2-7B-shaped decoder (synthetic
+    weights, 128 x 2048 calibration tokens): per layer the calibration
+    forward with tcgen05 Hessians, GPTQ + quantize of the seven projections
+    and the re-forward through the quantized layer; with several ranks the
+    samples, Hessians, inverses and GPTQ rows are split."""
+    import torch
+
+    from memboost_b200 import llama, rowsplit
+    comm = rowsplit.DistComm() if ws > 1 else None
+    cfg = llama.LlamaConfig()
+    _, st = llama.quantize_llama_synthetic(cfg, n_samples=128, seq_len=2048, comm=comm,
+                                           n_layers=n_layers)
+    sec = [max_over_ranks(ws, s) for s in st["seconds_per_layer"]]
+    return {"workload": "layer-streaming GPTQ, Llama-2-7B-shaped layers (synthetic weights), "
+                        "128 x 2048 calibration tokens, ratio 0.1",
+            "layers": n_layers, "seconds_per_layer": [round(x, 3) for x in sec],
+            "s_per_layer_after_first": round(sum(sec[1:]) / max(1, len(sec) - 1), 3),
+            "compression_ratio": round(st["compression_ratio"], 3), "n_gpus": ws}
+
+
 # ---------------------------------------------------------------------------
 # reference arm
 # ---------------------------------------------------------------------------
@@ -836,12 +919,17 @@ def main():
             print(json.dumps(run_reference_arm(args, ws, rank, local)), flush=True)
         return
     line, shapes, wl = run_ours(args, ws, rank, local)
-    if ws == 1 and not args.no_sub:
+    if not args.no_sub:
         import torch
         torch.cuda.empty_cache()
-        line["mlp_pair"] = sub_mlp_pair()
-        line["single_4096"] = sub_single_4096()
-        line["gptq_layer"] = sub_gptq()
+        if ws == 1:
+            line["mlp_pair"] = sub_mlp_pair()
+            line["single_4096"] = sub_single_4096()
+            line["gptq_layer"] = sub_gptq()
+        torch.cuda.empty_cache()
+        line["mlp_70b_rowsplit"] = sub_rowsplit(ws, rank)
+        torch.cuda.empty_cache()
+        line["gptq_stream"] = sub_gptq_stream(ws, rank)
     if rank == 0:
         if ws == 1 and not args.no_cpu_baseline:
             import torch

@@ -165,6 +165,60 @@ mb_status mb_quantize_noalloc(const void* weights_fp16, int64_t M, int64_t K, do
                               int64_t outlier_capacity, int64_t* nnz_host, mb_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * Row-split quantize -- one matrix's rows over several processes (GPUs); no
+ * counterpart in the reference, which quantizes a matrix on one device
+ * (core/torch_ops.cu:105-264).  The results equal mb_quantize on the whole
+ * matrix bit for bit.  Rank p holds the row slab [r0_p, r1_p) of W (slab
+ * boundaries multiples of 256 / gcd(ceil(K / 16), 256) rows, so no 2nd-order
+ * chunk of 256 scales spans two ranks) and a workspace of
+ * mb_quantize_workspace_size(M_slab, K) bytes.  Sequence per rank:
+ *   1. mb_rows_stats: stream the slab, write one 32-byte record per group
+ *      (mb_rows_record_bytes(K) bytes: min, max, prediction and moment of
+ *      the slab's sensitivity terms, rows, flags);
+ *   2. all-gather the records of all ranks in rank order (the caller's
+ *      collective; P * mb_rows_record_bytes(K) bytes);
+ *   3. mb_rows_select: group parameters and the 4-bit selection from the
+ *      gathered records -- identical on every rank.  counts[0] = groups left
+ *      pending (their sensitivity intervals straddle the boundary), counts[1]
+ *      = how many of them are 4-bit; pending_groups[0 .. counts[0]) lists
+ *      them (device memory, ascending);
+ *   4. if counts[0] > 0: the caller settles them by their exact serial sums
+ *      over all M_total rows -- e.g. gathers their column strips from every
+ *      rank, quantizes the strip matrix with ratio (counts[1] + 0.5) /
+ *      counts[0] and reads its group_precision -- and passes the result to
+ *      mb_rows_set_precision (always required before step 5 when counts[0]
+ *      > 0);
+ *   5. mb_rows_encode: the slab's outputs (as mb_quantize on the slab: its
+ *      rows of every [M, *] output, its ceil(M_slab * ng / 256) 2nd-order
+ *      entries, outlier row pointers local to the slab -- add the outlier
+ *      counts of the earlier ranks -- and *nnz_device); CSR values / columns
+ *      by mb_quantize_extract_outliers on the slab.
+ * ------------------------------------------------------------------------- */
+size_t mb_rows_record_bytes(int64_t K);
+
+mb_status mb_rows_stats(const void* weights_slab, int64_t M_slab, int64_t K, double ratio_4bit,
+                        const float* hessian_diag, int64_t hessian_numel, void* records,
+                        void* workspace, size_t workspace_bytes, mb_stream_t stream);
+
+mb_status mb_rows_select(const void* records_all, int n_ranks, int64_t M_total,
+                         const void* weights_slab, int64_t M_slab, int64_t K, double ratio_4bit,
+                         const float* hessian_diag, int64_t hessian_numel, void* workspace,
+                         size_t workspace_bytes, int32_t* pending_groups, int32_t* counts,
+                         mb_stream_t stream);
+
+mb_status mb_rows_set_precision(void* workspace, size_t workspace_bytes, int64_t M_slab,
+                                int64_t K, const int32_t* groups, const uint8_t* precision,
+                                int64_t n, mb_stream_t stream);
+
+mb_status mb_rows_encode(const void* weights_slab, int64_t M_slab, int64_t K, double ratio_4bit,
+                         const float* hessian_diag, int64_t hessian_numel, int32_t* packed_2bit,
+                         int32_t* packed_4bit, void* scales_1st_fp16, int8_t* zeros_1st,
+                         void* scales_2nd_fp16, int8_t* zeros_2nd, uint8_t* scales_1st_quant,
+                         uint8_t* group_precision, int32_t* outlier_row_ptrs,
+                         int32_t* nnz_device, void* workspace, size_t workspace_bytes,
+                         mb_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * dequantize -- replaces memboost::dequantize_op (core/torch_ops.h:24-29,
  * core/torch_ops.cu:267-301; bound as _C.dequantize, core/bindings.cpp:31-38).
  * out[r, c] = fp16(float(scales_1st[r, g]) * (q - zeros_1st[r, g])), no
@@ -266,6 +320,17 @@ mb_status mb_gptq_quantize(const float* W, int64_t M, int64_t K, const float* hi
                            const uint8_t* group_precision, int blocksize, int scalar_division,
                            float* Q, void* workspace, size_t workspace_bytes,
                            mb_stream_t stream);
+
+/* Rows [row0, row1) of gptq_quantize's Q (written to Q_rows, [row1 - row0,
+ * K]), with each group's min / max and scale over all M rows of W as the
+ * reference computes them (models/llama.py:248-263) -- the per-rank part of
+ * GPTQ with W's rows split over GPUs (rows are independent given Hinv_cho and
+ * the group parameters).  Q_rows equals rows [row0, row1) of mb_gptq_quantize
+ * bit for bit. */
+mb_status mb_gptq_quantize_rows(const float* W, int64_t M, int64_t K, int64_t row0, int64_t row1,
+                                const float* hinv_cho, const uint8_t* group_precision,
+                                int blocksize, int scalar_division, float* Q_rows,
+                                void* workspace, size_t workspace_bytes, mb_stream_t stream);
 
 #ifdef __cplusplus
 }

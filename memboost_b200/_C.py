@@ -42,6 +42,19 @@ _lib.mb_quantize_flags.argtypes = [_P, ctypes.c_size_t, _I64, _I64,
 _lib.mb_quantize_csr.restype = ctypes.c_int
 _lib.mb_quantize_csr.argtypes = ([_P, _I64, _I64, ctypes.c_double, _P, _I64] + [_P] * 10 +
                                  [_P, _P, _I64, _P, ctypes.c_size_t, _P])
+_lib.mb_rows_record_bytes.restype = ctypes.c_size_t
+_lib.mb_rows_record_bytes.argtypes = [_I64]
+_lib.mb_rows_stats.restype = ctypes.c_int
+_lib.mb_rows_stats.argtypes = [_P, _I64, _I64, ctypes.c_double, _P, _I64, _P, _P,
+                               ctypes.c_size_t, _P]
+_lib.mb_rows_select.restype = ctypes.c_int
+_lib.mb_rows_select.argtypes = [_P, ctypes.c_int, _I64, _P, _I64, _I64, ctypes.c_double, _P, _I64,
+                                _P, ctypes.c_size_t, _P, _P, _P]
+_lib.mb_rows_set_precision.restype = ctypes.c_int
+_lib.mb_rows_set_precision.argtypes = [_P, ctypes.c_size_t, _I64, _I64, _P, _P, _I64, _P]
+_lib.mb_rows_encode.restype = ctypes.c_int
+_lib.mb_rows_encode.argtypes = [_P, _I64, _I64, ctypes.c_double, _P, _I64] + [_P] * 10 + \
+    [_P, ctypes.c_size_t, _P]
 _lib.mb_quantize_info.restype = ctypes.c_int
 _lib.mb_quantize_info.argtypes = [_P, ctypes.c_size_t, _I64, _I64,
                                   ctypes.POINTER(ctypes.c_uint32), _P]
@@ -62,6 +75,9 @@ _lib.mb_hessian.restype = ctypes.c_int
 _lib.mb_hessian.argtypes = [_P, _I64, _I64, ctypes.c_int, ctypes.c_float, ctypes.c_int, _P, _P, _P]
 _lib.mb_gptq_workspace_size.restype = ctypes.c_size_t
 _lib.mb_gptq_workspace_size.argtypes = [_I64, _I64]
+_lib.mb_gptq_quantize_rows.restype = ctypes.c_int
+_lib.mb_gptq_quantize_rows.argtypes = [_P, _I64, _I64, _I64, _I64, _P, _P, ctypes.c_int,
+                                       ctypes.c_int, _P, _P, ctypes.c_size_t, _P]
 _lib.mb_gptq_quantize.restype = ctypes.c_int
 _lib.mb_gptq_quantize.argtypes = [_P, _I64, _I64, _P, _P, ctypes.c_int, ctypes.c_int, _P, _P,
                                   ctypes.c_size_t, _P]
@@ -511,8 +527,10 @@ def hessian(x: torch.Tensor, alpha: float = 1.0, out: torch.Tensor | None = None
 
 def gptq_quantize(W: torch.Tensor, Hinv_cho: torch.Tensor, group_precision: torch.Tensor,
                   blocksize: int = 128, scalar_division: int = GPTQ_DIV_RECIPROCAL,
-                  out: torch.Tensor | None = None) -> torch.Tensor:
-    """gptq_quantize of models/llama.py:234-294 on the GPU (fp32 [M, K])."""
+                  out: torch.Tensor | None = None, rows: tuple | None = None) -> torch.Tensor:
+    """gptq_quantize of models/llama.py:234-294 on the GPU (fp32 [M, K]);
+    with ``rows`` = (r0, r1) only those rows of Q ([r1 - r0, K]), the group
+    parameters still taken over all rows of W."""
     if W.dim() != 2 or W.dtype != torch.float32 or not W.is_cuda:
         raise RuntimeError("W must be a 2D float32 CUDA tensor")
     W = W.contiguous()
@@ -524,14 +542,18 @@ def gptq_quantize(W: torch.Tensor, Hinv_cho: torch.Tensor, group_precision: torc
     gp = group_precision.to(device=dev, dtype=torch.uint8).contiguous()
     if gp.numel() != K // GROUP_SIZE_1ST:
         raise RuntimeError("group_precision must hold K // 16 entries")
+    r0, r1 = (0, M) if rows is None else (int(rows[0]), int(rows[1]))
     with torch.cuda.device(dev):
         hc = Hinv_cho.contiguous()
         if out is None:
-            out = torch.empty_like(W)
+            out = torch.empty((r1 - r0, K), dtype=torch.float32, device=dev)
+        elif tuple(out.shape) != (r1 - r0, K) or out.dtype != torch.float32 or \
+                not out.is_contiguous() or out.device != dev:
+            raise RuntimeError("out must be a contiguous float32 [rows, K] tensor on W's device")
         ws = torch.empty(int(_lib.mb_gptq_workspace_size(M, K)), dtype=torch.uint8, device=dev)
-        _check(_lib.mb_gptq_quantize(_ptr(W), M, K, _ptr(hc), _ptr(gp), int(blocksize),
-                                     int(scalar_division), _ptr(out), _ptr(ws), ws.numel(),
-                                     _stream(dev)))
+        _check(_lib.mb_gptq_quantize_rows(_ptr(W), M, K, r0, r1, _ptr(hc), _ptr(gp),
+                                          int(blocksize), int(scalar_division), _ptr(out),
+                                          _ptr(ws), ws.numel(), _stream(dev)))
     return out
 
 

@@ -117,7 +117,7 @@ template <bool kRecip>
 __global__ void __launch_bounds__(128)
     gptq_block_kernel(const float* __restrict__ W, int64_t M, int64_t K,
                       const float* __restrict__ Hc, const GptqGroup* __restrict__ groups,
-                      float* __restrict__ Q) {
+                      float* __restrict__ Q, int64_t row0) {
   extern __shared__ float hs[];  // [kGB][kGB]: Hinv_cho[bs + j, bs + c]
   __shared__ GptqGroup gsh[kGB / kGroup1];
   const int64_t bs = (int64_t)blockIdx.x * kGB;
@@ -133,10 +133,11 @@ __global__ void __launch_bounds__(128)
                            : GptqGroup{0.0f, 0.0f, 0.0f, 0.0f, 3.0f, {0.0f, 0.0f, 0.0f}};
   }
   __syncthreads();
-  const int64_t row = (int64_t)blockIdx.y * blockDim.x + threadIdx.x;
+  // rows [row0, M) of W; Q holds them from its first row
+  const int64_t row = row0 + (int64_t)blockIdx.y * blockDim.x + threadIdx.x;
   if (row >= M) return;
   const float* wr = W + row * K + bs;
-  float* qr = Q + row * K + bs;
+  float* qr = Q + (row - row0) * K + bs;
   float w[kGB];
   if (n == kGB) {
 #pragma unroll
@@ -164,13 +165,13 @@ __global__ void __launch_bounds__(128)
 }
 
 template <bool kRecip>
-mb_status launch_block(const float* W, int64_t M, int64_t K, const float* Hc,
+mb_status launch_block(const float* W, int64_t row0, int64_t row1, int64_t K, const float* Hc,
                        const GptqGroup* groups, float* Q, cudaStream_t stream) {
   constexpr size_t smem = sizeof(float) * kGB * kGB;
   static std::atomic<uint64_t> attr_done{0};
   MB_CUDA_TRY(set_smem_limit_once(gptq_block_kernel<kRecip>, (int)smem, attr_done));
-  gptq_block_kernel<kRecip><<<dim3((unsigned)ceil_div(K, kGB), (unsigned)ceil_div(M, 128)), 128,
-                              smem, stream>>>(W, M, K, Hc, groups, Q);
+  gptq_block_kernel<kRecip><<<dim3((unsigned)ceil_div(K, kGB), (unsigned)ceil_div(row1 - row0, 128)),
+                              128, smem, stream>>>(W, row1, K, Hc, groups, Q, row0);
   MB_LAUNCH_CHECK("gptq_block_kernel");
   return MB_OK;
 }
@@ -186,18 +187,34 @@ extern "C" size_t mb_gptq_workspace_size(int64_t M, int64_t K) {
   return align_up(sizeof(GptqGroup) * (size_t)ceil_div(K, kGroup1), 256);
 }
 
+extern "C" mb_status mb_gptq_quantize_rows(const float* W, int64_t M, int64_t K, int64_t row0,
+                                           int64_t row1, const float* hinv_cho,
+                                           const uint8_t* group_precision, int blocksize,
+                                           int scalar_division, float* Q_rows, void* workspace,
+                                           size_t workspace_bytes, mb_stream_t stream_);
+
 extern "C" mb_status mb_gptq_quantize(const float* W, int64_t M, int64_t K, const float* hinv_cho,
                                       const uint8_t* group_precision, int blocksize,
                                       int scalar_division, float* Q, void* workspace,
                                       size_t workspace_bytes, mb_stream_t stream_) {
+  return mb_gptq_quantize_rows(W, M, K, 0, M, hinv_cho, group_precision, blocksize,
+                               scalar_division, Q, workspace, workspace_bytes, stream_);
+}
+
+extern "C" mb_status mb_gptq_quantize_rows(const float* W, int64_t M, int64_t K, int64_t row0,
+                                           int64_t row1, const float* hinv_cho,
+                                           const uint8_t* group_precision, int blocksize,
+                                           int scalar_division, float* Q, void* workspace,
+                                           size_t workspace_bytes, mb_stream_t stream_) {
   clear_error();
+  MB_REQUIRE(row0 >= 0 && row0 < row1 && row1 <= M, "row range must be inside [0, M)");
   MB_REQUIRE(W && hinv_cho && group_precision && Q, "null pointer");
   MB_REQUIRE(M > 0 && K > 0, "W must be a non-empty [M, K] matrix");
   MB_REQUIRE(K % kGroup1 == 0, "K must be a multiple of 16 (whole column groups)");
   MB_REQUIRE(blocksize == kGB, "blocksize must be 128");
   MB_REQUIRE(scalar_division == MB_GPTQ_DIV_TRUE || scalar_division == MB_GPTQ_DIV_RECIPROCAL,
              "unknown scalar_division mode");
-  MB_REQUIRE(M <= 65535LL * 128, "too many rows");
+  MB_REQUIRE(row1 - row0 <= 65535LL * 128, "too many rows");
   MB_REQUIRE(((reinterpret_cast<uintptr_t>(W) | reinterpret_cast<uintptr_t>(Q)) & 15u) == 0,
              "W and Q must be 16-byte aligned");
   MB_REQUIRE(W != Q, "Q must not alias W");
@@ -209,6 +226,6 @@ extern "C" mb_status mb_gptq_quantize(const float* W, int64_t M, int64_t K, cons
   gptq_group_kernel<<<(unsigned)ng, 256, 0, stream>>>(W, M, K, group_precision, groups);
   MB_LAUNCH_CHECK("gptq_group_kernel");
   return scalar_division == MB_GPTQ_DIV_RECIPROCAL
-             ? launch_block<true>(W, M, K, hinv_cho, groups, Q, stream)
-             : launch_block<false>(W, M, K, hinv_cho, groups, Q, stream);
+             ? launch_block<true>(W, row0, row1, K, hinv_cho, groups, Q, stream)
+             : launch_block<false>(W, row0, row1, K, hinv_cho, groups, Q, stream);
 }

@@ -804,7 +804,8 @@ struct QArgs {
   int n4;      // 4-bit groups to select
   int select;  // the selection runs (sensitivity needed)
   int w_aligned;
-  int enc_grid;  // CTAs of the encode kernel
+  int no_select;  // stats stops after the per-group totals (row-split slabs)
+  int enc_grid;   // CTAs of the encode kernel
   // encode / post outputs
   int32_t* packed2;
   int32_t* packed4;
@@ -1960,7 +1961,7 @@ __global__ void __launch_bounds__(kStatsThreads, 2)
       if (bad & (1u << s)) (void)mbar_wait(&full[s], 0u), (void)mbar_wait(&full[s], 1u);
   }
   __syncthreads();
-  if (s_select) {
+  if (s_select && !A.no_select) {
     __threadfence();
     select_all(A, dsm, (size_t)kStages * kTileBytes);
   }
@@ -3080,31 +3081,55 @@ mb_status launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t
   return MB_OK;
 }
 
-}  // namespace
-}  // namespace mb
+// Everything a quantize call launches, prepared on the host: arguments,
+// tensor maps and grids.
+struct QuantizeLaunch {
+  QArgs qa;
+  CUtensorMap tmap;
+  Enc3Maps omaps;
+  bool tma, enc3, sens;
+  int vec_out;
+  int64_t stats_grid, enc_grid, enc3_grid;
+  size_t hdr_bytes;
+};
 
-using namespace mb;
-
-extern "C" size_t mb_quantize_workspace_size(int64_t M, int64_t K) {
-  if (M <= 0 || K <= 0) return 0;
-  return workspace_layout(M, K, nullptr, nullptr);
+int device_sms() {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) != cudaSuccess) return sms;
+  static std::atomic<int> sm_cache[64];
+  if (dev < 64 && sm_cache[dev].load(std::memory_order_acquire) > 0)
+    return sm_cache[dev].load(std::memory_order_acquire);
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) sms = 148;
+  if (dev < 64) sm_cache[dev].store(sms, std::memory_order_release);
+  return sms;
 }
 
-extern "C" mb_status mb_quantize(const void* weights_fp16, int64_t M, int64_t K,
-                                 double ratio_4bit, const float* hessian_diag,
-                                 int64_t hessian_numel, int32_t* packed_2bit,
-                                 int32_t* packed_4bit, void* scales_1st_fp16, int8_t* zeros_1st,
-                                 void* scales_2nd_fp16, int8_t* zeros_2nd,
-                                 uint8_t* scales_1st_quant, uint8_t* group_precision,
-                                 int32_t* outlier_row_ptrs, int32_t* nnz_device, void* workspace,
-                                 size_t workspace_bytes, mb_stream_t stream_) {
-  clear_error();
-  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+// CTAs of encode_kernel (persistent: every CTA resident); the selection
+// splits the tiles among them.
+mb_status legacy_enc_grid(int64_t ntiles, int sms, int64_t* grid) {
+  static std::atomic<int> occ[64];
+  int per_sm = 1;
+  MB_CUDA_TRY(blocks_per_sm_once(encode_kernel, kEncThreads, kEncSmem, occ, 64, &per_sm));
+  *grid = std::max<int64_t>(
+      1, std::min<int64_t>({ntiles, (int64_t)sms * std::max(per_sm, 1), (int64_t)kMaxEncGrid}));
+  return MB_OK;
+}
+
+// Validation and set-up shared by mb_quantize and the row-split entry points.
+// With stats_only the outputs are not needed (may be null).
+mb_status quantize_prepare(const void* weights_fp16, int64_t M, int64_t K, double ratio_4bit,
+                           const float* hessian_diag, int64_t hessian_numel, int32_t* packed_2bit,
+                           int32_t* packed_4bit, void* scales_1st_fp16, int8_t* zeros_1st,
+                           void* scales_2nd_fp16, int8_t* zeros_2nd, uint8_t* scales_1st_quant,
+                           uint8_t* group_precision, int32_t* outlier_row_ptrs,
+                           int32_t* nnz_device, void* workspace, size_t workspace_bytes,
+                           bool stats_only, QuantizeLaunch& L) {
   if (mb_status st = check_common(weights_fp16, M, K)) return st;
-  MB_REQUIRE(packed_2bit && packed_4bit && scales_1st_fp16 && zeros_1st && scales_2nd_fp16 &&
-                 zeros_2nd && scales_1st_quant && group_precision && outlier_row_ptrs &&
-                 nnz_device,
-             "output pointers must not be null");
+  if (!stats_only)
+    MB_REQUIRE(packed_2bit && packed_4bit && scales_1st_fp16 && zeros_1st && scales_2nd_fp16 &&
+                   zeros_2nd && scales_1st_quant && group_precision && outlier_row_ptrs &&
+                   nnz_device,
+               "output pointers must not be null");
   const int64_t ng = ceil_div(K, kGroup1);
   const size_t need = workspace_layout(M, K, nullptr, nullptr);
   if (workspace == nullptr || workspace_bytes < need)
@@ -3130,12 +3155,12 @@ extern "C" mb_status mb_quantize(const void* weights_fp16, int64_t M, int64_t K,
     n4 = (int64_t)(int)(ratio_4bit * (double)(int)ng);  // torch_ops.cu:172
     n4 = std::max<int64_t>(0, std::min<int64_t>(n4, ng));
   }
-  const bool sens = selecting && n4 > 0;
+  L.sens = selecting && n4 > 0;
   const bool w_aligned = (reinterpret_cast<uintptr_t>(weights_fp16) & 15u) == 0;
+  L.hdr_bytes = sizeof(Header) + sizeof(uint32_t) * nct;
 
-  MB_CUDA_TRY(cudaMemsetAsync(ws.hdr, 0, sizeof(Header) + sizeof(uint32_t) * nct, stream));
-
-  QArgs qa;
+  QArgs& qa = L.qa;
+  std::memset(&qa, 0, sizeof(qa));
   qa.W = static_cast<const __half*>(weights_fp16);
   qa.M = M;
   qa.K = K;
@@ -3147,8 +3172,9 @@ extern "C" mb_status mb_quantize(const void* weights_fp16, int64_t M, int64_t K,
   qa.gp = group_precision;
   qa.cl = chunk_layout(M, ng);
   qa.n4 = (int)n4;
-  qa.select = sens;
+  qa.select = L.sens;
   qa.w_aligned = w_aligned;
+  qa.no_select = 0;
   qa.packed2 = packed_2bit;
   qa.packed4 = packed_4bit;
   qa.scales1 = static_cast<__half*>(scales_1st_fp16);
@@ -3161,87 +3187,217 @@ extern "C" mb_status mb_quantize(const void* weights_fp16, int64_t M, int64_t K,
 
   // TMA needs a 16-byte aligned base and a row pitch that is a multiple of 16
   // bytes; other inputs fill the same shared-memory layout with plain loads.
-  CUtensorMap tmap;
-  std::memset(&tmap, 0, sizeof(tmap));
-  const bool tma = w_aligned && (K % 8 == 0) &&
-                   make_tensor_map_2d_16bit_sw128(&tmap, weights_fp16, false, (uint64_t)M,
-                                                  (uint64_t)K, kChunkRows, 64);
-  int dev = 0, sms = 148;
-  MB_CUDA_TRY(cudaGetDevice(&dev));
-  {
-    static std::atomic<int> sm_cache[64];
-    if (dev < 64 && sm_cache[dev].load(std::memory_order_acquire) > 0) {
-      sms = sm_cache[dev].load(std::memory_order_acquire);
-    } else {
-      MB_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-      if (dev < 64) sm_cache[dev].store(sms, std::memory_order_release);
-    }
-  }
+  std::memset(&L.tmap, 0, sizeof(L.tmap));
+  L.tma = w_aligned && (K % 8 == 0) &&
+          make_tensor_map_2d_16bit_sw128(&L.tmap, weights_fp16, false, (uint64_t)M, (uint64_t)K,
+                                         kChunkRows, 64);
+  const int sms = device_sms();
   const int64_t ntiles = nct * nrc;
   // the encode grid (persistent: every CTA resident), known to the selection,
   // which splits the tiles among its CTAs
-  int64_t enc_grid = 1;
+  if (mb_status st = legacy_enc_grid(ntiles, sms, &L.enc_grid)) return st;
+  qa.enc_grid = (int)L.enc_grid;
   {
-    static std::atomic<int> occ[64];
+    auto kern = L.sens ? stats_kernel<true> : stats_kernel<false>;
+    static std::atomic<int> occ[2][64];
     int per_sm = 1;
-    MB_CUDA_TRY(blocks_per_sm_once(encode_kernel, kEncThreads, kEncSmem, occ, 64, &per_sm));
-    enc_grid = std::max<int64_t>(
-        1, std::min<int64_t>({ntiles, (int64_t)sms * std::max(per_sm, 1), (int64_t)kMaxEncGrid}));
+    MB_CUDA_TRY(blocks_per_sm_once(kern, kStatsThreads, kStatsSmem, occ[L.sens ? 1 : 0], 64,
+                                   &per_sm));
+    // at most one CTA per tile (no empty tile range) and the records' cap
+    L.stats_grid = std::max<int64_t>(
+        1, std::min<int64_t>(stats_grid_cap(ntiles), (int64_t)sms * std::max(per_sm, 1)));
   }
+  L.enc3 = false;
+  L.enc3_grid = 1;
+  L.vec_out = 0;
+  std::memset(&L.omaps, 0, sizeof(L.omaps));
+  if (stats_only) return MB_OK;
   // the wide-tile encode with whole-tile TMA stores: ng % 16 == 0 and 16-byte
   // aligned outputs
-  Enc3Maps omaps;
-  std::memset(&omaps, 0, sizeof(omaps));
   const auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   const uint64_t um = (uint64_t)M, ung = (uint64_t)ng;
-  const bool enc3 =
+  L.enc3 =
       (ng % kE3Groups == 0) && al16(packed_2bit) && al16(packed_4bit) &&
       al16(scales_1st_fp16) && al16(zeros_1st) && al16(scales_1st_quant) &&
-      make_tensor_map_2d(&omaps.p2, packed_2bit, 4, um, ung, kChunkRows, 16, 64) &&
-      make_tensor_map_2d(&omaps.p4, packed_4bit, 4, um, 2 * ung, kChunkRows, 32, 128) &&
-      make_tensor_map_2d(&omaps.sc, scales_1st_fp16, 2, um, ung, kChunkRows, 16, 0) &&
-      make_tensor_map_2d(&omaps.z, zeros_1st, 1, um, ung, kChunkRows, 16, 0) &&
-      make_tensor_map_2d(&omaps.sq, scales_1st_quant, 1, um, ung, kChunkRows, 16, 0);
-  int64_t enc3_grid = 1;
-  if (enc3) {
+      make_tensor_map_2d(&L.omaps.p2, packed_2bit, 4, um, ung, kChunkRows, 16, 64) &&
+      make_tensor_map_2d(&L.omaps.p4, packed_4bit, 4, um, 2 * ung, kChunkRows, 32, 128) &&
+      make_tensor_map_2d(&L.omaps.sc, scales_1st_fp16, 2, um, ung, kChunkRows, 16, 0) &&
+      make_tensor_map_2d(&L.omaps.z, zeros_1st, 1, um, ung, kChunkRows, 16, 0) &&
+      make_tensor_map_2d(&L.omaps.sq, scales_1st_quant, 1, um, ung, kChunkRows, 16, 0);
+  if (L.enc3) {
     static std::atomic<int> occ3[64];
     int per_sm = 1;
     MB_CUDA_TRY(blocks_per_sm_once(encode3_kernel, kE3Threads, kE3Smem, occ3, 64, &per_sm));
-    enc3_grid = std::max<int64_t>(
+    L.enc3_grid = std::max<int64_t>(
         1, std::min<int64_t>((ng / kE3Groups) * nrc, (int64_t)sms * std::max(per_sm, 1)));
   }
-  qa.enc_grid = (int)enc_grid;
-  {
-    auto kern = sens ? stats_kernel<true> : stats_kernel<false>;
-    static std::atomic<int> occ[2][64];
-    int per_sm = 1;
-    MB_CUDA_TRY(blocks_per_sm_once(kern, kStatsThreads, kStatsSmem, occ[sens ? 1 : 0], 64,
-                                   &per_sm));
-    // at most one CTA per tile (no empty tile range) and the records' cap
-    const int64_t grid = std::max<int64_t>(
-        1, std::min<int64_t>(stats_grid_cap(ntiles), (int64_t)sms * std::max(per_sm, 1)));
-    kern<<<(unsigned)grid, kStatsThreads, kStatsSmem, stream>>>(tmap, qa, tma ? 1 : 0);
-    MB_LAUNCH_CHECK("stats_kernel");
-  }
-  if (mb_status st = launch_pdl(exact_kernel, dim3(kExactCtas), dim3(256), 0, stream, qa))
-    return st;
-  if (enc3) {
-    if (mb_status st = launch_pdl(encode3_kernel, dim3((unsigned)enc3_grid), dim3(kE3Threads),
-                                  kE3Smem, stream, tmap, omaps, qa, tma ? 1 : 0))
-      return st;
-    return MB_OK;
-  }
-  {
-    const auto al = [](const void* p, unsigned m) {
-      return (reinterpret_cast<uintptr_t>(p) & (m - 1)) == 0;
-    };
-    const int vec_out = (ng % 8 == 0) && al(packed_2bit, 16) && al(packed_4bit, 16) &&
-                        al(scales_1st_fp16, 16) && al(zeros_1st, 8) && al(scales_1st_quant, 8);
-    if (mb_status st = launch_pdl(encode_kernel, dim3((unsigned)enc_grid), dim3(kEncThreads), kEncSmem,
-                                  stream, tmap, qa, tma ? 1 : 0, vec_out))
-      return st;
-  }
+  const auto al = [](const void* p, unsigned m) {
+    return (reinterpret_cast<uintptr_t>(p) & (m - 1)) == 0;
+  };
+  L.vec_out = (ng % 8 == 0) && al(packed_2bit, 16) && al(packed_4bit, 16) &&
+              al(scales_1st_fp16, 16) && al(zeros_1st, 8) && al(scales_1st_quant, 8);
   return MB_OK;
+}
+
+// The header memset and the stats kernel.
+mb_status launch_stats(const QuantizeLaunch& L, cudaStream_t stream) {
+  MB_CUDA_TRY(cudaMemsetAsync(L.qa.ws.hdr, 0, L.hdr_bytes, stream));
+  auto kern = L.sens ? stats_kernel<true> : stats_kernel<false>;
+  kern<<<(unsigned)L.stats_grid, kStatsThreads, kStatsSmem, stream>>>(L.tmap, L.qa,
+                                                                       L.tma ? 1 : 0);
+  MB_LAUNCH_CHECK("stats_kernel");
+  return MB_OK;
+}
+
+// The tables / exact-sum kernel and the encode kernel (chained with PDL).
+mb_status launch_tables_encode(const QuantizeLaunch& L, cudaStream_t stream) {
+  if (mb_status st = launch_pdl(exact_kernel, dim3(kExactCtas), dim3(256), 0, stream, L.qa))
+    return st;
+  if (L.enc3)
+    return launch_pdl(encode3_kernel, dim3((unsigned)L.enc3_grid), dim3(kE3Threads), kE3Smem,
+                      stream, L.tmap, L.omaps, L.qa, L.tma ? 1 : 0);
+  return launch_pdl(encode_kernel, dim3((unsigned)L.enc_grid), dim3(kEncThreads), kEncSmem,
+                    stream, L.tmap, L.qa, L.tma ? 1 : 0, L.vec_out);
+}
+
+// ---------------------------------------------------------------------------
+// Row-split quantize: one matrix's rows over several processes (GPUs).  Each
+// rank streams its slab of rows (stats without the selection) and exports one
+// 32-byte record per group: min / max, the prediction and moment of the
+// slab's serial-sum terms, the slab's rows and flags.  The records of all
+// ranks, in rank (row) order, give every rank the same group parameters and
+// the same sensitivity intervals as one pass over the whole matrix, so every
+// rank takes the same selection (rows_select_kernel).  Groups left pending
+// are settled by their exact serial sums over all rows (the caller gathers
+// their column strips and quantizes them; mb_rows_set_precision), then each
+// rank builds the 2nd-order tables and encodes its slab.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) rows_pack_kernel(const QArgs a, SegRec* __restrict__ rec) {
+  const int g = blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= a.ng) return;
+  SegRec r;
+  r.sum = a.select ? a.ws.gpred[g] : 0.0;
+  r.mom = a.select ? a.ws.gmom[g] : 0.0;
+  r.mn = a.ws.gmin[g];
+  r.mx = a.ws.gmax[g];
+  r.rows = (uint32_t)a.M;
+  r.flags = a.select ? a.ws.gflag[g] : 0u;
+  rec[g] = r;
+}
+
+// One CTA.  Group totals over the P slabs in row order (warp per group, lanes
+// over slabs: the combine of ct_combine with slabs as segments), parameters
+// of both precisions, intervals over all M_total rows, then the selection.
+__global__ void __launch_bounds__(kStatsThreads, 1)
+    rows_select_kernel(const QArgs A, const SegRec* __restrict__ rec, int P, int64_t M_total,
+                       int32_t* __restrict__ pending, int32_t* __restrict__ counts) {
+  extern __shared__ uint8_t dsm_raw[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int ng = A.ng;
+  for (int g = warp; g < ng; g += kStatsThreads / 32) {
+    float mn = INFINITY, mx = -INFINITY;
+    uint32_t flags = 0;
+    double carry = 0.0, mom = 0.0;
+    for (int pp = 0; pp < P; pp += 32) {
+      const int p = pp + lane;
+      double sum = 0.0, smom = 0.0;
+      uint32_t rows = 0;
+      if (p < P) {
+        const SegRec r = rec[(size_t)p * ng + g];
+        sum = r.sum;
+        smom = r.mom;
+        rows = r.rows;
+        mn = fminf(mn, r.mn);
+        mx = fmaxf(mx, r.mx);
+        flags |= r.flags;
+      }
+      double incl = sum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const double y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      mom += smom + (carry + (incl - sum)) * (16.0 * (double)rows);
+      carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    mn = warp_min(mn);
+    mx = warp_max(mx);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mom += __shfl_xor_sync(0xffffffffu, mom, o);
+    flags = __reduce_or_sync(0xffffffffu, flags);
+    if (lane == 0) {
+      A.ws.gmin[g] = mn;
+      A.ws.gmax[g] = mx;
+      if (A.select) {
+        A.ws.gpred[g] = carry;
+        A.ws.gmom[g] = mom;
+        A.ws.gflag[g] = flags;
+        A.ws.gkey[g] = sens_interval_of(flags, carry, mom, M_total);
+      }
+    }
+    group_params_warp(A.ws.params, A.ws.gscale, A.ws.greg, g, mn, mx, lane);
+  }
+  __threadfence();
+  __syncthreads();
+  select_from_intervals<kStatsThreads>(A, dsm_raw, (size_t)kStages * kTileBytes);
+  __syncthreads();
+  const Header* h = A.ws.hdr;
+  const uint32_t np = *reinterpret_cast<const volatile uint32_t*>(&h->n_pend);
+  const uint32_t nd = *reinterpret_cast<const volatile uint32_t*>(&h->n_dec);
+  for (uint32_t i = tid; i < np; i += kStatsThreads) pending[i] = A.ws.order[nd + i];
+  if (tid == 0) {
+    counts[0] = (int32_t)np;
+    counts[1] = np ? (int32_t)*reinterpret_cast<const volatile uint32_t*>(&h->need) : 0;
+  }
+}
+
+// The precisions of the pending groups, decided by the caller; nothing stays
+// pending afterwards.
+__global__ void rows_set_kernel(const QArgs a, const int32_t* __restrict__ groups,
+                                const uint8_t* __restrict__ prec, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int32_t g = groups[i];
+    if (g >= 0 && g < a.ng) a.ws.prec[g] = prec[i] ? 1 : 0;
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    a.ws.hdr->n_pend = 0;
+    a.ws.hdr->n_dec = (uint32_t)a.ng;
+  }
+  // the tile split of encode_kernel (uniform), which the selection leaves
+  // open while groups are pending
+  if (blockIdx.x == 0) enc_partition<256>(a, nullptr, nullptr);
+}
+
+}  // namespace
+}  // namespace mb
+
+using namespace mb;
+
+extern "C" size_t mb_quantize_workspace_size(int64_t M, int64_t K) {
+  if (M <= 0 || K <= 0) return 0;
+  return workspace_layout(M, K, nullptr, nullptr);
+}
+
+extern "C" mb_status mb_quantize(const void* weights_fp16, int64_t M, int64_t K,
+                                 double ratio_4bit, const float* hessian_diag,
+                                 int64_t hessian_numel, int32_t* packed_2bit,
+                                 int32_t* packed_4bit, void* scales_1st_fp16, int8_t* zeros_1st,
+                                 void* scales_2nd_fp16, int8_t* zeros_2nd,
+                                 uint8_t* scales_1st_quant, uint8_t* group_precision,
+                                 int32_t* outlier_row_ptrs, int32_t* nnz_device, void* workspace,
+                                 size_t workspace_bytes, mb_stream_t stream_) {
+  clear_error();
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  QuantizeLaunch L;
+  if (mb_status st = quantize_prepare(weights_fp16, M, K, ratio_4bit, hessian_diag,
+                                      hessian_numel, packed_2bit, packed_4bit, scales_1st_fp16,
+                                      zeros_1st, scales_2nd_fp16, zeros_2nd, scales_1st_quant,
+                                      group_precision, outlier_row_ptrs, nnz_device, workspace,
+                                      workspace_bytes, false, L))
+    return st;
+  if (mb_status st = launch_stats(L, stream)) return st;
+  return launch_tables_encode(L, stream);
 }
 
 extern "C" mb_status mb_quantize_extract_outliers(const void* weights_fp16, int64_t M, int64_t K,
@@ -3336,4 +3492,105 @@ extern "C" mb_status mb_quantize_flags(const void* workspace, size_t workspace_b
                               stream));
   MB_CUDA_TRY(cudaStreamSynchronize(stream));
   return MB_OK;
+}
+
+// ---- row-split quantize ----
+
+extern "C" size_t mb_rows_record_bytes(int64_t K) {
+  return K > 0 ? (size_t)ceil_div(K, kGroup1) * sizeof(SegRec) : 0;
+}
+
+extern "C" mb_status mb_rows_stats(const void* weights_slab, int64_t M_slab, int64_t K,
+                                   double ratio_4bit, const float* hessian_diag,
+                                   int64_t hessian_numel, void* records, void* workspace,
+                                   size_t workspace_bytes, mb_stream_t stream_) {
+  clear_error();
+  MB_REQUIRE(records != nullptr, "records must not be null");
+  MB_REQUIRE((reinterpret_cast<uintptr_t>(records) & 15u) == 0,
+             "records must be 16-byte aligned");
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  QuantizeLaunch L;
+  if (mb_status st = quantize_prepare(weights_slab, M_slab, K, ratio_4bit, hessian_diag,
+                                      hessian_numel, nullptr, nullptr, nullptr, nullptr, nullptr,
+                                      nullptr, nullptr, nullptr, nullptr, nullptr, workspace,
+                                      workspace_bytes, true, L))
+    return st;
+  L.qa.no_select = 1;
+  if (mb_status st = launch_stats(L, stream)) return st;
+  rows_pack_kernel<<<(unsigned)ceil_div(L.qa.ng, 256), 256, 0, stream>>>(
+      L.qa, static_cast<SegRec*>(records));
+  MB_LAUNCH_CHECK("rows_pack_kernel");
+  return MB_OK;
+}
+
+extern "C" mb_status mb_rows_select(const void* records_all, int n_ranks, int64_t M_total,
+                                    const void* weights_slab, int64_t M_slab, int64_t K,
+                                    double ratio_4bit, const float* hessian_diag,
+                                    int64_t hessian_numel, void* workspace,
+                                    size_t workspace_bytes, int32_t* pending_groups,
+                                    int32_t* counts, mb_stream_t stream_) {
+  clear_error();
+  MB_REQUIRE(records_all && pending_groups && counts, "null argument");
+  MB_REQUIRE(n_ranks >= 1, "n_ranks must be >= 1");
+  MB_REQUIRE(M_total >= M_slab, "M_total must cover the slab");
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  QuantizeLaunch L;
+  if (mb_status st = quantize_prepare(weights_slab, M_slab, K, ratio_4bit, hessian_diag,
+                                      hessian_numel, nullptr, nullptr, nullptr, nullptr, nullptr,
+                                      nullptr, nullptr, nullptr, nullptr, nullptr, workspace,
+                                      workspace_bytes, true, L))
+    return st;
+  const int smem = kStages * kTileBytes;
+  static std::atomic<uint64_t> attr_done{0};
+  MB_CUDA_TRY(set_smem_limit_once(rows_select_kernel, smem, attr_done));
+  rows_select_kernel<<<1, kStatsThreads, smem, stream>>>(
+      L.qa, static_cast<const SegRec*>(records_all), n_ranks, M_total, pending_groups, counts);
+  MB_LAUNCH_CHECK("rows_select_kernel");
+  return MB_OK;
+}
+
+extern "C" mb_status mb_rows_set_precision(void* workspace, size_t workspace_bytes,
+                                           int64_t M_slab, int64_t K, const int32_t* groups,
+                                           const uint8_t* precision, int64_t n,
+                                           mb_stream_t stream_) {
+  clear_error();
+  MB_REQUIRE(workspace != nullptr, "workspace must not be null");
+  MB_REQUIRE(n == 0 || (groups && precision), "null argument");
+  MB_REQUIRE(M_slab > 0 && K > 0, "M and K must be positive");
+  if (workspace_bytes < workspace_layout(M_slab, K, nullptr, nullptr))
+    return set_error(MB_ERR_WORKSPACE, "workspace too small");
+  QArgs qa;
+  std::memset(&qa, 0, sizeof(qa));
+  workspace_layout(M_slab, K, static_cast<char*>(workspace), &qa.ws);
+  qa.ng = (int)ceil_div(K, kGroup1);
+  qa.nct = (int)ceil_div(K, kTileCols);
+  qa.nrc = (int)ceil_div(M_slab, kChunkRows);
+  int64_t eg = 1;
+  if (mb_status st = legacy_enc_grid((int64_t)qa.nct * qa.nrc, device_sms(), &eg)) return st;
+  qa.enc_grid = (int)eg;
+  rows_set_kernel<<<1, 256, 0, reinterpret_cast<cudaStream_t>(stream_)>>>(qa, groups, precision,
+                                                                           n);
+  MB_LAUNCH_CHECK("rows_set_kernel");
+  return MB_OK;
+}
+
+extern "C" mb_status mb_rows_encode(const void* weights_slab, int64_t M_slab, int64_t K,
+                                    double ratio_4bit, const float* hessian_diag,
+                                    int64_t hessian_numel, int32_t* packed_2bit,
+                                    int32_t* packed_4bit, void* scales_1st_fp16,
+                                    int8_t* zeros_1st, void* scales_2nd_fp16, int8_t* zeros_2nd,
+                                    uint8_t* scales_1st_quant, uint8_t* group_precision,
+                                    int32_t* outlier_row_ptrs, int32_t* nnz_device,
+                                    void* workspace, size_t workspace_bytes,
+                                    mb_stream_t stream_) {
+  clear_error();
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  QuantizeLaunch L;
+  if (mb_status st = quantize_prepare(weights_slab, M_slab, K, ratio_4bit, hessian_diag,
+                                      hessian_numel, packed_2bit, packed_4bit, scales_1st_fp16,
+                                      zeros_1st, scales_2nd_fp16, zeros_2nd, scales_1st_quant,
+                                      group_precision, outlier_row_ptrs, nnz_device, workspace,
+                                      workspace_bytes, false, L))
+    return st;
+  return launch_tables_encode(L, stream);
 }

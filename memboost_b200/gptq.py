@@ -102,7 +102,8 @@ def compute_group_precision(W: torch.Tensor, h_diag: torch.Tensor, ratio_4bit: f
 
 
 def gptq_quantize(W: torch.Tensor, Hinv_cho: torch.Tensor, group_precision: torch.Tensor,
-                  blocksize: int = 128, scalar_division: int | None = None) -> torch.Tensor:
+                  blocksize: int = 128, scalar_division: int | None = None,
+                  rows: tuple | None = None) -> torch.Tensor:
     """Q of llama.py:234-294 (fp32 [M, K]), bit-identical to the reference.
 
     ``scalar_division`` picks which run of the reference to reproduce:
@@ -112,7 +113,7 @@ def gptq_quantize(W: torch.Tensor, Hinv_cho: torch.Tensor, group_precision: torc
     if scalar_division is None:
         scalar_division = GPTQ_DIV_RECIPROCAL
     return _C.gptq_quantize(W, Hinv_cho, group_precision, blocksize=blocksize,
-                            scalar_division=scalar_division)
+                            scalar_division=scalar_division, rows=rows)
 
 
 def forced_hessian_diag(group_precision: torch.Tensor, K: int, device=None) -> torch.Tensor:
@@ -185,4 +186,68 @@ def quantize_layer(weights: dict, inputs: dict, ratio_4bit: float = 0.1,
         h_diag, hinv_cho = inv[LAYER_INPUTS[name]]
         out[name] = make_quantized_linear(W, h_diag, hinv_cho, ratio_4bit,
                                           blocksize=blocksize).q_weight
+    return out
+
+
+def even_rows(M: int, world: int) -> list[tuple[int, int]]:
+    """Contiguous, as-even-as-possible row ranges of M rows over `world` ranks."""
+    return [(M * r // world, M * (r + 1) // world) for r in range(world)]
+
+
+def quantize_layer_distributed(weights: dict, inputs_local: dict, comm, ratio_4bit: float = 0.1,
+                               blocksize: int = 128, inverses: dict | None = None) -> dict:
+    """One layer's GPTQ (llama.py:530-617) with the calibration tokens and the
+    weight rows split over ranks; every rank ends with the same
+    QuantizedTensors.
+
+    * Hessians: each rank accumulates x^T x over its own tokens
+      (``inputs_local``: key -> [tokens_r, K]) on the tcgen05 kernel; the
+      partial sums are all-reduced (NCCL) and divided by the total token count
+      (llama.py:523-528, 547-551).
+    * Inverses: the four damped Cholesky inverses (llama.py:177-203) run on
+      different ranks (key i on rank i mod world) and are broadcast.
+    * GPTQ: each rank updates its rows of every weight (mb_gptq_quantize_rows,
+      group parameters over all rows), the fp16 rows are all-gathered, and the
+      memboost quantize (llama.py:331-371) runs on the whole Q.
+    Given the same inverses (``inverses``: key -> (h_diag, Hinv_cho)) the
+    result equals quantize_layer's bit for bit; the all-reduced Hessians
+    differ from one device's accumulation only by fp32 summation order.
+    ``comm``: rowsplit.DistComm or rowsplit.LocalComm."""
+    if inverses is None:
+        inverses = {}
+        keys = list(inputs_local)
+        dev = next(iter(inputs_local.values())).device
+        tok = torch.tensor([float(sum(int(x.reshape(-1, x.shape[-1]).shape[0])
+                                      for x in inputs_local.values()) / max(1, len(keys)))],
+                           dtype=torch.float64, device=dev)
+        total = float(comm.all_reduce_sum(tok).item())
+        for i, key in enumerate(keys):
+            x = inputs_local[key].reshape(-1, inputs_local[key].shape[-1])
+            K = int(x.shape[1])
+            H = hessian(x) if x.shape[0] > 0 else torch.zeros((K, K), device=x.device)
+            H = comm.all_reduce_sum(H)
+            H.div_(total)
+            owner = i % comm.world
+            if comm.rank == owner:
+                h_diag, hc = gptq_inverse(H)
+            else:
+                h_diag = torch.empty((K,), dtype=torch.float32, device=x.device)
+                hc = torch.empty((K, K), dtype=torch.float32, device=x.device)
+            del H
+            inverses[key] = (comm.broadcast(h_diag, owner), comm.broadcast(hc, owner))
+    out = {}
+    for name, W in weights.items():
+        h_diag, hc = inverses[LAYER_INPUTS[name]]
+        M, K = W.shape
+        if ratio_4bit > 0:
+            gp = compute_group_precision(W, h_diag, ratio_4bit)
+        else:
+            gp = torch.zeros(K // GROUP_SIZE, dtype=torch.uint8, device=W.device)
+        r0, r1 = even_rows(M, comm.world)[comm.rank]
+        Qs = gptq_quantize(W, hc, gp, blocksize=blocksize, rows=(r0, r1))
+        Q = comm.all_gather_rows(Qs.to(torch.float16)).contiguous()
+        if ratio_4bit > 0:
+            out[name] = quantize(Q, ratio_4bit=ratio_4bit, hessian_diag=forced_hessian_diag(gp, K))
+        else:
+            out[name] = quantize(Q, ratio_4bit=0.0)
     return out
