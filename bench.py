@@ -685,6 +685,56 @@ def sub_gptq(tokens=262144, reps=2):
                                      "flops": "N*K*(K+1) per Hessian (symmetric)"}}}
 
 
+def sub_qgemv(reps=50, copies=8):
+    """GEMV over the packed format (memboost_b200.qgemv, outliers applied) on
+    the quantized MLP pair: `copies` quantized copies of each matrix rotated
+    (more than the L2 together), the calls recorded once in a CUDA graph so
+    the number is device time; roofline from the bytes the kernel must read."""
+    import torch
+
+    import memboost_b200 as mb
+    from memboost_b200 import workloads as wl
+    dev = torch.device("cuda", torch.cuda.current_device())
+    pk, kind = peaks()
+    out = {}
+    for c in wl.mlp_7b():
+        M, K = c.weights.shape
+        w, h = c.weights.to(dev), c.hessian_diag.to(dev)
+        qts = [mb.quantize(w, c.ratio_4bit, h) for _ in range(copies)]
+        x = (torch.randn(K, generator=torch.Generator().manual_seed(1)) * 0.1).half().to(dev)
+        ys = [torch.empty(M, device=dev) for _ in qts]
+        ng = (K + 15) // 16
+        n4 = int(qts[0].group_precision.sum())
+        nnz = int(qts[0].nnz)
+        # code words of each group's own precision, scale, zero, precision, x,
+        # y, row pointers, CSR
+        alg = M * ((ng - n4) * 4 + n4 * 8 + ng * 3) + ng + 2 * K + 4 * M + 4 * (M + 1) + 6 * nnz
+        for q, y in zip(qts, ys):
+            mb.qgemv(q, x, out=y)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for q, y in zip(qts, ys):
+                mb.qgemv(q, x, out=y)
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (reps * copies)
+        out[f"{M}x{K}"] = {"us": round(us, 2), "algorithmic_bytes": alg,
+                           "achieved": round(alg / us / 1e3, 1),
+                           "frac": round(alg / us / 1e3 / pk["hbm_gbs"], 4),
+                           "fp16_gemv_equiv_gbs": round(2 * M * K / us / 1e3, 1)}
+        del qts, ys, g
+    return {"what": "y = W x from the packed words (mb_qgemv), outliers written back; "
+                    f"{copies} rotated copies, CUDA-graph replay", "of": f"{kind} hbm_gbs",
+            **out}
+
+
 def sub_rowsplit(ws, rank, steps=5, warmup=2):
     """Config 5: the Llama-70B MLP pair (28672x8192 and 8192x28672, 0.2% x10
     outliers, lognormal(0, 2) hessian, ratio 0.25) with each matrix's rows
@@ -926,6 +976,7 @@ def main():
             line["mlp_pair"] = sub_mlp_pair()
             line["single_4096"] = sub_single_4096()
             line["gptq_layer"] = sub_gptq()
+            line["qgemv"] = sub_qgemv()
         torch.cuda.empty_cache()
         line["mlp_70b_rowsplit"] = sub_rowsplit(ws, rank)
         torch.cuda.empty_cache()

@@ -65,6 +65,7 @@ constexpr int kTileBytes = 2 * kBoxBytes;         // 32 KB
 constexpr int kStages = 3;     // stats tile ring per CTA (two CTAs per SM)
 constexpr int kEncStages = 2;  // encode tile ring (its staging buffers take the rest)
 constexpr int kStatsSmem = kStages * kTileBytes + 1024;   // + alignment slack
+constexpr int kCombSmem = 96 * 1024;  // the selection's key / cost scratch
 constexpr int kEncSmem = kEncStages * kTileBytes + 1024;
 // encode CTA size: 8 warps, two CTAs per SM.  The items are taken from a
 // shared counter, so any warp count works; 10 or 12 warps (96 / 80
@@ -373,42 +374,50 @@ __device__ void group_scalars(float gmin, float gmax, int L, GroupParams& p) {
   p.scale_h = __half_as_ushort(__float2half_rn(scale));
 }
 
-// Parameters of group g for both precisions (one warp): lanes 0-2 find the
-// 2-bit thresholds, lanes 3-17 the 4-bit ones.  Also the compact copies of
-// the two fp16 scales and regular flags.
+// Parameters of group g for both precisions (one warp; lanes 0 and 1 write
+// them): scale, zero point, outlier threshold, regular flag, and the compact
+// copies of the two fp16 scales and regular flags.  The code thresholds are
+// left to group_thresholds_warp (later, grid-parallel): finding them is the
+// costly part and only encode needs them.
 __device__ void group_params_warp(GroupParams* params, uint32_t* gscale, uint8_t* greg, int64_t g,
                                   float mn, float mx, int lane) {
+  GroupParams q2, q4;
+  group_scalars(mn, mx, 4, q2);
+  group_scalars(mn, mx, 16, q4);
+  if (lane == 0) {
+    gscale[g] = (uint32_t)q2.scale_h | ((uint32_t)q4.scale_h << 16);
+    greg[g] = (uint8_t)((q2.flags & kFlagRegular) | ((q4.flags & kFlagRegular) << 1));
+  }
+  if (lane < 2) {
+    const GroupParams& p = lane ? q4 : q2;
+    GroupParams* d = params + 2 * g + lane;
+    d->gmin = p.gmin;
+    d->gmax = p.gmax;
+    d->scale = p.scale;
+    d->thr = p.thr;
+    d->zero = p.zero;
+    d->levels = p.levels;
+    d->flags = p.flags;
+    d->scale_h = p.scale_h;
+  }
+}
+
+// Code thresholds of group g for both precisions (one warp): lanes 0-2 find
+// the 2-bit thresholds, lanes 3-17 the 4-bit ones, from the parameters
+// group_params_warp wrote; unused slots and irregular groups get +inf.
+__device__ void group_thresholds_warp(GroupParams* params, int64_t g, int lane) {
   GroupParams* p2 = params + 2 * g;
   GroupParams* p4 = p2 + 1;
-  {
-    GroupParams q2, q4;
-    group_scalars(mn, mx, 4, q2);
-    group_scalars(mn, mx, 16, q4);
-    if (lane == 0) {
-      gscale[g] = (uint32_t)q2.scale_h | ((uint32_t)q4.scale_h << 16);
-      greg[g] = (uint8_t)((q2.flags & kFlagRegular) | ((q4.flags & kFlagRegular) << 1));
-    }
-  }
   if (lane < 18) {
     const bool four = lane >= 3;
     const int L = four ? 16 : 4;
     const int level = four ? lane - 2 : lane + 1;
-    GroupParams p;
-    group_scalars(mn, mx, L, p);
+    const GroupParams* d = four ? p4 : p2;
+    const float gmin = __ldcg(&d->gmin), scale = __ldcg(&d->scale);
+    const int flags = __ldcg(&d->flags);
     const uint16_t T =
-        (p.flags & kFlagRegular) ? find_threshold(mn, p.scale, L, level) : (uint16_t)0x7C00;
-    GroupParams* d = four ? p4 : p2;
-    d->thresh[level - 1] = T;
-    if (lane == 0 || lane == 3) {
-      d->gmin = p.gmin;
-      d->gmax = p.gmax;
-      d->scale = p.scale;
-      d->thr = p.thr;
-      d->zero = p.zero;
-      d->levels = p.levels;
-      d->flags = p.flags;
-      d->scale_h = p.scale_h;
-    }
+        (flags & kFlagRegular) ? find_threshold(gmin, scale, L, level) : (uint16_t)0x7C00;
+    (four ? p4 : p2)->thresh[level - 1] = T;
   } else {
     const int jx = lane - 18;  // 0..13: unused threshold slots
     if (jx < 13)
@@ -804,8 +813,11 @@ struct QArgs {
   int n4;      // 4-bit groups to select
   int select;  // the selection runs (sensitivity needed)
   int w_aligned;
-  int no_select;  // stats stops after the per-group totals (row-split slabs)
-  int enc_grid;   // CTAs of the encode kernel
+  int no_select;       // the combine stops after the per-group totals (row-split slabs)
+  int exact_thresholds;  // the exact kernel finds the code thresholds (row-split encode)
+  int stats_grid;      // CTAs of the stats kernel (the segment records' layout)
+  int comb_smem;       // dynamic shared memory of the combine kernel (selection scratch)
+  int enc_grid;        // CTAs of the encode kernel
   // encode / post outputs
   int32_t* packed2;
   int32_t* packed4;
@@ -1663,7 +1675,7 @@ __device__ __noinline__ void ct_combine(const QArgs& A, int ct, int warp, int la
   const int64_t g = (int64_t)ct * kTileGroups + warp;
   if (g >= A.ng) return;
   const int64_t M = A.M;
-  const int nrc = A.nrc, G = (int)gridDim.x, ntiles = A.nct * A.nrc;
+  const int nrc = A.nrc, G = A.stats_grid, ntiles = A.nct * A.nrc;
   const int64_t u0 = (int64_t)ct * nrc, u1 = u0 + nrc;
   // the CTAs holding the column tile's first and last chunk
   const int b0 = (int)floor_div_small((u0 + 1) * G - 1, ntiles);
@@ -1719,9 +1731,6 @@ __device__ __noinline__ void ct_combine(const QArgs& A, int ct, int warp, int la
   group_params_warp(A.ws.params, A.ws.gscale, A.ws.greg, g, mn, mx, lane);
 }
 
-__device__ __noinline__ void select_all(const QArgs& A, uint8_t* scratch, size_t bytes) {
-  select_from_intervals<kStatsThreads>(A, scratch, bytes);
-}
 
 // stats: persistent CTAs, each streaming its contiguous range of tiles
 // (column-major) through a TMA ring, one warp per group of the current tile.
@@ -1740,7 +1749,7 @@ __global__ void __launch_bounds__(kStatsThreads, 2)
   // shared array keeps the pointer in the shared space (plain LDS)
   uint8_t* dsm = dsm_raw + ((1024u - (smem_u32(dsm_raw) & 1023u)) & 1023u);
   __shared__ uint64_t full[kStages];
-  __shared__ int s_flag, s_select;
+
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t M = A.M, K = A.K;
   const int nrc = A.nrc, nct = A.nct;
@@ -1763,7 +1772,6 @@ __global__ void __launch_bounds__(kStatsThreads, 2)
       ++ct_ahead;
     }
   };
-  if (tid == 0) s_select = 0;
   if (tid == 0 && use_tma) {
     for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
     fence_mbar_init();
@@ -1925,26 +1933,11 @@ __global__ void __launch_bounds__(kStatsThreads, 2)
     if (ct == 0)
       for (int r = tid; r < kChunkRows; r += kStatsThreads)
         if (row0 + r < M) A.ws.row_counts[row0 + r] = 0;
-    if (seg_last) __threadfence();
     __syncthreads();  // the stage is free
     if (tid == 0 && use_tma && u_ahead < u_end) issue(st);
     if (++st == kStages) {
       st = 0;
       ph ^= 1u;
-    }
-    if (seg_last) {
-      // the column tile's chunks done so far; the CTA completing it combines
-      const uint32_t len = (uint32_t)(rc - seg_rc0 + 1);
-      if (tid == 0) s_flag = atomicAdd(&A.ws.ct_count[ct], len) + len == (uint32_t)nrc;
-      __syncthreads();
-      if (s_flag) {
-        __threadfence();
-        ct_combine<kSens>(A, ct, warp, lane);
-        __threadfence();
-        __syncthreads();
-        // the last column tile can only complete at this CTA's last tile
-        if (tid == 0) s_select = atomicAdd(&A.ws.hdr->ticket_ct, 1u) == (uint32_t)nct - 1u;
-      }
     }
     if (++rc == nrc) {
       rc = 0;
@@ -1956,15 +1949,39 @@ __global__ void __launch_bounds__(kStatsThreads, 2)
   if (tid == 0) {
     if (failed) atomicOr(&A.ws.hdr->status, kStatusTimeout);
     // loads whose wait ran out may still be in flight: let them land (the
-    // stage's last issued phase, bounded) before the ring is reused
+    // stage's last issued phase, bounded) before the CTA exits
     for (int s = 0; s < kStages; ++s)
       if (bad & (1u << s)) (void)mbar_wait(&full[s], 0u), (void)mbar_wait(&full[s], 1u);
   }
-  __syncthreads();
-  if (s_select && !A.no_select) {
-    __threadfence();
-    select_all(A, dsm, (size_t)kStages * kTileBytes);
+}
+
+// combine: a warp per group (grid-stride) adds the group's segment records
+// in row order (ct_combine): min / max, sensitivity interval, the parameters
+// of both precisions and their code thresholds.  The CTA finishing last
+// selects the 4-bit groups (torch_ops.cu:149-179) and splits the encode
+// tiles.  Launched after stats with programmatic dependent launch.
+constexpr int kCombThreads = 256;
+template <bool kSens>
+__global__ void __launch_bounds__(kCombThreads, 1)
+    combine_kernel(const __grid_constant__ QArgs A) {
+  extern __shared__ uint8_t csm[];
+  __shared__ int s_last;
+  const int tid = threadIdx.x, lane = tid & 31;
+  grid_dependency_wait();  // every segment record written
+  const int64_t nw = (int64_t)gridDim.x * (kCombThreads / 32);
+  for (int64_t g = ((int64_t)blockIdx.x * kCombThreads + tid) >> 5; g < A.ng; g += nw) {
+    ct_combine<kSens>(A, (int)(g / kTileGroups), (int)(g % kTileGroups), lane);
+    __syncwarp();  // the parameters lanes 0 and 1 wrote
+    group_thresholds_warp(A.ws.params, g, lane);
   }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = atomicAdd(&A.ws.hdr->ticket_ct, 1u) == gridDim.x - 1u;
+  __syncthreads();
+  grid_launch_dependents();
+  if (!s_last || A.no_select) return;
+  __threadfence();
+  select_from_intervals<kCombThreads>(A, csm, (size_t)A.comb_smem);
 }
 
 // ---------------------------------------------------------------------------
@@ -2201,6 +2218,14 @@ __device__ __noinline__ void tables_grid(const QArgs& a) {
 // on other streams can use meanwhile.
 __global__ void __launch_bounds__(256) exact_kernel(const __grid_constant__ QArgs a) {
   grid_dependency_wait();  // stats and the selection complete
+  // every group's code thresholds for both precisions (a warp per group),
+  // when the combine kernel did not find them (row-split slabs)
+  if (a.exact_thresholds) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t g = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; g < a.ng; g += nw)
+      group_thresholds_warp(a.ws.params, g, lane);
+  }
   if (*reinterpret_cast<const volatile uint32_t*>(&a.ws.hdr->n_pend) == 0)
     tables_grid(a);
   else
@@ -3089,7 +3114,7 @@ struct QuantizeLaunch {
   Enc3Maps omaps;
   bool tma, enc3, sens;
   int vec_out;
-  int64_t stats_grid, enc_grid, enc3_grid;
+  int64_t stats_grid, comb_grid, enc_grid, enc3_grid;
   size_t hdr_bytes;
 };
 
@@ -3207,6 +3232,17 @@ mb_status quantize_prepare(const void* weights_fp16, int64_t M, int64_t K, doubl
     L.stats_grid = std::max<int64_t>(
         1, std::min<int64_t>(stats_grid_cap(ntiles), (int64_t)sms * std::max(per_sm, 1)));
   }
+  qa.stats_grid = (int)L.stats_grid;
+  qa.exact_thresholds = 0;
+  L.comb_grid = std::max<int64_t>(1, std::min<int64_t>(ceil_div(ng, kCombThreads / 32), sms));
+  {
+    // the selection's scratch: keys when they do not fit in registers, then
+    // the column tiles' encode costs and their prefix (small CTAs let other
+    // matrices' kernels share the SMs)
+    size_t need = (ng > (int64_t)kSelKPT * kCombThreads) ? (size_t)ng * 8 : 0;
+    need = ((need + (size_t)nct * 4 + 7) & ~(size_t)7) + (size_t)(nct + 1) * 8 + 256;
+    qa.comb_smem = (int)std::min<size_t>(need, (size_t)kCombSmem);
+  }
   L.enc3 = false;
   L.enc3_grid = 1;
   L.vec_out = 0;
@@ -3246,7 +3282,11 @@ mb_status launch_stats(const QuantizeLaunch& L, cudaStream_t stream) {
   kern<<<(unsigned)L.stats_grid, kStatsThreads, kStatsSmem, stream>>>(L.tmap, L.qa,
                                                                        L.tma ? 1 : 0);
   MB_LAUNCH_CHECK("stats_kernel");
-  return MB_OK;
+  auto comb = L.sens ? combine_kernel<true> : combine_kernel<false>;
+  static std::atomic<uint64_t> attr_done[2];
+  MB_CUDA_TRY(set_smem_limit_once(comb, kCombSmem, attr_done[L.sens ? 1 : 0]));
+  return launch_pdl(comb, dim3((unsigned)L.comb_grid), dim3(kCombThreads),
+                    (size_t)L.qa.comb_smem, stream, L.qa);
 }
 
 // The tables / exact-sum kernel and the encode kernel (chained with PDL).
@@ -3592,5 +3632,6 @@ extern "C" mb_status mb_rows_encode(const void* weights_slab, int64_t M_slab, in
                                       group_precision, outlier_row_ptrs, nnz_device, workspace,
                                       workspace_bytes, false, L))
     return st;
+  L.qa.exact_thresholds = 1;  // the selection took the parameters from all slabs' records
   return launch_tables_encode(L, stream);
 }
