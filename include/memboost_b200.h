@@ -108,6 +108,52 @@ mb_status mb_quantize_csr(const void* weights_fp16, int64_t M, int64_t K, double
                           int64_t outlier_capacity, void* workspace, size_t workspace_bytes,
                           mb_stream_t stream);
 
+/* The arguments of one mb_quantize_csr call. */
+typedef struct mb_quantize_job {
+  const void* weights_fp16;
+  int64_t M, K;
+  double ratio_4bit;
+  const float* hessian_diag;
+  int64_t hessian_numel;
+  int32_t* packed_2bit;
+  int32_t* packed_4bit;
+  void* scales_1st_fp16;
+  int8_t* zeros_1st;
+  void* scales_2nd_fp16;
+  int8_t* zeros_2nd;
+  uint8_t* scales_1st_quant;
+  uint8_t* group_precision;
+  int32_t* outlier_row_ptrs;
+  int32_t* nnz_device;
+  void* outlier_values_fp16;
+  int32_t* outlier_col_indices;
+  int64_t outlier_capacity;
+  void* workspace;
+  size_t workspace_bytes;
+} mb_quantize_job;
+
+/* n mb_quantize_csr calls in one enqueue, with the same results as n
+ * separate calls -- the reference quantizes a model matrix by matrix
+ * (models/llama.py:553-600, one _make_quantized_linear, hence one
+ * quantize_op, each).  Up to 8 consecutive jobs
+ * (same sensitivity pass, i.e. all with or all without a hessian, and
+ * column groups a multiple of 16) run as one launch of each kernel, their
+ * CTAs split among the matrices by size, so the launch and pipeline start-up
+ * costs are paid once per 8 matrices.  Every job is validated before
+ * anything is enqueued; the jobs must not share outputs or workspaces. */
+mb_status mb_quantize_csr_many(const mb_quantize_job* jobs, int64_t n, mb_stream_t stream);
+
+/* Diagnostics: every group's sensitivity, the reference's serial fp32 sum
+ * of its M * 16 terms (core/quantize.cu:72-98), computed by the exact-sum
+ * path that mb_quantize uses for the groups straddling the 4-bit boundary
+ * -- here for all groups -- into sums[ceil(K / 16)], and the selection made
+ * from them into group_precision (the same as mb_quantize's).  Needs a
+ * hessian and a ratio_4bit that selects some but not all groups. */
+mb_status mb_quantize_exact_sums(const void* weights_fp16, int64_t M, int64_t K,
+                                 double ratio_4bit, const float* hessian_diag,
+                                 int64_t hessian_numel, float* sums, uint8_t* group_precision,
+                                 void* workspace, size_t workspace_bytes, mb_stream_t stream);
+
 /* Host-side flags of the last mb_quantize on `workspace` (synchronises the
  * stream).  Bit 0: the 4-bit selection met a tie of equal sensitivities at
  * the selection boundary and broke it by lowest group index (the reference

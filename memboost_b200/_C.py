@@ -42,6 +42,24 @@ _lib.mb_quantize_flags.argtypes = [_P, ctypes.c_size_t, _I64, _I64,
 _lib.mb_quantize_csr.restype = ctypes.c_int
 _lib.mb_quantize_csr.argtypes = ([_P, _I64, _I64, ctypes.c_double, _P, _I64] + [_P] * 10 +
                                  [_P, _P, _I64, _P, ctypes.c_size_t, _P])
+
+
+class QuantizeJob(ctypes.Structure):
+    """mb_quantize_job: the arguments of one mb_quantize_csr call."""
+    _fields_ = [("weights_fp16", _P), ("M", _I64), ("K", _I64), ("ratio_4bit", ctypes.c_double),
+                ("hessian_diag", _P), ("hessian_numel", _I64), ("packed_2bit", _P),
+                ("packed_4bit", _P), ("scales_1st_fp16", _P), ("zeros_1st", _P),
+                ("scales_2nd_fp16", _P), ("zeros_2nd", _P), ("scales_1st_quant", _P),
+                ("group_precision", _P), ("outlier_row_ptrs", _P), ("nnz_device", _P),
+                ("outlier_values_fp16", _P), ("outlier_col_indices", _P),
+                ("outlier_capacity", _I64), ("workspace", _P), ("workspace_bytes", ctypes.c_size_t)]
+
+
+_lib.mb_quantize_csr_many.restype = ctypes.c_int
+_lib.mb_quantize_csr_many.argtypes = [ctypes.POINTER(QuantizeJob), _I64, _P]
+_lib.mb_quantize_exact_sums.restype = ctypes.c_int
+_lib.mb_quantize_exact_sums.argtypes = [_P, _I64, _I64, ctypes.c_double, _P, _I64, _P, _P, _P,
+                                        ctypes.c_size_t, _P]
 _lib.mb_rows_record_bytes.restype = ctypes.c_size_t
 _lib.mb_rows_record_bytes.argtypes = [_I64]
 _lib.mb_rows_stats.restype = ctypes.c_int
@@ -557,6 +575,24 @@ def gptq_quantize(W: torch.Tensor, Hinv_cho: torch.Tensor, group_precision: torc
     return out
 
 
+def exact_sums(weights: torch.Tensor, hessian_diag: torch.Tensor, ratio_4bit: float = 0.5):
+    """Every group's sensitivity (the reference's serial fp32 sum) from the
+    exact-sum path, and the selection made from them (mb_quantize_exact_sums).
+    Returns (sums float32 [ng], group_precision uint8 [ng])."""
+    w = weights.to(torch.float16).contiguous()
+    h = hessian_diag.to(device=w.device, dtype=torch.float32).contiguous()
+    M, K = w.shape
+    ng = (K + GROUP_SIZE_1ST - 1) // GROUP_SIZE_1ST
+    with torch.cuda.device(w.device):
+        ws = QuantizeWorkspace(M, K, w.device)
+        sums = torch.empty((ng,), dtype=torch.float32, device=w.device)
+        gp = torch.empty((ng,), dtype=torch.uint8, device=w.device)
+        _check(_lib.mb_quantize_exact_sums(_ptr(w), M, K, float(ratio_4bit), _ptr(h), h.numel(),
+                                           _ptr(sums), _ptr(gp), _ptr(ws.buf), ws.nbytes,
+                                           _stream(w.device)))
+    return sums, gp
+
+
 class QuantizeBatch:
     """Quantizes a fixed list of matrices -- a model's weights -- with every
     launch recorded once into a CUDA graph and replayed.
@@ -564,11 +600,13 @@ class QuantizeBatch:
     The batch owns device buffers for the weights (``weights[i]``; refill them
     in place between replays), hessian diagonals, every output, a workspace
     per matrix and CSR arrays with room for ``csr_capacity`` outliers each.
-    Each matrix is one ``mb_quantize_csr`` call (stats, tables, encode and the
-    CSR extraction chained on the device, no host round trip); the matrices
-    are spread over ``branches`` parallel graph branches (largest first, each
-    to the least loaded branch), so one matrix's latency-bound selection
-    overlaps another's streaming.  ``launch`` replays the graph on the current
+    Consecutive matrices form groups of up to ``per_launch`` (8 at most); each
+    group is one ``mb_quantize_csr_many`` call: one launch of each kernel
+    (stats, combine, tables, encode, CSR extraction, chained on the device, no
+    host round trip) serves all its matrices, so launch and pipeline start-up
+    costs are paid once per group.  The groups are spread over ``branches``
+    parallel graph branches (largest first, each to the least loaded branch),
+    so one group's latency-bound selection overlaps another's streaming.  ``launch`` replays the graph on the current
     stream (a few microseconds of host time for the whole list); ``finish``
     waits for it and returns the reference's 11-tensor list per matrix, views
     into the batch's buffers valid until the next ``launch``.  A matrix with
@@ -577,7 +615,7 @@ class QuantizeBatch:
     """
 
     def __init__(self, weights: list, ratios, hessians: list | None = None, device=None,
-                 branches: int = 4, csr_capacity: int | None = None):
+                 branches: int = 2, csr_capacity: int | None = None, per_launch: int = 8):
         device = torch.device("cuda", torch.cuda.current_device()) if device is None \
             else torch.device(device)
         self.device = device
@@ -610,36 +648,69 @@ class QuantizeBatch:
                 self.cols.append(e((max(cap, 1),), torch.int32))
             self.nnz_dev = torch.zeros((n,), dtype=torch.int32, device=device)
             self.nnz_host = torch.zeros((n,), dtype=torch.int32).pin_memory()
-        # branches: largest matrices first, each to the least loaded branch
-        nb = max(1, min(int(branches), n))
+        # groups of consecutive matrices; branches: largest groups first, each
+        # to the least loaded branch
+        per = max(1, min(8, int(per_launch)))
+        self.groups = [list(range(i, min(n, i + per))) for i in range(0, n, per)]
+        size = [sum(self.shapes[i][0] * self.shapes[i][1] for i in g) for g in self.groups]
+        nb = max(1, min(int(branches), len(self.groups)))
         load = [0] * nb
-        self.branch_of = [0] * n
-        for i in sorted(range(n), key=lambda i: -self.shapes[i][0] * self.shapes[i][1]):
+        self.branch_of = [0] * len(self.groups)
+        for gi in sorted(range(len(self.groups)), key=lambda gi: -size[gi]):
             b = min(range(nb), key=lambda b: load[b])
-            self.branch_of[i] = b
-            load[b] += self.shapes[i][0] * self.shapes[i][1]
+            self.branch_of[gi] = b
+            load[b] += size[gi]
         self.nbranch = nb
+        self.jobs = [self._job(i) for i in range(n)]
         self.graph = None
         self.done = torch.cuda.Event()
 
-    def _enqueue(self, i: int, stream) -> None:
+    def kernel_launches(self) -> int:
+        """Kernels one replay launches: five (stats, combine, tables, encode,
+        CSR extraction) per launch set, formed as mb_quantize_csr_many forms
+        them (consecutive matrices with 16 | column groups and the same
+        sensitivity pass, 8 at most; any other matrix alone)."""
+        def ng(i):
+            return (self.shapes[i][1] + GROUP_SIZE_1ST - 1) // GROUP_SIZE_1ST
+
+        def sens(i):
+            return self.hess[i] is not None and int(self.ratios[i] * ng(i)) > 0
+
+        sets = 0
+        for idx in self.groups:
+            i = 0
+            while i < len(idx):
+                e = i + 1
+                if ng(idx[i]) % 16 == 0:
+                    while (e < len(idx) and e - i < 8 and ng(idx[e]) % 16 == 0
+                           and sens(idx[e]) == sens(idx[i])):
+                        e += 1
+                sets += 1
+                i = e
+        return 5 * sets
+
+    def _job(self, i: int) -> QuantizeJob:
         M, K = self.shapes[i]
         h = self.hess[i]
         o = self.out[i]
-        _check(_lib.mb_quantize_csr(
+        return QuantizeJob(
             _ptr(self.weights[i]), M, K, self.ratios[i], _ptr(h), 0 if h is None else h.numel(),
             *(_ptr(t) for t in o), _ptr(self.row_ptrs[i]),
             ctypes.c_void_p(self.nnz_dev.data_ptr() + 4 * i), _ptr(self.vals[i]),
-            _ptr(self.cols[i]), self.cap[i], _ptr(self.ws[i].buf), self.ws[i].nbytes,
-            ctypes.c_void_p(stream.cuda_stream)))
+            _ptr(self.cols[i]), self.cap[i], _ptr(self.ws[i].buf), self.ws[i].nbytes)
+
+    def _enqueue(self, gi: int, stream) -> None:
+        idx = self.groups[gi]
+        arr = (QuantizeJob * len(idx))(*(self.jobs[i] for i in idx))
+        _check(_lib.mb_quantize_csr_many(arr, len(idx), ctypes.c_void_p(stream.cuda_stream)))
 
     def _record(self, main) -> None:
         fork = torch.cuda.Event()
         fork.record(main)
         for st in self.streams:
             st.wait_event(fork)
-        for i in range(len(self.shapes)):
-            self._enqueue(i, self.streams[self.branch_of[i]])
+        for gi in range(len(self.groups)):
+            self._enqueue(gi, self.streams[self.branch_of[gi]])
         for st in self.streams:
             main.wait_stream(st)
         self.nnz_host.copy_(self.nnz_dev, non_blocking=True)
@@ -675,6 +746,7 @@ class QuantizeBatch:
                     self.cap[i] = k
                     self.vals[i] = torch.empty((k,), dtype=torch.float16, device=self.device)
                     self.cols[i] = torch.empty((k,), dtype=torch.int32, device=self.device)
+                    self.jobs[i] = self._job(i)
                     self.graph = None  # the graph holds the old arrays
                     _check(_lib.mb_quantize_extract_outliers(
                         _ptr(self.weights[i]), M, K, _ptr(self.row_ptrs[i]), _ptr(self.vals[i]),

@@ -37,6 +37,7 @@
 #include <chrono>
 #include <cmath>
 #include <cstring>
+#include <vector>
 
 #include "mb_common.cuh"
 #include "mb_tma.cuh"
@@ -818,6 +819,7 @@ struct QArgs {
   int stats_grid;      // CTAs of the stats kernel (the segment records' layout)
   int comb_smem;       // dynamic shared memory of the combine kernel (selection scratch)
   int enc_grid;        // CTAs of the encode kernel
+  int all_pending;     // every group takes its exact serial sum (mb_quantize_exact_sums)
   // encode / post outputs
   int32_t* packed2;
   int32_t* packed4;
@@ -830,11 +832,54 @@ struct QArgs {
   int32_t* nnz;
 };
 
+// Several matrices in one launch: the CTAs [cta0[m], cta0[m + 1]) of a
+// kernel serve matrix m exactly as a grid of their own would (CTA index b of
+// G); the matrices share nothing.  One matrix is a batch of one.
+constexpr int kMaxBatch = 8;
+template <int NB>
+struct BatchMap {
+  int n;
+  int cta0[NB + 1];
+};
+struct CtaSlot {
+  int m, b, G;
+};
+template <int NB>
+__device__ __forceinline__ CtaSlot batch_slot(const BatchMap<NB>& bm) {
+  const int x = (int)blockIdx.x;
+  int m = 0;
+#pragma unroll
+  for (int i = 1; i < NB; ++i) m += (i < bm.n && x >= bm.cta0[i]) ? 1 : 0;
+  return CtaSlot{m, x - bm.cta0[m], bm.cta0[m + 1] - bm.cta0[m]};
+}
+
+// combine / exact arguments of a batch
+template <int NB>
+struct ArgsBatch {
+  QArgs a[NB];
+  BatchMap<NB> bm;
+};
+
+// Transfer function g applied after f: (i0, i1, po) becomes the composite.
+// Increments saturate at 2^30 (any sum that large has left its binade).
+__device__ __forceinline__ void tf_then(int& i0, int& i1, int& po, int gi0, int gi1, int gpo) {
+  const int p0 = po & 1, p1 = (po >> 1) & 1;
+  const int n0 = min(i0 + (p0 ? gi1 : gi0), 1 << 30);
+  const int n1 = min(i1 + (p1 ? gi1 : gi0), 1 << 30);
+  po = ((gpo >> p0) & 1) | (((gpo >> p1) & 1) << 1);
+  i0 = n0;
+  i1 = n1;
+}
+
 // Replay runs [a, b) of group g's chunk rc exactly, starting from s.  Runs go
-// 32 at a time (lane = run): each batch is classified again from the exact s
-// (the drift bound restarts at 0, so only runs that really contain a binade
-// crossing stay unproven), proven runs are applied as transfer functions and
-// the others term by term.  The next batch's rows load while one is processed.
+// 32 at a time (lane = run).  From the exact s in binade e every lane takes
+// its run's transfer function in e; an inclusive scan composes them, so
+// lane j holds the sum after runs 0..j as if all stayed in e.  The first run
+// whose prefix leaves the binade (or holds a term >= 2^e) is added term by
+// term from the exact sum before it, and the scan resumes behind it in the
+// new binade: one scan per binade crossing instead of one step per run.
+// Sums below 2^-103 (where the binade's quantum is subnormal) go term by
+// term.  The next batch's rows load while one is processed.
 __device__ __noinline__ void replay_runs(const QArgs& A, const GroupDiv& gd, int g, int rc, int a,
                                          int b, float& s, int lane) {
   const int64_t c0 = (int64_t)g * kGroup1;
@@ -855,8 +900,8 @@ __device__ __noinline__ void replay_runs(const QArgs& A, const GroupDiv& gd, int
     const bool valid = nvalid;
     if (j0 + 32 < b) nvalid = fetch(j0 + 32, nv);
     uint64_t T2[8];
+    float tmax = 0.0f;
     bool finite = true;
-    double sum = 0.0;
     if (valid) {
       uint64_t X2[8];
       run_squares(v, cmask, X2);
@@ -866,46 +911,66 @@ __device__ __noinline__ void replay_runs(const QArgs& A, const GroupDiv& gd, int
         float t0, t1;
         f2_unpack(T2[k], t0, t1);
         finite &= isfinite(t0) && isfinite(t1);
-        sum += (double)t0 + (double)t1;
+        tmax = fmaxf(tmax, fmaxf(t0, t1));
       }
     } else {
 #pragma unroll
       for (int k = 0; k < 8; ++k) T2[k] = 0ull;
     }
-    double incl = sum;  // prefix from the exact s at the start of this batch
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const double y = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += y;
-    }
-    const double p_rs = (double)s + (incl - sum), p_re = (double)s + incl;
-    RunTF tf;
-    classify_run(T2, finite, p_rs, p_re, 16.0 * lane, tf);
-    // fast path: all runs zero, or proven in s's binade without ties
-    const bool simple = tf.kind == kRunZero || (tf.kind == kRunProven && tf.inc0 == tf.inc1 &&
-                                                s > 0.0f && s < 0x1p127f &&
-                                                tf.e == f32_binade(s));
-    if (__all_sync(0xffffffffu, simple)) {
-      const int tot =
-          (int)__reduce_add_sync(0xffffffffu, (unsigned)(tf.kind == kRunProven ? tf.inc0 : 0));
-      if (tot == 0) continue;
-      float s2 = s;
-      if (apply_tf(s2, f32_binade(s), tot, tot)) {
-        s = s2;
+    const int nrun = min(32, b - j0);
+    int cur = 0;  // runs [0, cur) of the batch are in s
+    while (cur < nrun) {
+      if (!(s >= 0x1p-103f && s < 0x1p127f)) {
+        // zero, tiny or huge sum: run cur term by term
+        float t = s;
+        if (lane == cur) t = serial_add(s, T2);
+        s = __shfl_sync(0xffffffffu, t, cur);
+        ++cur;
         continue;
       }
-    }
-    for (int u = 0; u < 32; ++u) {
-      const int kind = __shfl_sync(0xffffffffu, tf.kind, u);
-      if (kind == kRunZero) continue;
-      const int e = __shfl_sync(0xffffffffu, tf.e, u);
-      const int i0 = __shfl_sync(0xffffffffu, tf.inc0, u);
-      const int i1 = __shfl_sync(0xffffffffu, tf.inc1, u);
-      if (kind == kRunProven && apply_tf(s, e, i0, i1)) continue;
-      uint64_t U2[8];
+      const int e = f32_binade(s);
+      int i0 = 0, i1 = 0, po = 2;  // identity
+      bool bad = false;
+      if (lane >= cur && lane < nrun) {
+        if (finite && tmax < pow2f(e)) {
+          RunTF tf;
+          run_tf(T2, e, tf);
+          i0 = tf.inc0;
+          i1 = tf.inc1;
+          po = tf.pout;
+        } else {
+          bad = true;
+        }
+      }
 #pragma unroll
-      for (int k = 0; k < 8; ++k) U2[k] = __shfl_sync(0xffffffffu, T2[k], u);
-      s = serial_add(s, U2);
+      for (int o = 1; o < 32; o <<= 1) {
+        int u0 = __shfl_up_sync(0xffffffffu, i0, o);
+        int u1 = __shfl_up_sync(0xffffffffu, i1, o);
+        int up = __shfl_up_sync(0xffffffffu, po, o);
+        if (lane >= o) {
+          tf_then(u0, u1, up, i0, i1, po);  // the earlier lanes' runs first
+          i0 = u0;
+          i1 = u1;
+          po = up;
+        }
+      }
+      const int m = (int)__fmul_rn(s, pow2f(23 - e));  // s / q, in [2^23, 2^24)
+      const int m2 = min(m + ((m & 1) ? i1 : i0), 1 << 30);
+      const unsigned cross =
+          __ballot_sync(0xffffffffu, lane >= cur && lane < nrun && (bad || m2 >= (1 << 24)));
+      const int u = cross ? __ffs(cross) - 1 : nrun;  // first run that leaves binade e
+      if (u > cur) {
+        // runs [cur, u) stay in e: the sum after them, exactly
+        s = __shfl_sync(0xffffffffu, __fmul_rn((float)m2, pow2f(e - 23)), u - 1);
+      }
+      if (u < nrun) {
+        float t = s;
+        if (lane == u) t = serial_add(s, T2);
+        s = __shfl_sync(0xffffffffu, t, u);
+        cur = u + 1;
+      } else {
+        cur = nrun;
+      }
     }
   }
 }
@@ -919,10 +984,16 @@ __device__ void replay_span(const QArgs& A, const GroupDiv& gd, int g, int c0, i
   }
 }
 
+__device__ __forceinline__ unsigned lanes_upto(int x) { return (2u << x) - 1u; }  // 0..x
+
 // The exact sensitivity of group g from its chunk programs.  Consecutive
 // stretches in one binade compose without the sum (composition is
 // associative); the composite is applied to the exact sum when the binade
 // changes or a window comes, and replayed if the check in apply_tf fails.
+// Chunks come 32 at a time (lane = chunk); runs of chunks whose program is a
+// single stretch in one binade are composed at once by a segmented scan over
+// the lanes, so the serial walk visits only those runs, the other chunks'
+// items and the replays.
 __device__ __noinline__ float assemble_group(const QArgs& A, const GroupDiv& gd, int g,
                                              int lane) {
   float S = 0.0f;
@@ -932,54 +1003,95 @@ __device__ __noinline__ float assemble_group(const QArgs& A, const GroupDiv& gd,
     p_open = 0;
     if (!apply_tf(S, p_e, p_i0, p_i1)) replay_span(A, gd, g, p_c, p_r, c_end, r_end, S, lane);
   };
+  // one item: a window [ra, rb) of chunk (replayed), or a stretch in binade e
+  // with transfer function (i0, i1, po) from run ra of chunk
+  auto item = [&](int chunk, int e, int i0, int i1, int po, int ra, int rb) {
+    if (e == kItemWindow) {
+      flush(chunk, ra);
+      replay_runs(A, gd, g, chunk, ra, rb, S, lane);
+    } else if (p_open && p_e == e) {
+      tf_then(p_i0, p_i1, p_po, i0, i1, po);
+    } else {
+      flush(chunk, ra);
+      p_open = 1;
+      p_e = e;
+      p_i0 = i0;
+      p_i1 = i1;
+      p_po = po;
+      p_c = chunk;
+      p_r = ra;
+    }
+  };
   const int nrc = A.nrc;
   for (int cb = 0; cb < nrc && isfinite(S); cb += 32) {
     const size_t rec = (size_t)g * nrc + cb + lane;
     const bool have = cb + lane < nrc;
-    const uint32_t cw = have ? __ldcg(A.ws.icount + rec) : 0u;
+    // every slot at once (slots past the count are not used)
+    uint32_t cw = 0u;
     int4 it[kMaxItems];
 #pragma unroll
     for (int k = 0; k < kMaxItems; ++k)
-      it[k] = (have && k < (int)(cw & 0xFFFFu)) ? __ldcg(A.ws.items + rec * kMaxItems + k)
-                                                 : make_int4(0, 0, 0, 0);
+      it[k] = have ? __ldcg(A.ws.items + rec * kMaxItems + k) : make_int4(0, 0, 0, 0);
+    if (have) cw = __ldcg(A.ws.icount + rec);
+    const bool simple =
+        have && !(cw & kCntOverflow) && (cw & 0xFFFFu) == 1u && it[0].x != kItemWindow;
+    const unsigned smask = __ballot_sync(0xffffffffu, simple);
+    const int e_prev = __shfl_up_sync(0xffffffffu, it[0].x, 1);
+    const bool start =
+        simple && (lane == 0 || !((smask >> (lane - 1)) & 1u) || e_prev != it[0].x);
+    const unsigned stmask = __ballot_sync(0xffffffffu, start);
+    // segmented inclusive scan: lane holds the composite from its run's
+    // first chunk through itself
+    int s0 = it[0].y, s1 = it[0].z, sp = it[0].w & 3;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int u0 = __shfl_up_sync(0xffffffffu, s0, o);
+      int u1 = __shfl_up_sync(0xffffffffu, s1, o);
+      int up = __shfl_up_sync(0xffffffffu, sp, o);
+      const bool join =
+          simple && lane >= o && (stmask & lanes_upto(lane) & ~lanes_upto(lane - o)) == 0u;
+      if (join) {
+        tf_then(u0, u1, up, s0, s1, sp);
+        s0 = u0;
+        s1 = u1;
+        sp = up;
+      }
+    }
     const int nc = min(32, nrc - cb);
-    for (int c = 0; c < nc && isfinite(S); ++c) {
+    int c = 0;
+    while (c < nc && isfinite(S)) {
       const int chunk = cb + c;
+      if ((smask >> c) & 1u) {
+        const unsigned brk = (stmask | ~smask) & ~lanes_upto(c);
+        const int end = min(nc, brk ? __ffs(brk) - 1 : 32);
+        const int e = __shfl_sync(0xffffffffu, it[0].x, c);
+        const int ra = (__shfl_sync(0xffffffffu, it[0].w, c) >> 2) & 0x7FFF;
+        const int i0 = __shfl_sync(0xffffffffu, s0, end - 1);
+        const int i1 = __shfl_sync(0xffffffffu, s1, end - 1);
+        const int po = __shfl_sync(0xffffffffu, sp, end - 1);
+        item(chunk, e, i0, i1, po, ra, 0);
+        c = end;
+        continue;
+      }
       const uint32_t w = __shfl_sync(0xffffffffu, cw, c);
       if (w & kCntOverflow) {
         flush(chunk, 0);
         replay_runs(A, gd, g, chunk, 0, kChunkRows, S, lane);
-        continue;
-      }
-      const int n = (int)(w & 0xFFFFu);
+      } else {
+        const int n = (int)(w & 0xFFFFu);
+        for (int k = 0; k < n; ++k) {
+          int4 v = it[0];
 #pragma unroll
-      for (int k = 0; k < kMaxItems; ++k) {
-        if (k < n) {
-          const int ix = __shfl_sync(0xffffffffu, it[k].x, c);
-          const int iy = __shfl_sync(0xffffffffu, it[k].y, c);
-          const int iz = __shfl_sync(0xffffffffu, it[k].z, c);
-          const int iw = __shfl_sync(0xffffffffu, it[k].w, c);
-          const int ra = (iw >> 2) & 0x7FFF, rb = (iw >> 17) & 0x7FFF;
-          if (ix == kItemWindow) {
-            flush(chunk, ra);
-            replay_runs(A, gd, g, chunk, ra, rb, S, lane);
-          } else if (p_open && p_e == ix) {
-            const int q0 = p_po & 1, q1 = (p_po >> 1) & 1;
-            p_i0 += q0 ? iz : iy;
-            p_i1 += q1 ? iz : iy;
-            p_po = ((iw >> q0) & 1) | (((iw >> q1) & 1) << 1);
-          } else {
-            flush(chunk, ra);
-            p_open = 1;
-            p_e = ix;
-            p_i0 = iy;
-            p_i1 = iz;
-            p_po = iw & 3;
-            p_c = chunk;
-            p_r = ra;
-          }
+          for (int q = 1; q < kMaxItems; ++q)
+            if (q == k) v = it[q];
+          const int ix = __shfl_sync(0xffffffffu, v.x, c);
+          const int iy = __shfl_sync(0xffffffffu, v.y, c);
+          const int iz = __shfl_sync(0xffffffffu, v.z, c);
+          const int iw = __shfl_sync(0xffffffffu, v.w, c);
+          item(chunk, ix, iy, iz, iw & 3, (iw >> 2) & 0x7FFF, (iw >> 17) & 0x7FFF);
         }
       }
+      ++c;
     }
   }
   flush(nrc, 0);
@@ -994,6 +1106,15 @@ __device__ __noinline__ void exact_chunk(const QArgs& A, const GroupDiv& gd, int
   const bool vec = A.w_aligned && gs == kGroup1 && (A.K & 7) == 0;
   const uint32_t cmask = gs >= 16 ? 0xFFFFu : ((1u << gs) - 1u);
   const size_t rec = (size_t)g * A.nrc + rc;
+  const int64_t row0 = (int64_t)rc * kChunkRows;
+  // the chunk's rows (lane = run of each 32-run step), loaded up front so
+  // the four loads overlap one another and the prefix computation
+  Row16 rv[kSteps];
+#pragma unroll
+  for (int s = 0; s < kSteps; ++s) {
+    rv[s].lo = rv[s].hi = make_uint4(0, 0, 0, 0);
+    if (row0 + s * 32 + lane < A.M) rv[s] = load_row16(A.W, row0 + s * 32 + lane, A.K, c0, gs, vec);
+  }
   // predicted prefix before the chunk, from the column sums of the chunks
   float rc16[16];
 #pragma unroll
@@ -1008,7 +1129,6 @@ __device__ __noinline__ void exact_chunk(const QArgs& A, const GroupDiv& gd, int
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) pstart += __shfl_xor_sync(0xffffffffu, pstart, o);
-  const int64_t row0 = (int64_t)rc * kChunkRows;
   int4* items = A.ws.items + rec * kMaxItems;
   ProgBuilder pb;
   pb.open = 0;
@@ -1017,14 +1137,12 @@ __device__ __noinline__ void exact_chunk(const QArgs& A, const GroupDiv& gd, int
   pb.e = pb.inc0 = pb.inc1 = pb.a = pb.b = 0;
   pb.pout = 2;
   double ctot = 0.0;
+#pragma unroll
   for (int s = 0; s < kSteps; ++s) {
     const int r = s * 32 + lane;
     const bool rvalid = row0 + r < A.M;
-    Row16 v;
-    v.lo = v.hi = make_uint4(0, 0, 0, 0);
-    if (rvalid) v = load_row16(A.W, row0 + r, A.K, c0, gs, vec);
     uint64_t X2[8], T2[8];
-    run_squares(v, rvalid ? cmask : 0u, X2);
+    run_squares(rv[s], rvalid ? cmask : 0u, X2);
     float p = run_pred(X2, gd.R2);
     if (!isfinite(p)) p = 0.0f;
     run_terms(X2, gd.R2, gd.NH2, gd.mode, T2);
@@ -1511,7 +1629,7 @@ __device__ void select_from_intervals(const QArgs& a, uint8_t* scratch, size_t s
     auto classify = [&](int g, uint32_t l, uint32_t h, uint8_t greg, bool on) {
       uint8_t p = 0;
       if (on) {
-        p = (all_in || l > Bhi) ? 1 : (h < Alo ? 0 : 2);
+        p = a.all_pending ? 2 : ((all_in || l > Bhi) ? 1 : (h < Alo ? 0 : 2));
         c_in += p == 1;
         c_pend += p == 2;
         a.ws.prec[g] = p;
@@ -1538,7 +1656,7 @@ __device__ void select_from_intervals(const QArgs& a, uint8_t* scratch, size_t s
     sync_nt<NT>();
     const int need = n4 - (int)s_cnt[0], np = (int)s_cnt[1];
     if (tid == 0) a.ws.hdr->n_straddle = (uint32_t)np;
-    if (np > 0 && (need <= 0 || need >= np)) {
+    if (np > 0 && !a.all_pending && (need <= 0 || need >= np)) {
       // all pending groups take the same precision
       const uint8_t to = need > 0 ? 1 : 0;
       for (int g0 = 0; g0 < ng; g0 += NT) {
@@ -1741,9 +1859,8 @@ __device__ __noinline__ void ct_combine(const QArgs& A, int ct, int warp, int la
 // and the CTA completing the last column tile selects the 4-bit groups
 // (torch_ops.cu:149-179) and splits the encode tiles.
 template <bool kSens>
-__global__ void __launch_bounds__(kStatsThreads, 2)
-    stats_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ QArgs A,
-                 int use_tma) {
+__device__ __forceinline__ void stats_body(const CUtensorMap& tmap, const QArgs& A, int use_tma,
+                                           int bid, int G) {
   extern __shared__ uint8_t dsm_raw[];
   // 1024-byte aligned for the 128-byte swizzle; offset arithmetic on the
   // shared array keeps the pointer in the shared space (plain LDS)
@@ -1754,9 +1871,8 @@ __global__ void __launch_bounds__(kStatsThreads, 2)
   const int64_t M = A.M, K = A.K;
   const int nrc = A.nrc, nct = A.nct;
   const int ntiles = nct * nrc;  // below 2^31 (checked on the host)
-  const int G = (int)gridDim.x;
-  const int u_begin = stats_start((int)blockIdx.x, ntiles, G);
-  const int u_end = stats_start((int)blockIdx.x + 1, ntiles, G);
+  const int u_begin = stats_start(bid, ntiles, G);
+  const int u_end = stats_start(bid + 1, ntiles, G);
   int u_ahead = u_begin;  // thread 0: the next tile to load
   int ct_ahead = u_begin / nrc, rc_ahead = u_begin - ct_ahead * nrc;
   auto issue = [&](int s) {
@@ -1922,7 +2038,7 @@ __global__ void __launch_bounds__(kStatsThreads, 2)
                   (__any_sync(0xffffffffu, sloose) ? kGrpLoose : 0u);
         }
         if (lane == 0) {
-          SegRec* dst = A.ws.seg + ((size_t)(blockIdx.x + ct) * kTileGroups + gi);
+          SegRec* dst = A.ws.seg + ((size_t)(bid + ct) * kTileGroups + gi);
           reinterpret_cast<double2*>(dst)[0] = make_double2(sum, mom);
           reinterpret_cast<uint4*>(dst)[1] =
               make_uint4(__float_as_uint(mn), __float_as_uint(mx), srows, flags);
@@ -1955,28 +2071,45 @@ __global__ void __launch_bounds__(kStatsThreads, 2)
   }
 }
 
+template <int NB>
+struct __align__(64) StatsBatch {
+  CUtensorMap tmap[NB];
+  QArgs a[NB];
+  int use_tma[NB];
+  BatchMap<NB> bm;
+};
+
+template <bool kSens, int NB>
+__global__ void __launch_bounds__(kStatsThreads, 2)
+    stats_kernel(const __grid_constant__ StatsBatch<NB> P) {
+  const CtaSlot c = batch_slot(P.bm);
+  stats_body<kSens>(P.tmap[c.m], P.a[c.m], P.use_tma[c.m], c.b, c.G);
+}
+
 // combine: a warp per group (grid-stride) adds the group's segment records
 // in row order (ct_combine): min / max, sensitivity interval, the parameters
 // of both precisions and their code thresholds.  The CTA finishing last
 // selects the 4-bit groups (torch_ops.cu:149-179) and splits the encode
 // tiles.  Launched after stats with programmatic dependent launch.
 constexpr int kCombThreads = 256;
-template <bool kSens>
+template <bool kSens, int NB>
 __global__ void __launch_bounds__(kCombThreads, 1)
-    combine_kernel(const __grid_constant__ QArgs A) {
+    combine_kernel(const __grid_constant__ ArgsBatch<NB> P) {
   extern __shared__ uint8_t csm[];
   __shared__ int s_last;
+  const CtaSlot c = batch_slot(P.bm);
+  const QArgs& A = P.a[c.m];
   const int tid = threadIdx.x, lane = tid & 31;
   grid_dependency_wait();  // every segment record written
-  const int64_t nw = (int64_t)gridDim.x * (kCombThreads / 32);
-  for (int64_t g = ((int64_t)blockIdx.x * kCombThreads + tid) >> 5; g < A.ng; g += nw) {
+  const int64_t nw = (int64_t)c.G * (kCombThreads / 32);
+  for (int64_t g = ((int64_t)c.b * kCombThreads + tid) >> 5; g < A.ng; g += nw) {
     ct_combine<kSens>(A, (int)(g / kTileGroups), (int)(g % kTileGroups), lane);
     __syncwarp();  // the parameters lanes 0 and 1 wrote
     group_thresholds_warp(A.ws.params, g, lane);
   }
   __threadfence();
   __syncthreads();
-  if (tid == 0) s_last = atomicAdd(&A.ws.hdr->ticket_ct, 1u) == gridDim.x - 1u;
+  if (tid == 0) s_last = atomicAdd(&A.ws.hdr->ticket_ct, 1u) == (unsigned)c.G - 1u;
   __syncthreads();
   grid_launch_dependents();
   if (!s_last || A.no_select) return;
@@ -2087,20 +2220,17 @@ __device__ __noinline__ uint3 enc_irregular(const GroupParams& gp, const uint8_t
 // Exact sums of the pending groups (the first kExactCtas blocks of the encode
 // grid): warps take (pending group, chunk) work items; the last chunk of a
 // group assembles its exact sum, the last group completes the selection.
-__device__ __noinline__ void exact_ctas(const QArgs& a) {
+__device__ __noinline__ void exact_ctas(const QArgs& a, int bid, int G) {
   const Header* hdr = a.ws.hdr;
   const uint32_t np = *reinterpret_cast<const volatile uint32_t*>(&hdr->n_pend);
   if (np == 0) return;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t ndec = *reinterpret_cast<const volatile uint32_t*>(&hdr->n_dec);
   __shared__ GroupDiv s_div[8];
-  __shared__ __align__(16) float s_scr[1024];  // the completing warp's tables
   __shared__ uint32_t hist[256];
   __shared__ uint32_t s2[2];
-  __shared__ uint32_t s_wsum[1];
-  __shared__ int s_irr;
   const int64_t nwork = (int64_t)np * a.nrc;
-  for (int64_t w = (int64_t)blockIdx.x * 8 + warp; w < nwork; w += (int64_t)kExactCtas * 8) {
+  for (int64_t w = (int64_t)bid * 8 + warp; w < nwork; w += (int64_t)G * 8) {
     const int u = (int)(w / a.nrc), c = (int)(w % a.nrc);
     const int g = a.ws.order[ndec + u];
     load_group_div(a.hess, (int64_t)g * kGroup1, a.K, lane, &s_div[warp]);
@@ -2145,9 +2275,7 @@ __device__ __noinline__ void exact_ctas(const QArgs& a) {
       total_eq += __popc(b);
     }
     if (lane == 0 && total_eq > need_eq) atomicOr(&a.ws.hdr->status, kStatusTie);
-    __syncwarp();
-    // decided slots of `order` are being encoded meanwhile: keep it as is
-    finalize_tables<32>(a, s_scr, sizeof(s_scr), s_wsum, &s_irr, false);
+    // the tables follow in tables_kernel, over the whole grid
   }
 }
 
@@ -2156,11 +2284,11 @@ __device__ __noinline__ void exact_ctas(const QArgs& a) {
 // grid: threads over groups, one warp per chunk.  Chunk c's scales are those
 // of the groups s0 mod ng, s0 mod ng + 1, ... (cyclic, s0 = 256 c; the
 // partial chunk is the last).
-__device__ __noinline__ void tables_grid(const QArgs& a) {
+__device__ __noinline__ void tables_grid(const QArgs& a, int bid, int G) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int ng = a.ng;
   bool irr = false;
-  for (int g = blockIdx.x * blockDim.x + tid; g < ng; g += gridDim.x * blockDim.x) {
+  for (int g = bid * blockDim.x + tid; g < ng; g += G * blockDim.x) {
     const uint8_t pr = a.ws.prec[g];
     a.gp[g] = pr;
     irr |= !((a.ws.greg[g] >> pr) & 1);
@@ -2174,8 +2302,8 @@ __device__ __noinline__ void tables_grid(const QArgs& a) {
   const ChunkLayout& cl = a.cl;
   const int nchunks = cl.ntab_full + cl.has_partial;
   const int64_t step = kGroup2 % ng;  // s0 mod ng advances by this per chunk
-  const int nwarps = gridDim.x * (blockDim.x >> 5);
-  for (int ci = blockIdx.x * (blockDim.x >> 5) + warp; ci < nchunks; ci += nwarps) {
+  const int nwarps = G * (blockDim.x >> 5);
+  for (int ci = bid * (blockDim.x >> 5) + warp; ci < nchunks; ci += nwarps) {
     const bool partial = ci >= cl.ntab_full;
     const int64_t cidx = partial ? cl.nfull : ci;
     const int n = (int)min64(kGroup2, cl.total - cidx * kGroup2);
@@ -2210,26 +2338,42 @@ __device__ __noinline__ void tables_grid(const QArgs& a) {
   }
 }
 
-// Between the selection and encode: the tables when every precision is
-// known, else the exact sums of the pending groups (whose last warp completes
-// the selection and the tables).
+// Between the selection and the tables: the exact sums of the pending groups
+// (whose last warp completes the selection); nothing when no group is
+// pending.
 // Encode is launched only when this kernel is done: its CTAs are large
 // (two fill an SM) and, resident early, would hold the SMs that other work
 // on other streams can use meanwhile.
-__global__ void __launch_bounds__(256) exact_kernel(const __grid_constant__ QArgs a) {
+template <int NB>
+__global__ void __launch_bounds__(256) exact_kernel(const __grid_constant__ ArgsBatch<NB> P) {
+  const CtaSlot c = batch_slot(P.bm);
+  const QArgs& a = P.a[c.m];
   grid_dependency_wait();  // stats and the selection complete
   // every group's code thresholds for both precisions (a warp per group),
   // when the combine kernel did not find them (row-split slabs)
   if (a.exact_thresholds) {
     const int lane = threadIdx.x & 31;
-    const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
-    for (int64_t g = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; g < a.ng; g += nw)
+    const int64_t nw = (int64_t)c.G * (blockDim.x >> 5);
+    for (int64_t g = ((int64_t)c.b * blockDim.x + threadIdx.x) >> 5; g < a.ng; g += nw)
       group_thresholds_warp(a.ws.params, g, lane);
   }
-  if (*reinterpret_cast<const volatile uint32_t*>(&a.ws.hdr->n_pend) == 0)
-    tables_grid(a);
-  else
-    exact_ctas(a);
+  if (*reinterpret_cast<const volatile uint32_t*>(&a.ws.hdr->n_pend) != 0)
+    exact_ctas(a, c.b, c.G);
+  grid_launch_dependents();
+}
+
+// Once every precision is known: group_precision, any_irregular and the
+// 2nd-order chunk table over the whole grid; after exact sums (the
+// selection's tile split predates them) CTA 0 splits the legacy encode's
+// tiles evenly.
+template <int NB>
+__global__ void __launch_bounds__(256) tables_kernel(const __grid_constant__ ArgsBatch<NB> P) {
+  const CtaSlot c = batch_slot(P.bm);
+  const QArgs& a = P.a[c.m];
+  grid_dependency_wait();  // the selection (and exact sums) complete
+  tables_grid(a, c.b, c.G);
+  if (c.b == 0 && *reinterpret_cast<const volatile uint32_t*>(&a.ws.hdr->n_pend) != 0)
+    enc_partition<256>(a, nullptr, nullptr);
   grid_launch_dependents();
 }
 
@@ -2240,10 +2384,10 @@ __global__ void __launch_bounds__(256) exact_kernel(const __grid_constant__ QArg
 // ---------------------------------------------------------------------------
 // 2nd-order scales / zeros, and the row pointers when no group can hold
 // outliers (all CTAs of encode, grid-stride, once the tables are final).
-__device__ __forceinline__ void post_prologue(const QArgs& a) {
+__device__ __forceinline__ void post_prologue(const QArgs& a, int bid, int G) {
   const int64_t M = a.M;
-  const int64_t gtid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t gthreads = (int64_t)gridDim.x * blockDim.x;
+  const int64_t gtid = (int64_t)bid * blockDim.x + threadIdx.x;
+  const int64_t gthreads = (int64_t)G * blockDim.x;
   const ChunkLayout& cl = a.cl;
   for (int64_t c = gtid; c < cl.ng2; c += gthreads) {
     const float4 e = a.ws.chunk_tab[c < cl.nfull ? (int)(c % cl.period) : cl.ntab_full];
@@ -2259,7 +2403,7 @@ __device__ __forceinline__ void post_prologue(const QArgs& a) {
 // When groups may hold outliers: the last encode CTA to finish turns the
 // per-row counts into row pointers (all threads of every CTA call it).
 template <int NT>
-__device__ __forceinline__ void post_rowptr_scan(const QArgs& a) {
+__device__ __forceinline__ void post_rowptr_scan(const QArgs& a, int G) {
   if (a.ws.hdr->any_irregular == 0) return;
   __shared__ int s_last;
   __shared__ long long part[NT];
@@ -2267,7 +2411,7 @@ __device__ __forceinline__ void post_rowptr_scan(const QArgs& a) {
   const int64_t M = a.M;
   __threadfence();
   __syncthreads();
-  if (tid == 0) s_last = atomicAdd(&a.ws.hdr->ticket_post, 1u) == gridDim.x - 1;
+  if (tid == 0) s_last = atomicAdd(&a.ws.hdr->ticket_post, 1u) == (unsigned)G - 1u;
   __syncthreads();
   if (!s_last) return;
   __threadfence();
@@ -2454,7 +2598,7 @@ __global__ void __launch_bounds__(kEncThreads, 2)
   }
   if (tid < 2) item_next[tid] = 0;  // visible after the context's barriers
   grid_dependency_wait();  // the selection, parameters, 2nd-order table and ranges are final
-  post_prologue(a);
+  post_prologue(a, (int)blockIdx.x, (int)gridDim.x);
   // the tile range, clamped into the matrix whatever the split wrote
   const int64_t ntiles_all = (int64_t)a.nct * nrc;
   const int64_t S0 = max64(0, min64(ntiles_all, a.ws.enc_start[blockIdx.x]));
@@ -2657,7 +2801,7 @@ __global__ void __launch_bounds__(kEncThreads, 2)
     for (int s = 0; s < kEncStages; ++s)
       if (bad & (1u << s)) (void)mbar_wait(&full[s], 0u), (void)mbar_wait(&full[s], 1u);
   }
-  post_rowptr_scan<kEncThreads>(a);
+  post_rowptr_scan<kEncThreads>(a, (int)gridDim.x);
 }
 
 
@@ -2744,9 +2888,8 @@ __device__ __forceinline__ void enc3_quarter(const uint8_t* __restrict__ rb, int
   }
 }
 
-__global__ void __launch_bounds__(kE3Threads, 1)
-    encode3_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ Enc3Maps om,
-                   const __grid_constant__ QArgs a, int use_tma) {
+__device__ __forceinline__ void encode3_body(const CUtensorMap& tmap, const Enc3Maps& om,
+                                             const QArgs& a, int use_tma, int bid, int G) {
   extern __shared__ uint8_t dsm_raw[];
   uint8_t* dsm = dsm_raw + ((1024u - (smem_u32(dsm_raw) & 1023u)) & 1023u);
   __shared__ uint64_t full[kE3Stages], empty[kE3Stages];
@@ -2768,10 +2911,9 @@ __global__ void __launch_bounds__(kE3Threads, 1)
     fence_mbar_init();
   }
   grid_dependency_wait();  // the selection, parameters and 2nd-order table are final
-  post_prologue(a);
+  post_prologue(a, bid, G);
   const int64_t ntiles = (int64_t)nct3 * nrc;
-  const int G = (int)gridDim.x;
-  const int64_t S0 = ntiles * blockIdx.x / G, S1 = ntiles * (blockIdx.x + 1) / G;
+  const int64_t S0 = ntiles * bid / G, S1 = ntiles * (bid + 1) / G;
   const int64_t ntile_cta = S1 - S0;
   int a_ct = (int)(S0 / nrc), a_rc = (int)(S0 % nrc);  // thread 0: the next tile to load
   auto issue = [&](int s) {
@@ -3010,7 +3152,23 @@ __global__ void __launch_bounds__(kE3Threads, 1)
     for (int s = 0; s < kE3Stages; ++s)
       if (bad & (1u << s)) (void)mbar_wait(&full[s], 0u), (void)mbar_wait(&full[s], 1u);
   }
-  post_rowptr_scan<kE3Threads>(a);
+  post_rowptr_scan<kE3Threads>(a, G);
+}
+
+template <int NB>
+struct __align__(64) Enc3Batch {
+  CUtensorMap tmap[NB];
+  Enc3Maps om[NB];
+  QArgs a[NB];
+  int use_tma[NB];
+  BatchMap<NB> bm;
+};
+
+template <int NB>
+__global__ void __launch_bounds__(kE3Threads, 1)
+    encode3_kernel(const __grid_constant__ Enc3Batch<NB> P) {
+  const CtaSlot c = batch_slot(P.bm);
+  encode3_body(P.tmap[c.m], P.om[c.m], P.a[c.m], P.use_tma[c.m], c.b, c.G);
 }
 
 
@@ -3063,22 +3221,30 @@ __global__ void __launch_bounds__(256)
 // the kernels (mb_quantize_csr).  Nothing to do without outliers; more
 // outliers than `capacity` set kStatusCsrOverflow and write nothing.  Warps
 // stride over the rows.
-__global__ void __launch_bounds__(256)
-    extract_cap_kernel(const __half* __restrict__ W, int64_t M, int64_t K, int ng,
-                       const GroupParams* __restrict__ params, const uint8_t* __restrict__ prec,
-                       const int32_t* __restrict__ row_ptrs, const int32_t* nnz,
-                       int64_t capacity, __half* __restrict__ vals, int32_t* __restrict__ cols,
-                       uint32_t* status, int fma_mode) {
+template <int NB>
+struct CsrBatch {
+  QArgs a[NB];
+  int64_t capacity[NB];
+  __half* vals[NB];
+  int32_t* cols[NB];
+  BatchMap<NB> bm;
+};
+
+template <int NB>
+__global__ void __launch_bounds__(256) extract_cap_kernel(const __grid_constant__ CsrBatch<NB> P) {
+  const CtaSlot c = batch_slot(P.bm);
+  const QArgs& a = P.a[c.m];
   grid_dependency_wait();  // encode and its row-pointer scan complete
-  const int32_t n = *reinterpret_cast<const volatile int32_t*>(nnz);
+  const int32_t n = *reinterpret_cast<const volatile int32_t*>(a.nnz);
   if (n <= 0) return;
-  if ((int64_t)n > capacity) {
-    if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(status, kStatusCsrOverflow);
+  if ((int64_t)n > P.capacity[c.m]) {
+    if (c.b == 0 && threadIdx.x == 0) atomicOr(&a.ws.hdr->status, kStatusCsrOverflow);
     return;
   }
-  const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < M; r += nw)
-    extract_row(W, r, K, ng, params, prec, row_ptrs, vals, cols, fma_mode, threadIdx.x & 31);
+  const int64_t nw = (int64_t)c.G * (blockDim.x >> 5);
+  for (int64_t r = ((int64_t)c.b * blockDim.x + threadIdx.x) >> 5; r < a.M; r += nw)
+    extract_row(a.W, r, a.K, a.ng, a.ws.params, a.ws.prec, a.row_ptrs, P.vals[c.m],
+                P.cols[c.m], kOutlierFma, threadIdx.x & 31);
 }
 
 mb_status check_common(const void* weights, int64_t M, int64_t K) {
@@ -3115,6 +3281,7 @@ struct QuantizeLaunch {
   bool tma, enc3, sens;
   int vec_out;
   int64_t stats_grid, comb_grid, enc_grid, enc3_grid;
+  int64_t stats_full, enc3_full;  // every SM's resident CTAs (a batch's grids)
   size_t hdr_bytes;
 };
 
@@ -3223,14 +3390,14 @@ mb_status quantize_prepare(const void* weights_fp16, int64_t M, int64_t K, doubl
   if (mb_status st = legacy_enc_grid(ntiles, sms, &L.enc_grid)) return st;
   qa.enc_grid = (int)L.enc_grid;
   {
-    auto kern = L.sens ? stats_kernel<true> : stats_kernel<false>;
+    auto kern = L.sens ? stats_kernel<true, 1> : stats_kernel<false, 1>;
     static std::atomic<int> occ[2][64];
     int per_sm = 1;
     MB_CUDA_TRY(blocks_per_sm_once(kern, kStatsThreads, kStatsSmem, occ[L.sens ? 1 : 0], 64,
                                    &per_sm));
     // at most one CTA per tile (no empty tile range) and the records' cap
-    L.stats_grid = std::max<int64_t>(
-        1, std::min<int64_t>(stats_grid_cap(ntiles), (int64_t)sms * std::max(per_sm, 1)));
+    L.stats_full = (int64_t)sms * std::max(per_sm, 1);
+    L.stats_grid = std::max<int64_t>(1, std::min<int64_t>(stats_grid_cap(ntiles), L.stats_full));
   }
   qa.stats_grid = (int)L.stats_grid;
   qa.exact_thresholds = 0;
@@ -3245,6 +3412,7 @@ mb_status quantize_prepare(const void* weights_fp16, int64_t M, int64_t K, doubl
   }
   L.enc3 = false;
   L.enc3_grid = 1;
+  L.enc3_full = sms;
   L.vec_out = 0;
   std::memset(&L.omaps, 0, sizeof(L.omaps));
   if (stats_only) return MB_OK;
@@ -3263,9 +3431,9 @@ mb_status quantize_prepare(const void* weights_fp16, int64_t M, int64_t K, doubl
   if (L.enc3) {
     static std::atomic<int> occ3[64];
     int per_sm = 1;
-    MB_CUDA_TRY(blocks_per_sm_once(encode3_kernel, kE3Threads, kE3Smem, occ3, 64, &per_sm));
-    L.enc3_grid = std::max<int64_t>(
-        1, std::min<int64_t>((ng / kE3Groups) * nrc, (int64_t)sms * std::max(per_sm, 1)));
+    MB_CUDA_TRY(blocks_per_sm_once(encode3_kernel<1>, kE3Threads, kE3Smem, occ3, 64, &per_sm));
+    L.enc3_full = (int64_t)sms * std::max(per_sm, 1);
+    L.enc3_grid = std::max<int64_t>(1, std::min<int64_t>((ng / kE3Groups) * nrc, L.enc3_full));
   }
   const auto al = [](const void* p, unsigned m) {
     return (reinterpret_cast<uintptr_t>(p) & (m - 1)) == 0;
@@ -3275,29 +3443,174 @@ mb_status quantize_prepare(const void* weights_fp16, int64_t M, int64_t K, doubl
   return MB_OK;
 }
 
-// The header memset and the stats kernel.
-mb_status launch_stats(const QuantizeLaunch& L, cudaStream_t stream) {
-  MB_CUDA_TRY(cudaMemsetAsync(L.qa.ws.hdr, 0, L.hdr_bytes, stream));
-  auto kern = L.sens ? stats_kernel<true> : stats_kernel<false>;
-  kern<<<(unsigned)L.stats_grid, kStatsThreads, kStatsSmem, stream>>>(L.tmap, L.qa,
-                                                                       L.tma ? 1 : 0);
-  MB_LAUNCH_CHECK("stats_kernel");
-  auto comb = L.sens ? combine_kernel<true> : combine_kernel<false>;
-  static std::atomic<uint64_t> attr_done[2];
-  MB_CUDA_TRY(set_smem_limit_once(comb, kCombSmem, attr_done[L.sens ? 1 : 0]));
-  return launch_pdl(comb, dim3((unsigned)L.comb_grid), dim3(kCombThreads),
-                    (size_t)L.qa.comb_smem, stream, L.qa);
+// Grid shares of a batch: matrix i gets about total * w[i] / sum(w) CTAs, at
+// least 1 and at most cap[i].
+void split_grid(int n, const int64_t* w, const int64_t* cap, int64_t total, int64_t* out) {
+  double sw = 0.0;
+  for (int i = 0; i < n; ++i) sw += (double)w[i];
+  for (int i = 0; i < n; ++i) {
+    const int64_t g = (int64_t)std::llround((double)total * (double)w[i] / std::max(sw, 1.0));
+    out[i] = std::max<int64_t>(1, std::min<int64_t>(g, cap[i]));
+  }
 }
 
-// The tables / exact-sum kernel and the encode kernel (chained with PDL).
-mb_status launch_tables_encode(const QuantizeLaunch& L, cudaStream_t stream) {
-  if (mb_status st = launch_pdl(exact_kernel, dim3(kExactCtas), dim3(256), 0, stream, L.qa))
+template <int NB>
+void fill_map(BatchMap<NB>& bm, int n, const int64_t* grid) {
+  bm.n = n;
+  bm.cta0[0] = 0;
+  for (int i = 0; i < n; ++i) bm.cta0[i + 1] = bm.cta0[i] + (int)grid[i];
+}
+
+// The CSR arrays of mb_quantize_csr (one per matrix of a batch).
+struct CsrOut {
+  __half* vals;
+  int32_t* cols;
+  int64_t capacity;
+};
+
+// The header memsets, then one stats and one combine launch for n <= NB
+// matrices (all with or all without the sensitivity pass).  One matrix keeps
+// its own grids; in a batch the stats kernel's full grid is split by tile
+// count and each matrix's combine keeps its grid.
+template <int NB>
+mb_status launch_stats_batch(QuantizeLaunch* const* Ls, int n, cudaStream_t stream) {
+  const bool sens = Ls[0]->sens;
+  int64_t sg[NB], cg[NB];
+  if (n == 1) {
+    sg[0] = Ls[0]->stats_grid;
+  } else {
+    int64_t w[NB], cap[NB];
+    for (int i = 0; i < n; ++i) {
+      w[i] = (int64_t)Ls[i]->qa.nct * Ls[i]->qa.nrc;
+      cap[i] = stats_grid_cap(w[i]);
+    }
+    split_grid(n, w, cap, Ls[0]->stats_full, sg);
+  }
+  StatsBatch<NB> P;
+  ArgsBatch<NB> C;
+  std::memset(&P, 0, sizeof(P));
+  std::memset(&C, 0, sizeof(C));
+  int comb_smem = 0;
+  for (int i = 0; i < n; ++i) {
+    QuantizeLaunch& L = *Ls[i];
+    L.qa.stats_grid = (int)sg[i];  // the segment records' layout
+    MB_CUDA_TRY(cudaMemsetAsync(L.qa.ws.hdr, 0, L.hdr_bytes, stream));
+    P.tmap[i] = L.tmap;
+    P.a[i] = L.qa;
+    P.use_tma[i] = L.tma ? 1 : 0;
+    C.a[i] = L.qa;
+    cg[i] = L.comb_grid;
+    comb_smem = std::max(comb_smem, L.qa.comb_smem);
+  }
+  fill_map(P.bm, n, sg);
+  fill_map(C.bm, n, cg);
+  auto kern = sens ? stats_kernel<true, NB> : stats_kernel<false, NB>;
+  static std::atomic<uint64_t> sattr[2];
+  MB_CUDA_TRY(set_smem_limit_once(kern, kStatsSmem, sattr[sens ? 1 : 0]));
+  kern<<<(unsigned)P.bm.cta0[n], kStatsThreads, kStatsSmem, stream>>>(P);
+  MB_LAUNCH_CHECK("stats_kernel");
+  auto comb = sens ? combine_kernel<true, NB> : combine_kernel<false, NB>;
+  static std::atomic<uint64_t> cattr[2];
+  MB_CUDA_TRY(set_smem_limit_once(comb, kCombSmem, cattr[sens ? 1 : 0]));
+  return launch_pdl(comb, dim3((unsigned)C.bm.cta0[n]), dim3(kCombThreads), (size_t)comb_smem,
+                    stream, C);
+}
+
+// The tables kernel for n <= NB matrices: a thread per group, a warp per
+// distinct 2nd-order chunk.
+template <int NB>
+mb_status launch_tables(QuantizeLaunch* const* Ls, int n, cudaStream_t stream) {
+  ArgsBatch<NB> T;
+  std::memset(&T, 0, sizeof(T));
+  int64_t tg[NB];
+  for (int i = 0; i < n; ++i) {
+    const QArgs& qa = Ls[i]->qa;
+    T.a[i] = qa;
+    const int64_t nchunks = qa.cl.ntab_full + qa.cl.has_partial;
+    tg[i] = std::max<int64_t>(
+        1, std::min<int64_t>(32, ceil_div(std::max<int64_t>(qa.ng, nchunks * 32), 256)));
+  }
+  fill_map(T.bm, n, tg);
+  return launch_pdl(tables_kernel<NB>, dim3((unsigned)T.bm.cta0[n]), dim3(256), 0, stream, T);
+}
+
+// The exact-sum kernel, the tables, encode and (with csr) the CSR extraction
+// for n <= NB matrices, chained with PDL.  A batch (n > 1) needs every
+// matrix on the wide-tile encode; its full grid is split by tile count.
+template <int NB>
+mb_status launch_tables_encode_batch(QuantizeLaunch* const* Ls, int n, cudaStream_t stream,
+                                     const CsrOut* csr) {
+  ArgsBatch<NB> X;
+  std::memset(&X, 0, sizeof(X));
+  int64_t xg[NB];
+  for (int i = 0; i < n; ++i) {
+    X.a[i] = Ls[i]->qa;
+    // one matrix: the whole GPU; in a batch enough warps for the chunk
+    // programs of four pending groups at once
+    xg[i] = n == 1 ? kExactCtas
+                   : std::max<int64_t>(16, std::min<int64_t>(kExactCtas, (Ls[i]->qa.nrc + 1) / 2));
+  }
+  fill_map(X.bm, n, xg);
+  if (mb_status st = launch_pdl(exact_kernel<NB>, dim3((unsigned)X.bm.cta0[n]), dim3(256), 0,
+                                stream, X))
     return st;
-  if (L.enc3)
-    return launch_pdl(encode3_kernel, dim3((unsigned)L.enc3_grid), dim3(kE3Threads), kE3Smem,
-                      stream, L.tmap, L.omaps, L.qa, L.tma ? 1 : 0);
-  return launch_pdl(encode_kernel, dim3((unsigned)L.enc_grid), dim3(kEncThreads), kEncSmem,
-                    stream, L.tmap, L.qa, L.tma ? 1 : 0, L.vec_out);
+  if (mb_status st = launch_tables<NB>(Ls, n, stream)) return st;
+  if (n == 1 && !Ls[0]->enc3) {
+    const QuantizeLaunch& L = *Ls[0];
+    if (mb_status st = launch_pdl(encode_kernel, dim3((unsigned)L.enc_grid), dim3(kEncThreads),
+                                  kEncSmem, stream, L.tmap, L.qa, L.tma ? 1 : 0, L.vec_out))
+      return st;
+  } else {
+    int64_t eg[NB];
+    if (n == 1) {
+      eg[0] = Ls[0]->enc3_grid;
+    } else {
+      int64_t w[NB], cap[NB];
+      for (int i = 0; i < n; ++i) {
+        MB_REQUIRE(Ls[i]->enc3, "a batch needs the wide-tile encode for every matrix");
+        w[i] = cap[i] = (int64_t)(Ls[i]->qa.ng / kE3Groups) * Ls[i]->qa.nrc;
+      }
+      split_grid(n, w, cap, Ls[0]->enc3_full, eg);
+    }
+    Enc3Batch<NB> E;
+    std::memset(&E, 0, sizeof(E));
+    for (int i = 0; i < n; ++i) {
+      E.tmap[i] = Ls[i]->tmap;
+      E.om[i] = Ls[i]->omaps;
+      E.a[i] = Ls[i]->qa;
+      E.use_tma[i] = Ls[i]->tma ? 1 : 0;
+    }
+    fill_map(E.bm, n, eg);
+    static std::atomic<uint64_t> eattr{0};
+    MB_CUDA_TRY(set_smem_limit_once(encode3_kernel<NB>, kE3Smem, eattr));
+    if (mb_status st = launch_pdl(encode3_kernel<NB>, dim3((unsigned)E.bm.cta0[n]),
+                                  dim3(kE3Threads), kE3Smem, stream, E))
+      return st;
+  }
+  if (csr == nullptr) return MB_OK;
+  CsrBatch<NB> B;
+  std::memset(&B, 0, sizeof(B));
+  int64_t bg[NB];
+  for (int i = 0; i < n; ++i) {
+    B.a[i] = Ls[i]->qa;
+    B.capacity[i] = csr[i].capacity;
+    B.vals[i] = csr[i].vals;
+    B.cols[i] = csr[i].cols;
+    bg[i] = std::max<int64_t>(1, std::min<int64_t>(ceil_div(Ls[i]->qa.M, 8), 1184 / n));
+  }
+  fill_map(B.bm, n, bg);
+  return launch_pdl(extract_cap_kernel<NB>, dim3((unsigned)B.bm.cta0[n]), dim3(256), 0, stream,
+                    B);
+}
+
+mb_status launch_stats(QuantizeLaunch& L, cudaStream_t stream) {
+  QuantizeLaunch* p = &L;
+  return launch_stats_batch<1>(&p, 1, stream);
+}
+
+mb_status launch_tables_encode(QuantizeLaunch& L, cudaStream_t stream, const CsrOut* csr) {
+  QuantizeLaunch* p = &L;
+  return launch_tables_encode_batch<1>(&p, 1, stream, csr);
 }
 
 // ---------------------------------------------------------------------------
@@ -3437,7 +3750,7 @@ extern "C" mb_status mb_quantize(const void* weights_fp16, int64_t M, int64_t K,
                                       workspace_bytes, false, L))
     return st;
   if (mb_status st = launch_stats(L, stream)) return st;
-  return launch_tables_encode(L, stream);
+  return launch_tables_encode(L, stream, nullptr);
 }
 
 extern "C" mb_status mb_quantize_extract_outliers(const void* weights_fp16, int64_t M, int64_t K,
@@ -3475,26 +3788,110 @@ extern "C" mb_status mb_quantize_csr(const void* weights_fp16, int64_t M, int64_
                                      void* outlier_values_fp16, int32_t* outlier_col_indices,
                                      int64_t outlier_capacity, void* workspace,
                                      size_t workspace_bytes, mb_stream_t stream_) {
-  MB_REQUIRE(outlier_capacity >= 0, "outlier_capacity must not be negative");
-  MB_REQUIRE(outlier_capacity == 0 || (outlier_values_fp16 && outlier_col_indices),
-             "CSR pointers must not be null when outlier_capacity > 0");
-  if (mb_status st = mb_quantize(weights_fp16, M, K, ratio_4bit, hessian_diag, hessian_numel,
-                                 packed_2bit, packed_4bit, scales_1st_fp16, zeros_1st,
-                                 scales_2nd_fp16, zeros_2nd, scales_1st_quant, group_precision,
-                                 outlier_row_ptrs, nnz_device, workspace, workspace_bytes,
-                                 stream_))
+  mb_quantize_job job;
+  job.weights_fp16 = weights_fp16;
+  job.M = M;
+  job.K = K;
+  job.ratio_4bit = ratio_4bit;
+  job.hessian_diag = hessian_diag;
+  job.hessian_numel = hessian_numel;
+  job.packed_2bit = packed_2bit;
+  job.packed_4bit = packed_4bit;
+  job.scales_1st_fp16 = scales_1st_fp16;
+  job.zeros_1st = zeros_1st;
+  job.scales_2nd_fp16 = scales_2nd_fp16;
+  job.zeros_2nd = zeros_2nd;
+  job.scales_1st_quant = scales_1st_quant;
+  job.group_precision = group_precision;
+  job.outlier_row_ptrs = outlier_row_ptrs;
+  job.nnz_device = nnz_device;
+  job.outlier_values_fp16 = outlier_values_fp16;
+  job.outlier_col_indices = outlier_col_indices;
+  job.outlier_capacity = outlier_capacity;
+  job.workspace = workspace;
+  job.workspace_bytes = workspace_bytes;
+  return mb_quantize_csr_many(&job, 1, stream_);
+}
+
+extern "C" mb_status mb_quantize_csr_many(const mb_quantize_job* jobs, int64_t n,
+                                          mb_stream_t stream_) {
+  clear_error();
+  MB_REQUIRE(n >= 0, "the job count must not be negative");
+  MB_REQUIRE(n == 0 || jobs != nullptr, "jobs must not be null");
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  // every job is checked before anything is launched
+  std::vector<QuantizeLaunch> Ls((size_t)n);
+  std::vector<CsrOut> csr((size_t)n);
+  for (int64_t i = 0; i < n; ++i) {
+    const mb_quantize_job& j = jobs[i];
+    MB_REQUIRE(j.outlier_capacity >= 0, "outlier_capacity must not be negative");
+    MB_REQUIRE(j.outlier_capacity == 0 || (j.outlier_values_fp16 && j.outlier_col_indices),
+               "CSR pointers must not be null when outlier_capacity > 0");
+    if (mb_status st = quantize_prepare(
+            j.weights_fp16, j.M, j.K, j.ratio_4bit, j.hessian_diag, j.hessian_numel,
+            j.packed_2bit, j.packed_4bit, j.scales_1st_fp16, j.zeros_1st, j.scales_2nd_fp16,
+            j.zeros_2nd, j.scales_1st_quant, j.group_precision, j.outlier_row_ptrs,
+            j.nnz_device, j.workspace, j.workspace_bytes, false, Ls[(size_t)i]))
+      return st;
+    csr[(size_t)i] = CsrOut{static_cast<__half*>(j.outlier_values_fp16),
+                            j.outlier_col_indices, j.outlier_capacity};
+  }
+  // consecutive jobs on the wide-tile encode with the same sensitivity pass
+  // share launches, kMaxBatch at a time
+  int64_t i = 0;
+  while (i < n) {
+    QuantizeLaunch* grp[kMaxBatch];
+    int k = 0;
+    int64_t e = i;
+    if (Ls[(size_t)i].enc3)
+      while (e < n && k < kMaxBatch && Ls[(size_t)e].enc3 && Ls[(size_t)e].sens == Ls[(size_t)i].sens)
+        grp[k++] = &Ls[(size_t)e++];
+    if (k <= 1) {
+      if (mb_status st = launch_stats(Ls[(size_t)i], stream)) return st;
+      if (mb_status st = launch_tables_encode(Ls[(size_t)i], stream, &csr[(size_t)i])) return st;
+      ++i;
+      continue;
+    }
+    if (mb_status st = launch_stats_batch<kMaxBatch>(grp, k, stream)) return st;
+    if (mb_status st = launch_tables_encode_batch<kMaxBatch>(grp, k, stream, &csr[(size_t)i]))
+      return st;
+    i = e;
+  }
+  return MB_OK;
+}
+
+extern "C" mb_status mb_quantize_exact_sums(const void* weights_fp16, int64_t M, int64_t K,
+                                            double ratio_4bit, const float* hessian_diag,
+                                            int64_t hessian_numel, float* sums,
+                                            uint8_t* group_precision, void* workspace,
+                                            size_t workspace_bytes, mb_stream_t stream_) {
+  clear_error();
+  MB_REQUIRE(sums != nullptr && group_precision != nullptr, "output pointers must not be null");
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  QuantizeLaunch L;
+  if (mb_status st = quantize_prepare(weights_fp16, M, K, ratio_4bit, hessian_diag,
+                                      hessian_numel, nullptr, nullptr, nullptr, nullptr, nullptr,
+                                      nullptr, nullptr, nullptr, nullptr, nullptr, workspace,
+                                      workspace_bytes, true, L))
     return st;
-  Workspace ws;
-  workspace_layout(M, K, static_cast<char*>(workspace), &ws);
-  const int64_t ng = ceil_div(K, kGroup1);
-  const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(ceil_div(M, 8), 1184));
-  return launch_pdl(extract_cap_kernel, dim3((unsigned)grid), dim3(256), 0,
-                    reinterpret_cast<cudaStream_t>(stream_),
-                    static_cast<const __half*>(weights_fp16), M, K, (int)ng,
-                    (const GroupParams*)ws.params, (const uint8_t*)ws.prec,
-                    (const int32_t*)outlier_row_ptrs, (const int32_t*)nnz_device,
-                    outlier_capacity, static_cast<__half*>(outlier_values_fp16),
-                    outlier_col_indices, &ws.hdr->status, kOutlierFma);
+  MB_REQUIRE(L.sens && L.qa.n4 < L.qa.ng,
+             "the exact sums need a hessian and a ratio_4bit selecting some but not all groups");
+  L.qa.gp = group_precision;
+  L.qa.all_pending = 1;
+  if (mb_status st = launch_stats(L, stream)) return st;
+  ArgsBatch<1> X;
+  std::memset(&X, 0, sizeof(X));
+  X.a[0] = L.qa;
+  X.bm.n = 1;
+  X.bm.cta0[0] = 0;
+  X.bm.cta0[1] = kExactCtas;
+  if (mb_status st = launch_pdl(exact_kernel<1>, dim3(kExactCtas), dim3(256), 0, stream, X))
+    return st;
+  QuantizeLaunch* p = &L;
+  if (mb_status st = launch_tables<1>(&p, 1, stream)) return st;
+  MB_CUDA_TRY(cudaMemcpyAsync(sums, L.qa.ws.sens, sizeof(float) * (size_t)L.qa.ng,
+                              cudaMemcpyDeviceToDevice, stream));
+  return MB_OK;
 }
 
 extern "C" mb_status mb_quantize_info(const void* workspace, size_t workspace_bytes, int64_t M,
@@ -3633,5 +4030,5 @@ extern "C" mb_status mb_rows_encode(const void* weights_slab, int64_t M_slab, in
                                       workspace_bytes, false, L))
     return st;
   L.qa.exact_thresholds = 1;  // the selection took the parameters from all slabs' records
-  return launch_tables_encode(L, stream);
+  return launch_tables_encode(L, stream, nullptr);
 }
