@@ -14,7 +14,7 @@ ranks.  Rank 0 prints one JSON line.
              quantized by one CUDA-graph replay of its launches
              (memboost_b200._C.QuantizeBatch: stats, tables, encode and the
              CSR extraction chained on the device, one launch of each kernel
-             per 8 matrices, 2 graph branches); step k + 1 is enqueued
+             per 8 matrices, 8 graph branches); step k + 1 is enqueued
              before step k's outlier counts are read
   e2e        the public memboost_b200.quantize() call per matrix with host
              buffers: pinned H2D copy of the weights and hessian, quantize,
@@ -78,7 +78,7 @@ def parse():
     p.add_argument("--layers", type=int, default=32, help="model layers (32 = the config)")
     p.add_argument("--per-launch", type=int, default=8,
                    help="matrices sharing one launch of each quantize kernel (1-8)")
-    p.add_argument("--branches", type=int, default=2, help="parallel CUDA-graph branches")
+    p.add_argument("--branches", type=int, default=8, help="parallel CUDA-graph branches")
     return p.parse_args()
 
 

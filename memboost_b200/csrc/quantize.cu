@@ -2401,12 +2401,12 @@ __device__ __forceinline__ void post_prologue(const QArgs& a, int bid, int G) {
 }
 
 // When groups may hold outliers: the last encode CTA to finish turns the
-// per-row counts into row pointers (all threads of every CTA call it).
+// per-row counts into row pointers (all threads of every CTA call it;
+// `part`: NT entries of shared scratch the CTA no longer needs).
 template <int NT>
-__device__ __forceinline__ void post_rowptr_scan(const QArgs& a, int G) {
+__device__ __forceinline__ void post_rowptr_scan(const QArgs& a, int G, long long* part) {
   if (a.ws.hdr->any_irregular == 0) return;
   __shared__ int s_last;
-  __shared__ long long part[NT];
   const int tid = threadIdx.x;
   const int64_t M = a.M;
   __threadfence();
@@ -2801,13 +2801,70 @@ __global__ void __launch_bounds__(kEncThreads, 2)
     for (int s = 0; s < kEncStages; ++s)
       if (bad & (1u << s)) (void)mbar_wait(&full[s], 0u), (void)mbar_wait(&full[s], 1u);
   }
-  post_rowptr_scan<kEncThreads>(a, (int)gridDim.x);
+  post_rowptr_scan<kEncThreads>(a, (int)gridDim.x, reinterpret_cast<long long*>(dsm));
 }
 
 
+// scales_1st, zeros_1st and scales_1st_quant of rows [M b / G, M (b + 1) / G)
+// (CTA b of G), each a contiguous stretch of its array written with 16-byte
+// stores.  scales_1st and zeros_1st are the same in every row (the column
+// group's parameters); the 2nd-order code of (r, g) takes the chunk table
+// entry of its flat index r ng + g (quantize.cu:245-272), which for rows in
+// full chunks repeats every rp = 256 / gcd(ng, 256) rows: those rows copy
+// one of rp pattern rows built in shared memory, the others compute it.
+// Needs ng % 16 == 0 and 16-byte aligned arrays; `scratch` is shared memory
+// the CTA no longer needs.
+__device__ __noinline__ void fill_row_arrays(const QArgs& a, int bid, int G, uint8_t* scratch,
+                                             size_t scratch_bytes) {
+  const int ng = a.ng, tid = threadIdx.x, nt = blockDim.x;
+  const int64_t r0 = a.M * bid / G, r1 = a.M * (bid + 1) / G;
+  uint16_t* sc = reinterpret_cast<uint16_t*>(scratch);  // [ng] fp16 bits
+  int8_t* zr = reinterpret_cast<int8_t*>(scratch + 2 * ng);
+  uint8_t* pat = scratch + 3 * ng;  // [rp][ng]
+  const int rp = (int)((int64_t)a.cl.period * kGroup2 / ng);
+  const int64_t full_rows = a.cl.nfull * kGroup2 / ng;  // rows whose scales lie in full chunks
+  const bool use_pat = (size_t)(3 + rp) * (size_t)ng <= scratch_bytes;
+  for (int g = tid; g < ng; g += nt) {
+    const GroupParams& p = a.ws.params[2 * g + a.ws.prec[g]];
+    sc[g] = (uint16_t)p.scale_h;
+    zr[g] = (int8_t)p.zero;
+  }
+  __syncthreads();
+  if (use_pat)
+    for (int e = tid; e < rp * ng; e += nt) {
+      const int ph = e / ng, g = e - (e / ng) * ng;
+      pat[e] = sq_direct(a, __half2float(__ushort_as_half(sc[g])), ph, g);
+    }
+  __syncthreads();
+  const int n = (int)((r1 - r0) * ng);  // elements of the CTA's stretch (below 2^31)
+  const int64_t e0 = r0 * ng;
+  uint4* sc_out = reinterpret_cast<uint4*>(a.scales1 + e0);
+  for (int j = tid; j < n / 8; j += nt)
+    sc_out[j] = *reinterpret_cast<const uint4*>(sc + (j * 8) % ng);
+  uint4* z_out = reinterpret_cast<uint4*>(a.zeros1 + e0);
+  uint4* q_out = reinterpret_cast<uint4*>(a.sq + e0);
+  for (int j = tid; j < n / 16; j += nt) {
+    const int l = j * 16, rl = l / ng, g = l - rl * ng;
+    z_out[j] = *reinterpret_cast<const uint4*>(zr + g);
+    const int64_t r = r0 + rl;
+    uint4 q;
+    if (use_pat && r < full_rows) {
+      q = *reinterpret_cast<const uint4*>(pat + (int)(r % rp) * ng + g);
+    } else {
+      uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+      for (int k = 0; k < 16; ++k)
+        w[k >> 2] |= (uint32_t)sq_direct(a, __half2float(__ushort_as_half(sc[g + k])), r, g + k)
+                     << (8 * (k & 3));
+      q = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    q_out[j] = q;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // encode, wide-tile form: tiles of 128 rows x 256 columns (16 groups), lane =
-// row, outputs written whole by TMA.  Warp w takes the 32 rows
+// row, packed words written whole by TMA.  Warp w takes the 32 rows
 // [32 (w & 3), 32 (w & 3) + 32) of the tile and four of its groups, the
 // quarter ((w >> 2) + i) & 3 on the CTA's i-th tile, so every warp carries
 // the same mix of 2-bit / 4-bit groups over any four tiles and no work queue
@@ -2815,35 +2872,31 @@ __global__ void __launch_bounds__(kEncThreads, 2)
 // code per 2/4-bit pattern of the quarter) and writes the words to a staging
 // tile laid out as the output rows (packed_2bit with the 64-byte swizzle,
 // packed_4bit with the 128-byte swizzle: conflict-free).  One thread then
-// stores the whole tile -- 64 bytes of packed_2bit, 128 of packed_4bit, 32
-// of scales_1st and 16 each of zeros_1st and 2nd-order codes per row -- with
-// five TMA stores, so every output row segment leaves as one write.
-// scales_1st and zeros_1st are the same in every row of a column tile: their
-// 128-row blocks are built once per column tile.  Tile stages are released
-// per warp (a 16-arrival mbarrier).  Needs ng % 16 == 0 and 16-byte aligned
-// outputs; other shapes take encode_kernel.  CTA b takes the tiles
-// [floor(b T / G), floor((b + 1) T / G)) of the T tiles in column-major order.
+// stores the tile's 64 bytes of packed_2bit and 128 of packed_4bit per row
+// with two TMA stores.  The per-row arrays (scales_1st, zeros_1st, 2nd-order
+// codes: 16 or 32 bytes per row and tile, too narrow for efficient stores)
+// are written after the tiles, row by row (fill_row_arrays).  Tiles arrive
+// through a three-stage TMA ring; a stage is released per warp (a 16-arrival
+// mbarrier) and refilled as soon as the last warp is done with it.  Needs
+// ng % 16 == 0 and 16-byte aligned outputs; other shapes take encode_kernel.
+// CTA b takes the tiles [floor(b T / G), floor((b + 1) T / G)) of the T
+// tiles in column-major order.
 // ---------------------------------------------------------------------------
 constexpr int kE3Cols = 256;
 constexpr int kE3Groups = kE3Cols / kGroup1;        // 16
 constexpr int kE3Threads = 512;                     // 16 warps
-constexpr int kE3Stages = 2;
+constexpr int kE3Stages = 3;
 constexpr int kE3Tile = kChunkRows * kE3Cols * 2;   // 64 KB: four 64-column boxes
 constexpr int kE3P2 = kChunkRows * 64;              // 128 rows x 16 words
 constexpr int kE3P4 = kChunkRows * 128;             // 128 rows x 32 words
-constexpr int kE3Sq = kChunkRows * 16;              // 128 rows x 16 codes
-constexpr int kE3Out = kE3P2 + kE3P4 + kE3Sq;       // one staging buffer: 26 KB
+constexpr int kE3Out = kE3P2 + kE3P4;               // the staging buffer: 24 KB
 constexpr int kE3OffOut = kE3Stages * kE3Tile;
-constexpr int kE3OffScale = kE3OffOut + 2 * kE3Out;
-constexpr int kE3OffZero = kE3OffScale + kChunkRows * 32;
-constexpr int kE3Smem = kE3OffZero + kChunkRows * 16 + 1024;  // + alignment slack
-static_assert(kE3OffOut % 1024 == 0 && kE3Out % 1024 == 0 && kE3P2 % 1024 == 0 &&
-                  kE3OffScale % 128 == 0 && kE3OffZero % 128 == 0,
+constexpr int kE3Smem = kE3OffOut + kE3Out + 1024;  // + alignment slack
+static_assert(kE3OffOut % 1024 == 0 && kE3Out % 1024 == 0 && kE3P2 % 1024 == 0,
               "staging alignment");
 
 struct __align__(16) Enc3Ctx {
   uint4 thr[kE3Groups][4];                    // T_1..T_15 as broadcast half2, +inf pad
-  uint8_t sqrow[kE3Groups][kE3Groups];        // 2nd-order code by (row mod rp, group); rp <= 16
   uint8_t kind[kE3Groups];
   uint8_t gs[kE3Groups];
   uint8_t pr[kE3Groups];
@@ -2851,9 +2904,8 @@ struct __align__(16) Enc3Ctx {
 };
 
 struct Enc3Maps {
-  CUtensorMap p2, p4, sc, z, sq;  // packed_2bit (box 128 x 16, 64B swizzle), packed_4bit
-                                  // (128 x 32, 128B swizzle), scales_1st (128 x 16),
-                                  // zeros_1st (128 x 16), scales_1st_quant (128 x 16)
+  CUtensorMap p2, p4;  // packed_2bit (box 128 x 16, 64B swizzle), packed_4bit (128 x 32,
+                       // 128B swizzle)
 };
 
 // Codes of one row's four runs of a quarter whose groups are all regular and
@@ -2901,8 +2953,6 @@ __device__ __forceinline__ void encode3_body(const CUtensorMap& tmap, const Enc3
   const int slab = warp & 3, qsel = warp >> 2;
   const int rr = slab * 32 + lane;  // this lane's row in the tile
   const int sw = rr & 7;            // its 128-byte swizzle phase
-  uint8_t* cscale = dsm + kE3OffScale;
-  uint8_t* czero = dsm + kE3OffZero;
   if (tid == 0) {
     for (int s = 0; s < kE3Stages; ++s) {
       mbar_init(&full[s], 1);
@@ -2931,9 +2981,6 @@ __device__ __forceinline__ void encode3_body(const CUtensorMap& tmap, const Enc3
   __syncthreads();  // barrier initialisation visible
   if (tid == 0 && use_tma)
     for (int s = 0; s < kE3Stages && s < ntile_cta; ++s) issue(s);
-  const int P256 = a.cl.period * kGroup2;
-  const int rp = P256 / ng;                              // divides 16 here
-  const int64_t full_rows = a.cl.nfull * kGroup2 / ng;  // rows whose scales lie in full chunks
   bool failed = false;
   uint32_t bad = 0;  // thread 0: stages whose wait ran out
   int cur_ct = -1;
@@ -2942,25 +2989,17 @@ __device__ __forceinline__ void encode3_body(const CUtensorMap& tmap, const Enc3
     const int s = (int)(i % kE3Stages);
     const uint32_t ph = (uint32_t)((i / kE3Stages) & 1);
     if (ct != cur_ct) {
-      // a new column tile: every warp is done with the old context and the
-      // constant blocks' last TMA stores have read them
-      if (cur_ct >= 0) {
-        if (tid == 0) bulk_wait_read<0>();
-        __syncthreads();
-      }
+      // a new column tile (every warp read the old context before the last
+      // tile's barriers)
       const int64_t g = (int64_t)ct * kE3Groups + warp;  // warp w builds group w
       uint32_t t = 0x7C007C00u;  // +inf: never reached
       int kind = kEncKindNone, pr = 0, gs = 0;
-      uint16_t sh = 0;
-      int8_t z = 0;
       if (g < ng) {
         pr = a.ws.prec[g];
         const GroupParams& p = a.ws.params[2 * g + pr];
         if (lane < 15) t = (uint32_t)p.thresh[lane] * 0x00010001u;
         kind = (p.flags & kFlagRegular) ? (pr ? kEncKind4 : kEncKind2) : kEncKindIrr;
         gs = (int)min64(kGroup1, a.K - g * kGroup1);
-        sh = (uint16_t)p.scale_h;
-        z = (int8_t)p.zero;
       }
       if (lane < 16) (&cx.thr[warp][0].x)[lane] = t;
       if (lane == 0) {
@@ -2968,23 +3007,6 @@ __device__ __forceinline__ void encode3_body(const CUtensorMap& tmap, const Enc3
         cx.gs[warp] = (uint8_t)gs;
         cx.pr[warp] = (uint8_t)pr;
       }
-      for (int r = lane; r < kChunkRows; r += 32) {
-        reinterpret_cast<uint16_t*>(cscale + r * 32)[warp] = sh;
-        reinterpret_cast<int8_t*>(czero + r * 16)[warp] = z;
-      }
-      // 2nd-order codes of group w by row phase (rows in full chunks)
-      if (lane < rp) {
-        uint8_t q = 0;
-        if (g < ng) {
-          const int u = (int)(((int64_t)lane * ng + g) % P256);
-          const float4 ch = a.ws.chunk_tab[min(u >> 8, a.cl.ntab_full)];
-          const float s1f = __half2float(__ushort_as_half(sh));
-          const int q2 = f2i_rz(roundf(__fdiv_rn(__fsub_rn(s1f, ch.x), ch.y)));
-          q = (uint8_t)max(0, min(15, q2));
-        }
-        cx.sqrow[lane][warp] = q;
-      }
-      fence_proxy_async_smem();
       __syncthreads();
       if (tid < 4) {
         int pat = 0;
@@ -3084,33 +3106,24 @@ __device__ __forceinline__ void encode3_body(const CUtensorMap& tmap, const Enc3
           }
         }
     }
-    // the tile's stage is free once every warp has read its part
+    // the tile's stage is free once every warp has read its part; thread 0
+    // refills it as soon as the last warp is done
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
-    const int64_t row = row0 + rr;
-    if (cnt && row < M) atomicAdd(a.ws.row_counts + row, (int)cnt);
-    // 2nd-order codes of this lane's row
-    uint32_t q4;
-    if (row < full_rows) {
-      q4 = *reinterpret_cast<const uint32_t*>(&cx.sqrow[(int)(row & (rp - 1))][4 * qq]);
-    } else {
-      q4 = 0;
-      if (row < M) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint16_t shb = reinterpret_cast<const uint16_t*>(cscale)[4 * qq + q];
-          q4 |= (uint32_t)sq_direct(a, __half2float(__ushort_as_half(shb)), row,
-                                    (int64_t)ct * kE3Groups + 4 * qq + q)
-                << (8 * q);
-        }
+    if (tid == 0 && use_tma && i + kE3Stages < ntile_cta && !failed) {
+      if (mbar_wait(&empty[s], ph)) {
+        fence_proxy_async_smem();
+        issue(s);
+      } else {
+        failed = true;
       }
     }
-    // staging buffer (i & 1): the stores of two tiles ago have read it
-    const int b = (int)(i & 1);
-    uint8_t* s2 = dsm + kE3OffOut + b * kE3Out;
+    const int64_t row = row0 + rr;
+    if (cnt && row < M) atomicAdd(a.ws.row_counts + row, (int)cnt);
+    // the staging buffer: the previous tile's stores have read it
+    uint8_t* s2 = dsm + kE3OffOut;
     uint8_t* s4 = s2 + kE3P2;
-    uint8_t* ssq = s4 + kE3P4;
-    if (tid == 0) bulk_wait_read<1>();
+    if (tid == 0) bulk_wait_read<0>();
     __syncthreads();
     *reinterpret_cast<uint4*>(s2 + rr * 64 + ((qq ^ ((rr >> 1) & 3)) << 4)) =
         make_uint4(w2[0], w2[1], w2[2], w2[3]);
@@ -3118,26 +3131,13 @@ __device__ __forceinline__ void encode3_body(const CUtensorMap& tmap, const Enc3
         make_uint4(w4[0], w4[1], w4[2], w4[3]);
     *reinterpret_cast<uint4*>(s4 + rr * 128 + (((2 * qq + 1) ^ sw) << 4)) =
         make_uint4(w4[4], w4[5], w4[6], w4[7]);
-    *reinterpret_cast<uint32_t*>(ssq + rr * 16 + 4 * qq) = q4;
     fence_proxy_async_smem();
     __syncthreads();
     if (tid == 0) {
       const int x = ct * kE3Groups, y = (int)row0;
       tma_store_2d(&om.p2, s2, x, y);
       tma_store_2d(&om.p4, s4, 2 * x, y);
-      tma_store_2d(&om.sq, ssq, x, y);
-      tma_store_2d(&om.sc, cscale, x, y);
-      tma_store_2d(&om.z, czero, x, y);
       bulk_commit();
-      // refill this stage once every warp has released it
-      if (use_tma && i + kE3Stages < ntile_cta && !failed) {
-        if (mbar_wait(&empty[s], ph)) {
-          fence_proxy_async_smem();
-          issue(s);
-        } else {
-          failed = true;
-        }
-      }
     }
     if (++rc == nrc) {
       rc = 0;
@@ -3152,7 +3152,9 @@ __device__ __forceinline__ void encode3_body(const CUtensorMap& tmap, const Enc3
     for (int s = 0; s < kE3Stages; ++s)
       if (bad & (1u << s)) (void)mbar_wait(&full[s], 0u), (void)mbar_wait(&full[s], 1u);
   }
-  post_rowptr_scan<kE3Threads>(a, G);
+  // the tiles and the staging buffer are free: the per-row arrays
+  fill_row_arrays(a, bid, G, dsm, (size_t)(kE3Smem - 1024));
+  post_rowptr_scan<kE3Threads>(a, G, reinterpret_cast<long long*>(dsm));
 }
 
 template <int NB>
@@ -3424,10 +3426,7 @@ mb_status quantize_prepare(const void* weights_fp16, int64_t M, int64_t K, doubl
       (ng % kE3Groups == 0) && al16(packed_2bit) && al16(packed_4bit) &&
       al16(scales_1st_fp16) && al16(zeros_1st) && al16(scales_1st_quant) &&
       make_tensor_map_2d(&L.omaps.p2, packed_2bit, 4, um, ung, kChunkRows, 16, 64) &&
-      make_tensor_map_2d(&L.omaps.p4, packed_4bit, 4, um, 2 * ung, kChunkRows, 32, 128) &&
-      make_tensor_map_2d(&L.omaps.sc, scales_1st_fp16, 2, um, ung, kChunkRows, 16, 0) &&
-      make_tensor_map_2d(&L.omaps.z, zeros_1st, 1, um, ung, kChunkRows, 16, 0) &&
-      make_tensor_map_2d(&L.omaps.sq, scales_1st_quant, 1, um, ung, kChunkRows, 16, 0);
+      make_tensor_map_2d(&L.omaps.p4, packed_4bit, 4, um, 2 * ung, kChunkRows, 32, 128);
   if (L.enc3) {
     static std::atomic<int> occ3[64];
     int per_sm = 1;
