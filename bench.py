@@ -79,6 +79,14 @@ def parse():
     p.add_argument("--per-launch", type=int, default=8,
                    help="matrices sharing one launch of each quantize kernel (1-8)")
     p.add_argument("--branches", type=int, default=8, help="parallel CUDA-graph branches")
+    p.add_argument("--only", default=None,
+                   choices=("mlp_pair", "single_4096", "gptq_layer", "hessian", "qgemv",
+                            "rowsplit", "gptq_stream"),
+                   help="run one sub-record alone and print it (small cases for profiling)")
+    p.add_argument("--tokens", type=int, default=262144,
+                   help="calibration tokens of the gptq_layer / hessian records")
+    p.add_argument("--sub-steps", type=int, default=None,
+                   help="timed steps of the mlp_pair / single_4096 records")
     return p.parse_args()
 
 
@@ -421,7 +429,8 @@ def run_ours(args, ws, rank, local):
                    "l2": "per-step inputs 12.95 GB (1.6 GB per rank at 8) > 126 MB L2; "
                          "not flushed",
                    "parallelism": f"{ws} ranks, matrices split by size (LPT), no collective on "
-                                  "the data path"},
+                                  "the data path",
+                   "schedule": {"branches": args.branches, "per_launch": args.per_launch}},
         "roofline": {"bound": "hbm", "achieved": round(achieved / ws, 1), "peak": hbm,
                      "unit": "GB/s", "frac": round(achieved / ws / hbm, 4),
                      "peak_kind": peak_kind, "of": f"{peak_kind} hbm_gbs per GPU",
@@ -635,10 +644,11 @@ def sub_single_4096(steps=200, warmup=5):
                                         "l2": "8 rotated input/output sets (8 x 41 MB)"}}}
 
 
-def sub_gptq(tokens=262144, reps=2):
+def sub_gptq(tokens=262144, reps=2, hessian_only=False):
     """Config 4: one Llama-7B layer's GPTQ (4 tcgen05 Hessians over `tokens`
     calibration tokens, 4 inverses, 7 GPTQ updates, 7 quantize calls), s per
-    layer; and the Hessians alone in TFLOP/s of N*K*(K+1)."""
+    layer; and the Hessians alone in TFLOP/s of N*K*(K+1).  hessian_only
+    skips the layer timing (a small case for profiling the Hessian kernel)."""
     import torch
 
     from memboost_b200 import gptq
@@ -646,16 +656,18 @@ def sub_gptq(tokens=262144, reps=2):
     dev = torch.device("cuda", torch.cuda.current_device())
     weights, inputs = wl.gptq_layer(tokens=tokens, device=dev)
     torch.cuda.synchronize()
-    gptq.quantize_layer(weights, inputs)  # warm-up
-    torch.cuda.synchronize()
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    t0.record()
-    for _ in range(reps):
-        gptq.quantize_layer(weights, inputs)
-    t1.record()
-    torch.cuda.synchronize()
-    s_layer = t0.elapsed_time(t1) / 1e3 / reps
+    s_layer = None
+    if not hessian_only:
+        gptq.quantize_layer(weights, inputs)  # warm-up
+        torch.cuda.synchronize()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(reps):
+            gptq.quantize_layer(weights, inputs)
+        t1.record()
+        torch.cuda.synchronize()
+        s_layer = round(t0.elapsed_time(t1) / 1e3 / reps, 4)
     hres = {}
     flops_all, ms_all = 0.0, 0.0
     for key, x in inputs.items():
@@ -681,7 +693,7 @@ def sub_gptq(tokens=262144, reps=2):
     return {"workload": f"GPTQ of one Llama-7B layer: calibration X {tokens} tokens bf16 "
                         "(Student-t(4)/sqrt(4096), 1% channels x20) for K=4096 (3 inputs) and "
                         "11008 (down_proj); H=X^T X fp32; block 128; ratio 0.1",
-            "s_per_layer": round(s_layer, 4), "reps": reps,
+            "s_per_layer": s_layer, "reps": reps,
             "hessian": {"per_input": hres, "tflops": round(tf, 1),
                         "flops_per_layer": flops_all, "ms_per_layer": round(ms_all, 3),
                         "roofline": {"bound": "tensor", "achieved": round(tf, 1),
@@ -973,6 +985,23 @@ def main():
     if args.impl == "reference":
         if rank == 0:
             print(json.dumps(run_reference_arm(args, ws, rank, local)), flush=True)
+        return
+    if args.only is not None:
+        kw = {} if args.sub_steps is None else {"steps": args.sub_steps}
+        if args.only in ("mlp_pair", "single_4096", "qgemv", "gptq_layer", "hessian") and ws > 1:
+            raise SystemExit(f"--only {args.only} is a one-GPU record")
+        rec = {"mlp_pair": lambda: sub_mlp_pair(**kw),
+               "single_4096": lambda: sub_single_4096(**kw),
+               "gptq_layer": lambda: sub_gptq(tokens=args.tokens),
+               "hessian": lambda: sub_gptq(tokens=args.tokens, hessian_only=True),
+               "qgemv": sub_qgemv,
+               "rowsplit": lambda: sub_rowsplit(ws, rank),
+               "gptq_stream": lambda: sub_gptq_stream(ws, rank)}[args.only]()
+        if rank == 0:
+            print(json.dumps({args.only: rec}), flush=True)
+        if ws > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
         return
     line, shapes, wl = run_ours(args, ws, rank, local)
     if not args.no_sub:

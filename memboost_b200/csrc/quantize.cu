@@ -1875,13 +1875,16 @@ __device__ __forceinline__ void stats_body(const CUtensorMap& tmap, const QArgs&
   const int u_end = stats_start(bid + 1, ntiles, G);
   int u_ahead = u_begin;  // thread 0: the next tile to load
   int ct_ahead = u_begin / nrc, rc_ahead = u_begin - ct_ahead * nrc;
+  // W stays in L2 for encode's second read where it fits (encode's own
+  // loads and stores are evict-first)
+  const uint64_t pol = l2_evict_last();
   auto issue = [&](int s) {
     uint8_t* dst = dsm + (size_t)s * kTileBytes;
     fence_proxy_async_smem();
     mbar_arrive_expect_tx(&full[s], kTileBytes);
-    tma_load_2d(dst, &tmap, &full[s], ct_ahead * kTileCols, rc_ahead * kChunkRows);
-    tma_load_2d(dst + kBoxBytes, &tmap, &full[s], ct_ahead * kTileCols + 64,
-                rc_ahead * kChunkRows);
+    tma_load_2d_hint(dst, &tmap, &full[s], ct_ahead * kTileCols, rc_ahead * kChunkRows, pol);
+    tma_load_2d_hint(dst + kBoxBytes, &tmap, &full[s], ct_ahead * kTileCols + 64,
+                     rc_ahead * kChunkRows, pol);
     ++u_ahead;
     if (++rc_ahead == nrc) {
       rc_ahead = 0;
@@ -2864,27 +2867,32 @@ __device__ __noinline__ void fill_row_arrays(const QArgs& a, int bid, int G, uin
 
 // ---------------------------------------------------------------------------
 // encode, wide-tile form: tiles of 128 rows x 256 columns (16 groups), lane =
-// row, packed words written whole by TMA.  Warp w takes the 32 rows
+// row, packed words written whole by TMA.  Compute warp w takes the 32 rows
 // [32 (w & 3), 32 (w & 3) + 32) of the tile and four of its groups, the
 // quarter ((w >> 2) + i) & 3 on the CTA's i-th tile, so every warp carries
 // the same mix of 2-bit / 4-bit groups over any four tiles and no work queue
 // is needed.  A lane codes its row's four runs in registers (straight-line
 // code per 2/4-bit pattern of the quarter) and writes the words to a staging
 // tile laid out as the output rows (packed_2bit with the 64-byte swizzle,
-// packed_4bit with the 128-byte swizzle: conflict-free).  One thread then
-// stores the tile's 64 bytes of packed_2bit and 128 of packed_4bit per row
-// with two TMA stores.  The per-row arrays (scales_1st, zeros_1st, 2nd-order
-// codes: 16 or 32 bytes per row and tile, too narrow for efficient stores)
-// are written after the tiles, row by row (fill_row_arrays).  Tiles arrive
-// through a three-stage TMA ring; a stage is released per warp (a 16-arrival
-// mbarrier) and refilled as soon as the last warp is done with it.  Needs
-// ng % 16 == 0 and 16-byte aligned outputs; other shapes take encode_kernel.
-// CTA b takes the tiles [floor(b T / G), floor((b + 1) T / G)) of the T
-// tiles in column-major order.
+// packed_4bit with the 128-byte swizzle: conflict-free).  The per-row arrays
+// (scales_1st, zeros_1st, 2nd-order codes: 16 or 32 bytes per row and tile,
+// too narrow for efficient stores) are written after the tiles, row by row
+// (fill_row_arrays).
+//
+// Warp specialisation: the 16 compute warps never wait on one another inside
+// the tile loop.  A producer warp (warp 16, one thread) issues the TMA loads
+// of a three-stage tile ring and the two TMA stores of each staged tile, and
+// hands buffers over through mbarriers: full[s] (tile landed), empty[s]
+// (16 warps done reading it), stg_full (16 warps wrote the staging tile),
+// stg_empty (the stores have read it).  A warp codes tile i + 1 in registers
+// while tile i's stores drain.  Needs ng % 16 == 0 and 16-byte aligned
+// outputs; other shapes take encode_kernel.  CTA b takes the tiles
+// [floor(b T / G), floor((b + 1) T / G)) of the T tiles in column-major order.
 // ---------------------------------------------------------------------------
 constexpr int kE3Cols = 256;
 constexpr int kE3Groups = kE3Cols / kGroup1;        // 16
-constexpr int kE3Threads = 512;                     // 16 warps
+constexpr int kE3Compute = 512;                     // 16 compute warps
+constexpr int kE3Threads = kE3Compute + 32;         // + the producer warp
 constexpr int kE3Stages = 3;
 constexpr int kE3Tile = kChunkRows * kE3Cols * 2;   // 64 KB: four 64-column boxes
 constexpr int kE3P2 = kChunkRows * 64;              // 128 rows x 16 words
@@ -2900,13 +2908,17 @@ struct __align__(16) Enc3Ctx {
   uint8_t kind[kE3Groups];
   uint8_t gs[kE3Groups];
   uint8_t pr[kE3Groups];
-  int pat[4];  // per quarter: 4-bit mask of the 4-bit groups, or 16 (general path)
 };
 
 struct Enc3Maps {
   CUtensorMap p2, p4;  // packed_2bit (box 128 x 16, 64B swizzle), packed_4bit (128 x 32,
                        // 128B swizzle)
 };
+
+// Barrier among the compute warps only (named barrier 1).
+__device__ __forceinline__ void enc3_compute_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kE3Compute) : "memory");
+}
 
 // Codes of one row's four runs of a quarter whose groups are all regular and
 // 16 columns wide; bit q of P: group q of the quarter is 4-bit.  The run of
@@ -2940,24 +2952,74 @@ __device__ __forceinline__ void enc3_quarter(const uint8_t* __restrict__ rb, int
   }
 }
 
+// The producer: TMA loads into the ring, TMA stores of each staged tile.
+// One thread.  Returns false if a wait ran out (it then stops issuing).
+__device__ __forceinline__ bool enc3_producer(const CUtensorMap& tmap, const Enc3Maps& om,
+                                              uint8_t* dsm, uint64_t* full, uint64_t* empty,
+                                              uint64_t* stg_full, uint64_t* stg_empty,
+                                              int64_t S0, int64_t n, int nrc, int use_tma,
+                                              uint32_t& issued_mask) {
+  int l_ct = (int)(S0 / nrc), l_rc = (int)(S0 % nrc);  // the next tile to load
+  int s_ct = l_ct, s_rc = l_rc;                        // the next tile to store
+  const uint64_t pol_in = l2_evict_first(), pol_out = l2_evict_first();
+  auto issue = [&](int s) {
+    uint8_t* dst = dsm + (size_t)s * kE3Tile;
+    mbar_arrive_expect_tx(&full[s], kE3Tile);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      tma_load_2d_hint(dst + j * kBoxBytes, &tmap, &full[s], l_ct * kE3Cols + 64 * j,
+                       l_rc * kChunkRows, pol_in);
+    issued_mask |= 1u << s;
+    if (++l_rc == nrc) {
+      l_rc = 0;
+      ++l_ct;
+    }
+  };
+  if (use_tma)
+    for (int s = 0; s < kE3Stages && s < n; ++s) issue(s);
+  uint8_t* s2 = dsm + kE3OffOut;
+  uint8_t* s4 = s2 + kE3P2;
+  for (int64_t i = 0; i < n; ++i) {
+    // the warps release tile i's stage before they write its staging tile:
+    // the refill goes out first
+    if (use_tma && i + kE3Stages < n) {
+      const int s = (int)(i % kE3Stages);
+      if (!mbar_wait(&empty[s], (uint32_t)((i / kE3Stages) & 1))) return false;
+      fence_proxy_async_smem();
+      issue(s);
+    }
+    if (!mbar_wait(stg_full, (uint32_t)(i & 1))) return false;
+    const int x = s_ct * kE3Groups, y = s_rc * kChunkRows;
+    tma_store_2d_hint(&om.p2, s2, x, y, pol_out);
+    tma_store_2d_hint(&om.p4, s4, 2 * x, y, pol_out);
+    bulk_commit();
+    if (++s_rc == nrc) {
+      s_rc = 0;
+      ++s_ct;
+    }
+    bulk_wait_read<0>();  // the staging tile is read: the warps may refill it
+    mbar_arrive(stg_empty);
+  }
+  return true;
+}
+
 __device__ __forceinline__ void encode3_body(const CUtensorMap& tmap, const Enc3Maps& om,
                                              const QArgs& a, int use_tma, int bid, int G) {
   extern __shared__ uint8_t dsm_raw[];
   uint8_t* dsm = dsm_raw + ((1024u - (smem_u32(dsm_raw) & 1023u)) & 1023u);
-  __shared__ uint64_t full[kE3Stages], empty[kE3Stages];
-  __shared__ Enc3Ctx cx;
+  __shared__ uint64_t full[kE3Stages], empty[kE3Stages], stg_bar[2];
+  __shared__ Enc3Ctx cxs[2];  // contexts of consecutive column tiles
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t M = a.M;
   const int ng = a.ng, nrc = a.nrc;
   const int nct3 = ng / kE3Groups;
-  const int slab = warp & 3, qsel = warp >> 2;
-  const int rr = slab * 32 + lane;  // this lane's row in the tile
-  const int sw = rr & 7;            // its 128-byte swizzle phase
   if (tid == 0) {
     for (int s = 0; s < kE3Stages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kE3Threads / 32);
+      mbar_init(&empty[s], kE3Compute / 32);
     }
+    mbar_init(&stg_bar[0], kE3Compute / 32);  // stg_full: the 16 warps wrote the staging tile
+    mbar_init(&stg_bar[1], 1);                // stg_empty: the stores have read it
     fence_mbar_init();
   }
   grid_dependency_wait();  // the selection, parameters and 2nd-order table are final
@@ -2965,193 +3027,185 @@ __device__ __forceinline__ void encode3_body(const CUtensorMap& tmap, const Enc3
   const int64_t ntiles = (int64_t)nct3 * nrc;
   const int64_t S0 = ntiles * bid / G, S1 = ntiles * (bid + 1) / G;
   const int64_t ntile_cta = S1 - S0;
-  int a_ct = (int)(S0 / nrc), a_rc = (int)(S0 % nrc);  // thread 0: the next tile to load
-  auto issue = [&](int s) {
-    uint8_t* dst = dsm + (size_t)s * kE3Tile;
-    mbar_arrive_expect_tx(&full[s], kE3Tile);
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-      tma_load_2d(dst + j * kBoxBytes, &tmap, &full[s], a_ct * kE3Cols + 64 * j,
-                  a_rc * kChunkRows);
-    if (++a_rc == nrc) {
-      a_rc = 0;
-      ++a_ct;
-    }
-  };
   __syncthreads();  // barrier initialisation visible
-  if (tid == 0 && use_tma)
-    for (int s = 0; s < kE3Stages && s < ntile_cta; ++s) issue(s);
   bool failed = false;
-  uint32_t bad = 0;  // thread 0: stages whose wait ran out
-  int cur_ct = -1;
-  int ct = (int)(S0 / nrc), rc = (int)(S0 % nrc);
-  for (int64_t i = 0; i < ntile_cta; ++i) {
-    const int s = (int)(i % kE3Stages);
-    const uint32_t ph = (uint32_t)((i / kE3Stages) & 1);
-    if (ct != cur_ct) {
-      // a new column tile (every warp read the old context before the last
-      // tile's barriers)
-      const int64_t g = (int64_t)ct * kE3Groups + warp;  // warp w builds group w
-      uint32_t t = 0x7C007C00u;  // +inf: never reached
-      int kind = kEncKindNone, pr = 0, gs = 0;
-      if (g < ng) {
-        pr = a.ws.prec[g];
-        const GroupParams& p = a.ws.params[2 * g + pr];
-        if (lane < 15) t = (uint32_t)p.thresh[lane] * 0x00010001u;
-        kind = (p.flags & kFlagRegular) ? (pr ? kEncKind4 : kEncKind2) : kEncKindIrr;
-        gs = (int)min64(kGroup1, a.K - g * kGroup1);
-      }
-      if (lane < 16) (&cx.thr[warp][0].x)[lane] = t;
-      if (lane == 0) {
-        cx.kind[warp] = (uint8_t)kind;
-        cx.gs[warp] = (uint8_t)gs;
-        cx.pr[warp] = (uint8_t)pr;
-      }
-      __syncthreads();
-      if (tid < 4) {
-        int pat = 0;
-        for (int q = 0; q < 4; ++q) {
-          const int gi = 4 * tid + q;
-          const int kd = cx.kind[gi];
-          if (cx.gs[gi] != kGroup1 || (kd != kEncKind2 && kd != kEncKind4)) pat = 16;
-          if (pat < 16 && kd == kEncKind4) pat |= 1 << q;
+  uint32_t issued = 0;  // producer: stages that received a load
+  if (warp == kE3Compute / 32) {
+    if (lane == 0)
+      failed = !enc3_producer(tmap, om, dsm, full, empty, &stg_bar[0], &stg_bar[1], S0,
+                              ntile_cta, nrc, use_tma, issued);
+  } else {
+    const int slab = warp & 3, qsel = warp >> 2;
+    const int rr = slab * 32 + lane;  // this lane's row in the tile
+    const int sw = rr & 7;            // its 128-byte swizzle phase
+    uint8_t* s2 = dsm + kE3OffOut;
+    uint8_t* s4 = s2 + kE3P2;
+    int cur_ct = -1, pats = 0;  // pats: the 4 quarters' patterns, 5 bits each
+    const Enc3Ctx* cx = &cxs[0];
+    int ct = (int)(S0 / nrc), rc = (int)(S0 % nrc);
+    for (int64_t i = 0; i < ntile_cta; ++i) {
+      const int s = (int)(i % kE3Stages);
+      const uint32_t ph = (uint32_t)((i / kE3Stages) & 1);
+      if (ct != cur_ct) {
+        // a new column tile: its context goes to the other slot (before the
+        // last barrier every warp finished the tiles of the column tile
+        // that used it); warp w builds group w
+        Enc3Ctx* nx = &cxs[ct & 1];
+        const int64_t g = (int64_t)ct * kE3Groups + warp;
+        uint32_t t = 0x7C007C00u;  // +inf: never reached
+        int kind = kEncKindNone, pr = 0, gs = 0;
+        if (g < ng) {
+          pr = a.ws.prec[g];
+          const GroupParams& p = a.ws.params[2 * g + pr];
+          if (lane < 15) t = (uint32_t)p.thresh[lane] * 0x00010001u;
+          kind = (p.flags & kFlagRegular) ? (pr ? kEncKind4 : kEncKind2) : kEncKindIrr;
+          gs = (int)min64(kGroup1, a.K - g * kGroup1);
         }
-        cx.pat[tid] = pat;
+        if (lane < 16) (&nx->thr[warp][0].x)[lane] = t;
+        if (lane == 0) {
+          nx->kind[warp] = (uint8_t)kind;
+          nx->gs[warp] = (uint8_t)gs;
+          nx->pr[warp] = (uint8_t)pr;
+        }
+        enc3_compute_sync();
+        int pat = 0;
+        if (lane < 4) {
+          for (int q = 0; q < 4; ++q) {
+            const int gi = 4 * lane + q;
+            const int kd = nx->kind[gi];
+            if (nx->gs[gi] != kGroup1 || (kd != kEncKind2 && kd != kEncKind4)) pat = 16;
+            if (pat < 16 && kd == kEncKind4) pat |= 1 << q;
+          }
+        }
+        pats = 0;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) pats |= __shfl_sync(0xffffffffu, pat, q) << (5 * q);
+        cx = nx;
+        cur_ct = ct;
       }
-      __syncthreads();
-      cur_ct = ct;
-    }
-    uint8_t* buf = dsm + (size_t)s * kE3Tile;
-    if (use_tma) {
-      // after a wait ran out the thread stops waiting (outputs are flagged
-      // invalid), so a failed pipeline ends in bounded time
-      const bool ok = failed || mbar_wait(&full[s], ph);
-      if (!ok) {
-        failed = true;
-        if (tid == 0) bad |= 1u << s;
+      uint8_t* buf = dsm + (size_t)s * kE3Tile;
+      if (use_tma) {
+        // after a wait ran out the thread stops waiting (outputs are flagged
+        // invalid), so a failed pipeline ends in bounded time
+        if (!failed && !mbar_wait(&full[s], ph)) failed = true;
+      } else {
+        enc3_compute_sync();  // every compute warp is done with the stage
+        for (int j = 0; j < 2; ++j) {
+          uint8_t* dst = buf + j * kTileBytes;
+          for (int e = tid; e < kChunkRows * kTileCols; e += kE3Compute) {
+            const int r = e / kTileCols, c = e % kTileCols;
+            const int64_t gr = (int64_t)rc * kChunkRows + r,
+                          gc = (2 * (int64_t)ct + j) * kTileCols + c;
+            const uint16_t v = (gr < M && gc < a.K) ? __half_as_ushort(a.W[gr * a.K + gc]) : 0;
+            const int half = c >> 6, cc = c & 63;
+            *reinterpret_cast<uint16_t*>(dst + half * kBoxBytes + r * 128 +
+                                         (((cc >> 3) ^ (r & 7)) << 4) + (cc & 7) * 2) = v;
+          }
+        }
+        enc3_compute_sync();
       }
-    } else {
-      __syncthreads();  // every warp is done with the stage
-      for (int j = 0; j < 2; ++j)
-        tile_fill_at(a.W, M, a.K, buf + j * kTileBytes, rc, 2 * (int64_t)ct + j, 0);
-      __syncthreads();
-    }
-    const int64_t row0 = (int64_t)rc * kChunkRows;
-    const int qq = (qsel + (int)(i & 3)) & 3;  // this warp's quarter of the tile
-    // codes of this lane's row, groups 4 qq .. 4 qq + 3 (box qq of the tile)
-    const uint8_t* rb = buf + qq * kBoxBytes + rr * 128;
-    uint32_t w2[4], w4[8];
-    uint32_t cnt = 0;
-    const uint4(*thr)[4] = &cx.thr[4 * qq];
-    switch (cx.pat[qq]) {
+      const int64_t row0 = (int64_t)rc * kChunkRows;
+      const int qq = (qsel + (int)(i & 3)) & 3;  // this warp's quarter of the tile
+      // codes of this lane's row, groups 4 qq .. 4 qq + 3 (box qq of the tile)
+      const uint8_t* rb = buf + qq * kBoxBytes + rr * 128;
+      uint32_t w2[4], w4[8];
+      uint32_t cnt = 0;
+      const uint4(*thr)[4] = &cx->thr[4 * qq];
+      switch ((pats >> (5 * qq)) & 31) {
 #define MB_ENC3_CASE(P) \
   case P:               \
     enc3_quarter<P>(rb, sw, thr, w2, w4); \
     break;
-      MB_ENC3_CASE(0) MB_ENC3_CASE(1) MB_ENC3_CASE(2) MB_ENC3_CASE(3)
-      MB_ENC3_CASE(4) MB_ENC3_CASE(5) MB_ENC3_CASE(6) MB_ENC3_CASE(7)
-      MB_ENC3_CASE(8) MB_ENC3_CASE(9) MB_ENC3_CASE(10) MB_ENC3_CASE(11)
-      MB_ENC3_CASE(12) MB_ENC3_CASE(13) MB_ENC3_CASE(14) MB_ENC3_CASE(15)
+        MB_ENC3_CASE(0) MB_ENC3_CASE(1) MB_ENC3_CASE(2) MB_ENC3_CASE(3)
+        MB_ENC3_CASE(4) MB_ENC3_CASE(5) MB_ENC3_CASE(6) MB_ENC3_CASE(7)
+        MB_ENC3_CASE(8) MB_ENC3_CASE(9) MB_ENC3_CASE(10) MB_ENC3_CASE(11)
+        MB_ENC3_CASE(12) MB_ENC3_CASE(13) MB_ENC3_CASE(14) MB_ENC3_CASE(15)
 #undef MB_ENC3_CASE
-      default:
+        default:
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int gi = 4 * qq + q;
-          const int kind = cx.kind[gi];
-          const int lo_off = ((2 * q) ^ sw) << 4, hi_off = ((2 * q + 1) ^ sw) << 4;
-          w2[q] = 0u;
-          w4[2 * q] = w4[2 * q + 1] = 0u;
-          if (kind == kEncKind2) {
-            Row16 v;
-            v.lo = *reinterpret_cast<const uint4*>(rb + lo_off);
-            v.hi = *reinterpret_cast<const uint4*>(rb + hi_off);
-            const uint4 T = cx.thr[gi][0];
-            uint32_t w = enc2_run(v, T.x, T.y, T.z);
-            const int gs = cx.gs[gi];
-            if (gs < kGroup1) w &= (1u << (2 * gs)) - 1u;  // columns past K hold code 0
-            w2[q] = w;
-          } else if (kind == kEncKind4) {
-            Row16 v;
-            v.lo = *reinterpret_cast<const uint4*>(rb + lo_off);
-            v.hi = *reinterpret_cast<const uint4*>(rb + hi_off);
-            uint32_t t[16];
+          for (int q = 0; q < 4; ++q) {
+            const int gi = 4 * qq + q;
+            const int kind = cx->kind[gi];
+            const int lo_off = ((2 * q) ^ sw) << 4, hi_off = ((2 * q + 1) ^ sw) << 4;
+            w2[q] = 0u;
+            w4[2 * q] = w4[2 * q + 1] = 0u;
+            if (kind == kEncKind2) {
+              Row16 v;
+              v.lo = *reinterpret_cast<const uint4*>(rb + lo_off);
+              v.hi = *reinterpret_cast<const uint4*>(rb + hi_off);
+              const uint4 T = cx->thr[gi][0];
+              uint32_t w = enc2_run(v, T.x, T.y, T.z);
+              const int gs = cx->gs[gi];
+              if (gs < kGroup1) w &= (1u << (2 * gs)) - 1u;  // columns past K hold code 0
+              w2[q] = w;
+            } else if (kind == kEncKind4) {
+              Row16 v;
+              v.lo = *reinterpret_cast<const uint4*>(rb + lo_off);
+              v.hi = *reinterpret_cast<const uint4*>(rb + hi_off);
+              uint32_t t[16];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const uint4 T = cx.thr[gi][k];
-              t[4 * k] = T.x;
-              t[4 * k + 1] = T.y;
-              t[4 * k + 2] = T.z;
-              t[4 * k + 3] = T.w;
+              for (int k = 0; k < 4; ++k) {
+                const uint4 T = cx->thr[gi][k];
+                t[4 * k] = T.x;
+                t[4 * k + 1] = T.y;
+                t[4 * k + 2] = T.z;
+                t[4 * k + 3] = T.w;
+              }
+              uint32_t x, y;
+              enc4_run(v, t, x, y);
+              const int gs = cx->gs[gi];
+              if (gs < kGroup1) {
+                x &= gs >= 8 ? 0xFFFFFFFFu : ((1u << (4 * gs)) - 1u);
+                y &= gs <= 8 ? 0u : ((1u << (4 * (gs - 8))) - 1u);
+              }
+              w4[2 * q] = x;
+              w4[2 * q + 1] = y;
+            } else if (kind == kEncKindIrr) {
+              const int64_t g = (int64_t)ct * kE3Groups + gi;
+              const GroupParams& gp = a.ws.params[2 * g + cx->pr[gi]];
+              const uint3 c = enc_irregular(gp, rb, lo_off, hi_off, cx->gs[gi]);
+              if (cx->pr[gi]) {
+                w4[2 * q] = c.x;
+                w4[2 * q + 1] = c.y;
+              } else {
+                w2[q] = c.x;
+              }
+              cnt += c.z;
             }
-            uint32_t x, y;
-            enc4_run(v, t, x, y);
-            const int gs = cx.gs[gi];
-            if (gs < kGroup1) {
-              x &= gs >= 8 ? 0xFFFFFFFFu : ((1u << (4 * gs)) - 1u);
-              y &= gs <= 8 ? 0u : ((1u << (4 * (gs - 8))) - 1u);
-            }
-            w4[2 * q] = x;
-            w4[2 * q + 1] = y;
-          } else if (kind == kEncKindIrr) {
-            const int64_t g = (int64_t)ct * kE3Groups + gi;
-            const GroupParams& gp = a.ws.params[2 * g + cx.pr[gi]];
-            const uint3 c = enc_irregular(gp, rb, lo_off, hi_off, cx.gs[gi]);
-            if (cx.pr[gi]) {
-              w4[2 * q] = c.x;
-              w4[2 * q + 1] = c.y;
-            } else {
-              w2[q] = c.x;
-            }
-            cnt += c.z;
           }
-        }
-    }
-    // the tile's stage is free once every warp has read its part; thread 0
-    // refills it as soon as the last warp is done
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
-    if (tid == 0 && use_tma && i + kE3Stages < ntile_cta && !failed) {
-      if (mbar_wait(&empty[s], ph)) {
-        fence_proxy_async_smem();
-        issue(s);
-      } else {
-        failed = true;
       }
-    }
-    const int64_t row = row0 + rr;
-    if (cnt && row < M) atomicAdd(a.ws.row_counts + row, (int)cnt);
-    // the staging buffer: the previous tile's stores have read it
-    uint8_t* s2 = dsm + kE3OffOut;
-    uint8_t* s4 = s2 + kE3P2;
-    if (tid == 0) bulk_wait_read<0>();
-    __syncthreads();
-    *reinterpret_cast<uint4*>(s2 + rr * 64 + ((qq ^ ((rr >> 1) & 3)) << 4)) =
-        make_uint4(w2[0], w2[1], w2[2], w2[3]);
-    *reinterpret_cast<uint4*>(s4 + rr * 128 + (((2 * qq) ^ sw) << 4)) =
-        make_uint4(w4[0], w4[1], w4[2], w4[3]);
-    *reinterpret_cast<uint4*>(s4 + rr * 128 + (((2 * qq + 1) ^ sw) << 4)) =
-        make_uint4(w4[4], w4[5], w4[6], w4[7]);
-    fence_proxy_async_smem();
-    __syncthreads();
-    if (tid == 0) {
-      const int x = ct * kE3Groups, y = (int)row0;
-      tma_store_2d(&om.p2, s2, x, y);
-      tma_store_2d(&om.p4, s4, 2 * x, y);
-      bulk_commit();
-    }
-    if (++rc == nrc) {
-      rc = 0;
-      ++ct;
+      // this warp is done reading the stage
+      __syncwarp();
+      if (lane == 0 && use_tma) mbar_arrive(&empty[s]);
+      const int64_t row = row0 + rr;
+      if (cnt && row < M) atomicAdd(a.ws.row_counts + row, (int)cnt);
+      // the staging tile: the previous tile's stores have read it
+      if (i > 0 && !failed && !mbar_wait(&stg_bar[1], (uint32_t)((i - 1) & 1))) failed = true;
+      *reinterpret_cast<uint4*>(s2 + rr * 64 + ((qq ^ ((rr >> 1) & 3)) << 4)) =
+          make_uint4(w2[0], w2[1], w2[2], w2[3]);
+      *reinterpret_cast<uint4*>(s4 + rr * 128 + (((2 * qq) ^ sw) << 4)) =
+          make_uint4(w4[0], w4[1], w4[2], w4[3]);
+      *reinterpret_cast<uint4*>(s4 + rr * 128 + (((2 * qq + 1) ^ sw) << 4)) =
+          make_uint4(w4[4], w4[5], w4[6], w4[7]);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&stg_bar[0]);
+      if (++rc == nrc) {
+        rc = 0;
+        ++ct;
+      }
     }
   }
   grid_launch_dependents();
-  if (tid == 0) bulk_wait<0>();  // the CTA's stores are complete
+  if (warp == kE3Compute / 32 && lane == 0) bulk_wait<0>();  // the CTA's stores are complete
   failed = __syncthreads_or(failed) != 0;
-  if (tid == 0) {
-    if (failed) atomicOr(&a.ws.hdr->status, kStatusTimeout);
+  if (tid == kE3Compute && failed) {
+    atomicOr(&a.ws.hdr->status, kStatusTimeout);
+    // loads still in flight land before the shared memory is reused
     for (int s = 0; s < kE3Stages; ++s)
-      if (bad & (1u << s)) (void)mbar_wait(&full[s], 0u), (void)mbar_wait(&full[s], 1u);
+      if (issued & (1u << s)) (void)mbar_wait(&full[s], 0u), (void)mbar_wait(&full[s], 1u);
   }
+  __syncthreads();
   // the tiles and the staging buffer are free: the per-row arrays
   fill_row_arrays(a, bid, G, dsm, (size_t)(kE3Smem - 1024));
   post_rowptr_scan<kE3Threads>(a, G, reinterpret_cast<long long*>(dsm));
