@@ -17,8 +17,9 @@ ranks.  Rank 0 prints one JSON line.
              per 8 matrices, 8 graph branches); step k + 1 is enqueued
              before step k's outlier counts are read
   e2e        the public memboost_b200.quantize() call per matrix with host
-             buffers: pinned H2D copy of the weights and hessian, quantize,
-             D2H of every output tensor, inside the timed region
+             buffers: pinned H2D copies of the weights and hessians (all
+             enqueued first on a copy stream), quantize, D2H of every output
+             tensor, inside the timed region
   roofline   algorithmic bytes of the step's quantize calls (3.0 B per weight
              plus hessian, 2nd-order, CSR and precision bytes) / device time
              per step, against MEASURED_PEAKS.json
@@ -59,11 +60,13 @@ WORKLOAD = ("llama2_7b model: 32 layers x {q,k,v,o 4096x4096, gate/up 11008x4096
             "lognormal(0,1.5) per matrix; ratio_4bit 0.1; 16-col groups; matrices split over "
             "ranks by size (LPT)")
 
-# DRAM read + write per quantize call of a 4096x11008 / 11008x4096 matrix
-# (ncu, one pipelined step of the MLP pair, L2 kept between kernels), as
-# summarised in profiles/quantize_mlp7b_launches.md: the measured traffic the
-# roofline's algorithmic bytes are compared with.
-TRAFFIC_PER_CALL_MLP7B = 197_200_000
+# Measured DRAM read + write (ncu, L2 kept between kernels) that the
+# roofline's algorithmic bytes are compared with: one step of the whole
+# model on one GPU (19.44 GB algorithmic), and one quantize call of a
+# 4096x11008 / 11008x4096 matrix in the pipelined MLP-pair record (135.4 MB
+# algorithmic).
+TRAFFIC_PER_STEP_MODEL = 26_160_000_000
+TRAFFIC_PER_CALL_MLP7B = 169_700_000
 
 
 def parse():
@@ -87,6 +90,8 @@ def parse():
                    help="calibration tokens of the gptq_layer / hessian records")
     p.add_argument("--sub-steps", type=int, default=None,
                    help="timed steps of the mlp_pair / single_4096 records")
+    p.add_argument("--pair-sets", type=int, default=2,
+                   help="mlp_pair: step sets in flight (a stream and a plan per matrix each)")
     return p.parse_args()
 
 
@@ -434,11 +439,10 @@ def run_ours(args, ws, rank, local):
         "roofline": {"bound": "hbm", "achieved": round(achieved / ws, 1), "peak": hbm,
                      "unit": "GB/s", "frac": round(achieved / ws / hbm, 4),
                      "peak_kind": peak_kind, "of": f"{peak_kind} hbm_gbs per GPU",
-                     "traffic": TRAFFIC_PER_CALL_MLP7B,
-                     "traffic_what": "DRAM read+write of one 4096x11008 quantize call (ncu, "
-                                     "profiles/quantize_mlp7b_launches.md) against "
-                                     f"{algorithmic_bytes(4096, 11008, 0, True)} algorithmic "
-                                     "bytes",
+                     "traffic": int(TRAFFIC_PER_STEP_MODEL * fp16_bytes / total_fp16),
+                     "traffic_what": "DRAM read+write per step of this GPU's share (ncu "
+                                     "capture of one whole-model step on one GPU, L2 kept "
+                                     "between kernels, scaled by the share's bytes)",
                      "kernel": "the quantize calls of a step (stats, combine, tables, encode, "
                                "extract per launch set of matrices, chained with PDL): "
                                "algorithmic bytes of the whole job per GPU / device time per "
@@ -459,8 +463,11 @@ def run_ours(args, ws, rank, local):
 def run_e2e(args, ws, dev, batch, fp16_bytes, total_fp16):
     """memboost_b200.quantize() per matrix of this rank's share with host
     buffers: upload (pinned), quantize, download of every output into pinned
-    buffers, all inside the timed region; two streams alternate so one
-    matrix's download overlaps the next one's upload."""
+    buffers, all inside the timed region.  The uploads of the whole share
+    are enqueued first on a copy stream (one event per matrix), so they run
+    back to back while quantize() -- which waits for its matrix's kernels to
+    size the CSR arrays -- and the downloads (two alternating streams)
+    follow behind them."""
     import torch
 
     import memboost_b200 as mb
@@ -468,18 +475,30 @@ def run_e2e(args, ws, dev, batch, fp16_bytes, total_fp16):
     hh = [h.cpu().pin_memory() if h is not None else None for h in batch.hess]
     h2d = sum(t.numel() * t.element_size() for t in hw) + \
         sum(t.numel() * t.element_size() for t in hh if t is not None)
+    wd = [torch.empty_like(w, device=dev) for w in hw]
+    hd = [torch.empty_like(h, device=dev) if h is not None else None for h in hh]
+    up = torch.cuda.Stream(dev)
     streams = [torch.cuda.Stream(dev) for _ in range(2)]
+    ev_up = [torch.cuda.Event() for _ in hw]
+    ev_used = [torch.cuda.Event() for _ in hw]
     host_out = [dict() for _ in hw]
     d2h = {"b": 0}
 
     def step():
         nb = 0
-        for i, (w, h) in enumerate(zip(hw, hh)):
+        with torch.cuda.stream(up):
+            for i, (w, h) in enumerate(zip(hw, hh)):
+                up.wait_event(ev_used[i])  # the previous step's quantize read the buffer
+                wd[i].copy_(w, non_blocking=True)
+                if h is not None:
+                    hd[i].copy_(h, non_blocking=True)
+                ev_up[i].record(up)
+        for i in range(len(hw)):
             st = streams[i % 2]
+            st.wait_event(ev_up[i])
             with torch.cuda.stream(st):
-                wd = w.to(dev, non_blocking=True)
-                hd = h.to(dev, non_blocking=True) if h is not None else None
-                qt = mb.quantize(wd, batch.ratios[i], hd)
+                qt = mb.quantize(wd[i], batch.ratios[i], hd[i])
+                ev_used[i].record(st)
                 for k, v in qt.state_dict().items():
                     if not (isinstance(v, torch.Tensor) and v.is_cuda):
                         continue
@@ -489,7 +508,6 @@ def run_e2e(args, ws, dev, batch, fp16_bytes, total_fp16):
                         host_out[i][k] = dst
                     dst.copy_(v, non_blocking=True)
                     nb += v.numel() * v.element_size()
-                wd.record_stream(st)
         d2h["b"] = nb
 
     step()
@@ -499,11 +517,11 @@ def run_e2e(args, ws, dev, batch, fp16_bytes, total_fp16):
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
-    for st in streams:
+    for st in streams + [up]:
         st.wait_event(e0)
     for _ in range(args.e2e_steps):
         step()
-    for st in streams:
+    for st in streams + [up]:
         torch.cuda.current_stream(dev).wait_stream(st)
     e1.record()
     torch.cuda.synchronize()
@@ -512,18 +530,19 @@ def run_e2e(args, ws, dev, batch, fp16_bytes, total_fp16):
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h["b"],
             "per": "rank 0 (every rank moves its own share)", "steps": args.e2e_steps,
             "ms_per_step": round(ems / args.e2e_steps, 3),
-            "path": "memboost_b200.quantize() per matrix (C ABI), pinned host buffers, "
-                    "2 alternating streams"}
+            "path": "memboost_b200.quantize() per matrix (C ABI), pinned host buffers; uploads "
+                    "on a copy stream ahead of the quantize calls, downloads on 2 alternating "
+                    "streams"}
 
 
 # ---------------------------------------------------------------------------
 # one-GPU sub-records
 # ---------------------------------------------------------------------------
 
-def sub_mlp_pair(steps=1000, warmup=5):
+def sub_mlp_pair(steps=1000, warmup=5, sets=2):
     """Config 2: the Llama-7B MLP pair, QuantizePlan per matrix, every plan on
-    a stream of its own (two matrices x two step sets), step k + 1 enqueued
-    before step k is finished."""
+    a stream of its own (two matrices x `sets` step sets), step k + sets - 1
+    enqueued before step k is finished."""
     import torch
 
     from memboost_b200 import _C
@@ -532,7 +551,7 @@ def sub_mlp_pair(steps=1000, warmup=5):
     cases = wl.mlp_7b()
     W = [c.weights.to(dev) for c in cases]
     H = [c.hessian_diag.to(dev) for c in cases]
-    stream_sets = [[torch.cuda.Stream(dev) for _ in W] for _ in range(2)]
+    stream_sets = [[torch.cuda.Stream(dev) for _ in W] for _ in range(sets)]
     streams = [st for ss in stream_sets for st in ss]
     plan_sets = [[_C.QuantizePlan(*w.shape, dev, stream=st) for w, st in zip(W, ss)]
                  for ss in stream_sets]
@@ -540,12 +559,13 @@ def sub_mlp_pair(steps=1000, warmup=5):
 
     def run_steps(n):
         for k in range(n):
-            for p, w, h, c in zip(plan_sets[k % 2], W, H, cases):
+            for p, w, h, c in zip(plan_sets[k % sets], W, H, cases):
                 p.launch(w, c.ratio_4bit, h)
-            if k > 0:
+            if k >= sets - 1:
                 nnz_seen.append([int(r[8].numel()) for r in
-                                 (p.finish() for p in plan_sets[(k - 1) % 2])])
-        nnz_seen.append([int(r[8].numel()) for r in (p.finish() for p in plan_sets[(n - 1) % 2])])
+                                 (p.finish() for p in plan_sets[(k - sets + 1) % sets])])
+        for k in range(max(0, n - sets + 1), n):
+            nnz_seen.append([int(r[8].numel()) for r in (p.finish() for p in plan_sets[k % sets])])
 
     run_steps(warmup)
     torch.cuda.synchronize()
@@ -572,7 +592,7 @@ def sub_mlp_pair(steps=1000, warmup=5):
                          "frac": round(ach / pk["hbm_gbs"], 4), "of": f"{kind} hbm_gbs",
                          "traffic": TRAFFIC_PER_CALL_MLP7B,
                          "algorithmic_bytes_per_call": alg},
-            "gpu_launches": 3 * len(W) * steps}
+            "gpu_launches": 5 * len(W) * steps}
 
 
 def sub_single_4096(steps=200, warmup=5):
@@ -590,23 +610,27 @@ def sub_single_4096(steps=200, warmup=5):
     M, K = batch.shapes[0]
     out = torch.empty((M, K), dtype=torch.float16, device=dev)
 
+    o = batch.out[0]
+
     def step():
+        # quantize (graph replay), then dequantize of its outputs on the same
+        # stream; the outlier count is read once after the timed steps
         batch.launch()
-        r = batch.finish()[0]
-        _C.dequantize(r[0], r[1], r[2], r[3], r[7], M, K, out)
-        return r
+        _C.dequantize(o[0], o[1], o[2], o[3], o[7], M, K, out)
 
     for _ in range(warmup):
-        r = step()
+        step()
+    r = batch.finish()[0]
     torch.cuda.synchronize()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record()
     for _ in range(steps):
-        r = step()
+        step()
     t1.record()
     torch.cuda.synchronize()
     ms = t0.elapsed_time(t1) / steps
+    r = batch.finish()[0]
     nnz = int(r[8].numel())
     # dequantize alone, inputs rotated over 8 copies (larger than L2 together)
     copies = [[t.clone() for t in (r[0], r[1], r[2], r[3], r[7])] for _ in range(8)]
@@ -634,6 +658,7 @@ def sub_single_4096(steps=200, warmup=5):
             "value": round(2 * M * K / (ms / 1e3) / 1e9, 2), "unit": UNIT,
             "ms_per_step": round(ms, 4), "nnz": nnz, "steps": steps,
             "quantize_plus_dequantize_bytes": qb + db,
+            "l2": "the same 32 MB matrix every step: largely L2-resident (no roofline claim)",
             "dequantize": {"ms": round(dms, 4),
                            "value": round(2 * M * K / (dms / 1e3) / 1e9, 1), "unit": UNIT,
                            "roofline": {"bound": "hbm", "algorithmic_bytes": db,
@@ -990,7 +1015,7 @@ def main():
         kw = {} if args.sub_steps is None else {"steps": args.sub_steps}
         if args.only in ("mlp_pair", "single_4096", "qgemv", "gptq_layer", "hessian") and ws > 1:
             raise SystemExit(f"--only {args.only} is a one-GPU record")
-        rec = {"mlp_pair": lambda: sub_mlp_pair(**kw),
+        rec = {"mlp_pair": lambda: sub_mlp_pair(sets=args.pair_sets, **kw),
                "single_4096": lambda: sub_single_4096(**kw),
                "gptq_layer": lambda: sub_gptq(tokens=args.tokens),
                "hessian": lambda: sub_gptq(tokens=args.tokens, hessian_only=True),
