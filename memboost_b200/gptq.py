@@ -169,24 +169,97 @@ LAYER_INPUTS = {
 }
 
 
+class InverseWorkers:
+    """The layer's inverses (gptq_inverse), each in a host thread and on a
+    CUDA stream of its own.  The Cholesky factorisations are the longest
+    part of a layer (the 11008 x 11008 one ~105 ms of a ~200 ms layer) and
+    wait on the host for their error checks (with the interpreter lock
+    released), so started as soon as their Hessian is final they overlap one
+    another and the caller's Hessians, GPTQ updates and quantize calls on its
+    own stream.  The results are those of gptq_inverse: the same torch
+    calls."""
+
+    _linalg_ready = set()  # devices whose torch.linalg set-up ran
+    _streams = {}          # device -> the workers' streams, kept across layers
+
+    def __init__(self, device, workers: int = 4):
+        from concurrent.futures import ThreadPoolExecutor
+        self.device = torch.device(device)
+        if self.device not in InverseWorkers._linalg_ready:
+            # torch.linalg initialises its CUDA back end lazily on the first
+            # call, which must not happen in several threads at once
+            e = torch.eye(2, device=self.device)
+            torch.linalg.cholesky(torch.cholesky_inverse(torch.linalg.cholesky(e)), upper=True)
+            InverseWorkers._linalg_ready.add(self.device)
+        # the same streams every layer: the caching allocator and the solver
+        # keep their blocks and workspaces per stream
+        pool = InverseWorkers._streams.setdefault(self.device, [])
+        while len(pool) < workers:
+            pool.append(torch.cuda.Stream(self.device))
+        self.streams = pool[:workers]
+        self.pool = ThreadPoolExecutor(max_workers=workers)
+        self.futures = {}
+
+    def start(self, key, H: torch.Tensor) -> None:
+        """Begin the inverse of H (complete in stream order on the current
+        stream)."""
+        ready = torch.cuda.Event()
+        ready.record(torch.cuda.current_stream(self.device))
+        s = self.streams[len(self.futures) % len(self.streams)]
+        self.futures[key] = self.pool.submit(self._run, H, ready, s)
+
+    def _run(self, H: torch.Tensor, ready, s):
+        with torch.cuda.device(self.device):
+            s.wait_event(ready)
+            with torch.cuda.stream(s):
+                H.record_stream(s)
+                h_diag, hinv_cho = gptq_inverse(H)
+                done = torch.cuda.Event()
+                done.record(s)
+        return h_diag, hinv_cho, done
+
+    def take(self, key):
+        """(h_diag, Hinv_cho) of key, ordered before later work on the
+        current stream."""
+        h_diag, hinv_cho, done = self.futures[key].result()
+        cur = torch.cuda.current_stream(self.device)
+        cur.wait_event(done)
+        h_diag.record_stream(cur)
+        hinv_cho.record_stream(cur)
+        return h_diag, hinv_cho
+
+    def close(self) -> None:
+        self.pool.shutdown(wait=True)
+
+
 def quantize_layer(weights: dict, inputs: dict, ratio_4bit: float = 0.1,
                    blocksize: int = 128) -> dict:
     """One transformer layer's GPTQ (llama.py:530-617): the four Hessians
     from the calibration inputs (``inputs``: "attn", "o", "mlp", "down" ->
     [tokens, K] fp16/bf16), their inverses, then GPTQ + quantize of the seven
     fp32 weight matrices (``weights``: names of ``LAYER_INPUTS``).  Returns
-    name -> QuantizedTensor."""
-    inv = {}
-    for key, x in inputs.items():
-        acc = HessianAccumulator(x.shape[-1], x.device)
-        acc.add(x)
-        inv[key] = gptq_inverse(acc.finalize())
-    out = {}
-    for name, W in weights.items():
-        h_diag, hinv_cho = inv[LAYER_INPUTS[name]]
-        out[name] = make_quantized_linear(W, h_diag, hinv_cho, ratio_4bit,
-                                          blocksize=blocksize).q_weight
-    return out
+    name -> QuantizedTensor.
+
+    The largest Hessian goes first and every inverse runs beside the rest
+    (InverseWorkers); the weights then take their turn in the order their
+    inverses come ready (the small Hessians' first).  The results do not
+    depend on the order."""
+    dev = next(iter(inputs.values())).device
+    workers = InverseWorkers(dev, workers=len(inputs))
+    try:
+        for key in sorted(inputs, key=lambda k: -inputs[k].shape[-1]):
+            x = inputs[key]
+            acc = HessianAccumulator(x.shape[-1], x.device)
+            acc.add(x)
+            workers.start(key, acc.finalize())
+        out = {}
+        for name in sorted(weights, key=lambda n: inputs[LAYER_INPUTS[n]].shape[-1]):
+            h_diag, hinv_cho = workers.take(LAYER_INPUTS[name])
+            out[name] = make_quantized_linear(weights[name], h_diag, hinv_cho, ratio_4bit,
+                                              blocksize=blocksize).q_weight
+    finally:
+        workers.close()
+    return {name: out[name] for name in weights}
 
 
 def even_rows(M: int, world: int) -> list[tuple[int, int]]:

@@ -164,13 +164,19 @@ def quantize_llama_synthetic(cfg: LlamaConfig, n_samples: int = 128, seq_len: in
                 block_forward(cfg, hidden[s0:s0 + batch], lin, cos, sin,
                               capture={k: a.add for k, a in accs.items()})
         if comm is None:
-            inv = {}
-            for key, acc in accs.items():
-                inv[key] = gptq.gptq_inverse(acc.finalize())
-            q = {}
-            for name, W in w.items():
-                h_diag, hc = inv[gptq.LAYER_INPUTS[name]]
-                q[name] = gptq.make_quantized_linear(W, h_diag, hc, cfg.ratio_4bit).q_weight
+            # the inverses beside the GPTQ updates (largest Hessian first)
+            workers = gptq.InverseWorkers(device, workers=len(accs))
+            try:
+                for key in sorted(accs, key=lambda k: -accs[k].K):
+                    workers.start(key, accs[key].finalize())
+                q = {}
+                for name in sorted(w, key=lambda n: accs[gptq.LAYER_INPUTS[n]].K):
+                    h_diag, hc = workers.take(gptq.LAYER_INPUTS[name])
+                    q[name] = gptq.make_quantized_linear(w[name], h_diag, hc,
+                                                         cfg.ratio_4bit).q_weight
+            finally:
+                workers.close()
+            q = {name: q[name] for name in w}
         else:
             # the accumulated sums over this rank's tokens, reduced inside
             tokens = torch.tensor([float(accs["attn"].tokens)], dtype=torch.float64,

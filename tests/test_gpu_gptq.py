@@ -271,3 +271,28 @@ def test_quantize_layer_full_shapes(gq):
         M, K = weights[name].shape
         assert (qt.M, qt.K) == (M, K)
         assert int(qt.group_precision.sum()) == int(0.1 * (K // 16))
+
+
+def test_quantize_layer_overlapped_equals_sequential(gq):
+    """quantize_layer runs the inverses in worker threads beside the GPTQ
+    updates; its tensors equal the plain sequence (Hessian, gptq_inverse,
+    make_quantized_linear, one matrix after another) bit for bit."""
+    from memboost_b200 import workloads
+    weights, inputs = workloads.gptq_layer(tokens=4096, device="cuda", scale=8)
+    out = gq.quantize_layer(weights, inputs, ratio_4bit=0.1)
+    inv = {}
+    for key, x in inputs.items():
+        acc = gq.HessianAccumulator(x.shape[-1], x.device)
+        acc.add(x)
+        inv[key] = gq.gptq_inverse(acc.finalize())
+    for name, W in weights.items():
+        h_diag, hc = inv[gq.LAYER_INPUTS[name]]
+        want = gq.make_quantized_linear(W, h_diag, hc, 0.1).q_weight
+        got = out[name]
+        for f in ("packed_2bit", "packed_4bit", "scales_1st", "zeros_1st", "scales_2nd",
+                  "zeros_2nd", "scales_1st_quant", "group_precision", "outlier_values",
+                  "outlier_col_indices", "outlier_row_ptrs"):
+            a, b = getattr(got, f), getattr(want, f)
+            if a.dtype == torch.float16:
+                a, b = a.view(torch.int16), b.view(torch.int16)
+            assert torch.equal(a, b), (name, f)
