@@ -90,7 +90,7 @@ def parse():
                    help="calibration tokens of the gptq_layer / hessian records")
     p.add_argument("--sub-steps", type=int, default=None,
                    help="timed steps of the mlp_pair / single_4096 records")
-    p.add_argument("--pair-sets", type=int, default=2,
+    p.add_argument("--pair-sets", type=int, default=4,
                    help="mlp_pair: step sets in flight (a stream and a plan per matrix each)")
     return p.parse_args()
 
@@ -539,7 +539,7 @@ def run_e2e(args, ws, dev, batch, fp16_bytes, total_fp16):
 # one-GPU sub-records
 # ---------------------------------------------------------------------------
 
-def sub_mlp_pair(steps=1000, warmup=5, sets=2):
+def sub_mlp_pair(steps=1000, warmup=5, sets=4):
     """Config 2: the Llama-7B MLP pair, QuantizePlan per matrix, every plan on
     a stream of its own (two matrices x `sets` step sets), step k + sets - 1
     enqueued before step k is finished."""

@@ -1759,20 +1759,6 @@ __device__ __forceinline__ void tile_fill(const __half* W, int64_t M, int64_t K,
   }
 }
 
-// The same layout for the 128-column tile ct of row chunk rc (columns or rows
-// outside the matrix read as `fill`).
-__device__ __forceinline__ void tile_fill_at(const __half* W, int64_t M, int64_t K, uint8_t* dst,
-                                             int64_t rc, int64_t ct, uint16_t fill) {
-  for (int e = threadIdx.x; e < kChunkRows * kTileCols; e += blockDim.x) {
-    const int r = e / kTileCols, c = e % kTileCols;
-    const int64_t gr = rc * kChunkRows + r, gc = ct * kTileCols + c;
-    const uint16_t v = (gr < M && gc < K) ? __half_as_ushort(W[gr * K + gc]) : fill;
-    const int half = c >> 6, cc = c & 63;
-    *reinterpret_cast<uint16_t*>(dst + half * kBoxBytes + r * 128 +
-                                 (((cc >> 3) ^ (r & 7)) << 4) + (cc & 7) * 2) = v;
-  }
-}
-
 // Tile u of the stats pass is (column tile u / nrc, row chunk u % nrc); stats
 // CTA b takes the tiles [U_b, U_b+1), U_b = floor(b * ntiles / G), G <= ntiles
 // (so no range is empty).  A CTA's tiles of one column tile form a segment,
