@@ -101,6 +101,7 @@ def load_workloads():
     spec = importlib.util.spec_from_file_location(
         "mb_workloads", os.path.join(ROOT, "memboost_b200", "workloads.py"))
     mod = importlib.util.module_from_spec(spec)
+    sys.modules[spec.name] = mod  # dataclasses look their module up there
     spec.loader.exec_module(mod)
     return mod
 
