@@ -181,6 +181,7 @@ struct Workspace {
   float* sens;          // [ng] exact sums (pending groups)
   GroupParams* params;  // [2 * ng]: 2g = 2-bit, 2g + 1 = 4-bit
   float4* chunk_tab;    // [ntab_full + 1]: (min, fp32 scale2, fp16 bits of scale2, zero2)
+  uint8_t* sq_pat;      // [ntab_full * 256]: 2nd-order codes of the distinct full chunks
   int32_t* row_counts;  // [M]
   uint8_t* prec;        // [ng] selected precision (copy of group_precision)
   int32_t* order;       // [ng] decided 2-bit, decided 4-bit, then pending groups
@@ -214,6 +215,7 @@ size_t workspace_layout(int64_t M, int64_t K, char* base, Workspace* ws) {
   char* p_sens = take(sizeof(float) * ng);
   char* p_par = take(sizeof(GroupParams) * 2 * ng);
   char* p_ch = take(sizeof(float4) * (cl.ntab_full + 1));
+  char* p_sq = take((size_t)kGroup2 * std::max(1, cl.ntab_full));
   char* p_rc = take(sizeof(int32_t) * M);
   char* p_pr = take(ng);
   char* p_or = take(sizeof(int32_t) * ng);
@@ -237,6 +239,7 @@ size_t workspace_layout(int64_t M, int64_t K, char* base, Workspace* ws) {
     ws->sens = reinterpret_cast<float*>(p_sens);
     ws->params = reinterpret_cast<GroupParams*>(p_par);
     ws->chunk_tab = reinterpret_cast<float4*>(p_ch);
+    ws->sq_pat = reinterpret_cast<uint8_t*>(p_sq);
     ws->row_counts = reinterpret_cast<int32_t*>(p_rc);
     ws->prec = reinterpret_cast<uint8_t*>(p_pr);
     ws->order = reinterpret_cast<int32_t*>(p_or);
@@ -2315,14 +2318,25 @@ __device__ __noinline__ void tables_grid(const QArgs& a, int bid, int G) {
     }
     mn = warp_min(mn);
     mx = warp_max(mx);
+    float sc2 = __fdiv_rn(__fsub_rn(mx, mn), 15.0f);
+    if (sc2 < 1e-10f) sc2 = 1e-10f;
     if (lane == 0) {
-      float sc2 = __fdiv_rn(__fsub_rn(mx, mn), 15.0f);
-      if (sc2 < 1e-10f) sc2 = 1e-10f;
       const int z2 = f2i_rz(roundf(__fdiv_rn(-mn, sc2)));
       if (z2 < -128 || z2 > 127) atomicOr(&a.ws.hdr->status, kStatusZero2Wrap);
       a.ws.chunk_tab[partial ? cl.ntab_full : ci] =
           make_float4(mn, sc2, __int_as_float((int)__half_as_ushort(__float2half_rn(sc2))),
                       __int_as_float((int)(int8_t)z2));
+    }
+    if (!partial) {
+      // the chunk's 256 2nd-order codes (quantize.cu:274-279), in flat order:
+      // every full chunk of the same position in the period has them
+      const int g0 = (int)((cidx * step) % ng);
+      for (int k = lane; k < kGroup2; k += 32) {
+        int g = g0 + k % ng;
+        if (g >= ng) g -= ng;
+        const int q2 = f2i_rz(roundf(__fdiv_rn(__fsub_rn(scale_of(g), mn), sc2)));
+        a.ws.sq_pat[ci * kGroup2 + k] = (uint8_t)max(0, min(15, q2));
+      }
     }
   }
 }
@@ -2800,30 +2814,25 @@ __global__ void __launch_bounds__(kEncThreads, 2)
 // group's parameters); the 2nd-order code of (r, g) takes the chunk table
 // entry of its flat index r ng + g (quantize.cu:245-272), which for rows in
 // full chunks repeats every rp = 256 / gcd(ng, 256) rows: those rows copy
-// one of rp pattern rows built in shared memory, the others compute it.
-// Needs ng % 16 == 0 and 16-byte aligned arrays; `scratch` is shared memory
-// the CTA no longer needs.
+// one of the rp pattern rows the tables kernel wrote once per matrix (each
+// CTA computing them, rp * ng codes, had cost the 4096x11008 encode ~5 M
+// warp instructions), the rows of the partial chunk compute theirs.  Needs
+// ng % 16 == 0 and 16-byte aligned arrays; `scratch` is shared memory the CTA
+// no longer needs (3 ng bytes).
 __device__ __noinline__ void fill_row_arrays(const QArgs& a, int bid, int G, uint8_t* scratch,
                                              size_t scratch_bytes) {
   const int ng = a.ng, tid = threadIdx.x, nt = blockDim.x;
   const int64_t r0 = a.M * bid / G, r1 = a.M * (bid + 1) / G;
   uint16_t* sc = reinterpret_cast<uint16_t*>(scratch);  // [ng] fp16 bits
   int8_t* zr = reinterpret_cast<int8_t*>(scratch + 2 * ng);
-  uint8_t* pat = scratch + 3 * ng;  // [rp][ng]
+  (void)scratch_bytes;  // 3 ng bytes are used
   const int rp = (int)((int64_t)a.cl.period * kGroup2 / ng);
   const int64_t full_rows = a.cl.nfull * kGroup2 / ng;  // rows whose scales lie in full chunks
-  const bool use_pat = (size_t)(3 + rp) * (size_t)ng <= scratch_bytes;
   for (int g = tid; g < ng; g += nt) {
     const GroupParams& p = a.ws.params[2 * g + a.ws.prec[g]];
     sc[g] = (uint16_t)p.scale_h;
     zr[g] = (int8_t)p.zero;
   }
-  __syncthreads();
-  if (use_pat)
-    for (int e = tid; e < rp * ng; e += nt) {
-      const int ph = e / ng, g = e - (e / ng) * ng;
-      pat[e] = sq_direct(a, __half2float(__ushort_as_half(sc[g])), ph, g);
-    }
   __syncthreads();
   const int n = (int)((r1 - r0) * ng);  // elements of the CTA's stretch (below 2^31)
   const int64_t e0 = r0 * ng;
@@ -2837,8 +2846,10 @@ __device__ __noinline__ void fill_row_arrays(const QArgs& a, int bid, int G, uin
     z_out[j] = *reinterpret_cast<const uint4*>(zr + g);
     const int64_t r = r0 + rl;
     uint4 q;
-    if (use_pat && r < full_rows) {
-      q = *reinterpret_cast<const uint4*>(pat + (int)(r % rp) * ng + g);
+    if (r < full_rows) {
+      // row r's codes are those of row r mod rp of the period: the tables
+      // kernel's per-chunk codes in flat order
+      q = __ldg(reinterpret_cast<const uint4*>(a.ws.sq_pat + (int)(r % rp) * ng + g));
     } else {
       uint32_t w[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
