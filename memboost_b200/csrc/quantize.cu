@@ -1438,107 +1438,6 @@ __device__ void enc_partition(const QArgs& a, const uint32_t* s_cost /* nct, or 
   }
 }
 
-// 2nd-order tables, any_irregular and the group_precision output once every
-// group's precision is in ws.prec (quantize.cu:245-272 over the flattened
-// [M, ng] scales).  scales_1st[r, g] depends only on g, so full chunks repeat
-// with period ng / gcd(ng, 256), and a chunk starting at flat index s0 holds
-// the groups s0 mod ng, s0 mod ng + 1, ... cyclically.  With rebuild_order
-// (used when nothing stays pending) the decided / pending counts are reset;
-// otherwise (the selection completed after encode started) `order` and the
-// counts stay as they are.
-template <int NT>
-__device__ void finalize_tables(const QArgs& a, float* s1, size_t s1_bytes, uint32_t* s_wsum,
-                                int* s_irr, bool rebuild_order) {
-  const int ng = a.ng, nct = a.nct;
-  const int tid = threadIdx.x % NT, lane = threadIdx.x & 31, warp = tid >> 5;
-  constexpr int NWARP = NT / 32;
-  (void)s_wsum;
-  const bool s1_in_smem = (size_t)ng * sizeof(float) <= s1_bytes;
-  // encode work of each column tile, after s1 (for the tile split)
-  uint32_t* s_cost = reinterpret_cast<uint32_t*>(s1 + ng);
-  const size_t pref_off = ((size_t)(ng + nct) * sizeof(float) + 7) & ~(size_t)7;
-  long long* s_pref = reinterpret_cast<long long*>(reinterpret_cast<uint8_t*>(s1) + pref_off);
-  const bool cost_in_smem =
-      s1_in_smem && pref_off + (size_t)(nct + 1) * sizeof(long long) <= s1_bytes;
-  if (tid == 0) *s_irr = 0;
-  if (cost_in_smem)
-    for (int ct = tid; ct < nct; ct += NT) s_cost[ct] = 160;
-  sync_nt<NT>();
-  auto scale_from = [&](int g, uint8_t pr) -> float {
-    const uint32_t sh2 = __ldcg(a.ws.gscale + g);
-    return __half2float(__ushort_as_half((uint16_t)(pr ? (sh2 >> 16) : (sh2 & 0xFFFFu))));
-  };
-  int irr = 0;
-  for (int g = tid; g < ng; g += NT) {
-    const uint8_t pr = a.ws.prec[g];
-    a.gp[g] = pr;
-    if (s1_in_smem) s1[g] = scale_from(g, pr);
-    const bool reg = (a.ws.greg[g] >> pr) & 1;
-    irr |= !reg;
-    if (cost_in_smem) atomicAdd(&s_cost[g / kTileGroups], !reg ? 180u : pr ? 54u : 20u);
-  }
-  if (__any_sync(0xffffffffu, irr) && lane == 0) atomicOr(s_irr, 1);
-  sync_nt<NT>();
-  auto scale_of = [&](int g) -> float {
-    return s1_in_smem ? s1[g] : scale_from(g, a.ws.prec[g]);
-  };
-  // Chunk c's scales are the groups s0 mod ng, s0 mod ng + 1, ... (cyclic,
-  // s0 = 256 c; the partial chunk is the last).  Phase 1: one warp per chunk
-  // reduces min / max (into the chunk table's slots); phase 2: one thread per
-  // chunk derives scale / zero.
-  const ChunkLayout& cl = a.cl;
-  const int nchunks = cl.ntab_full + cl.has_partial;
-  const int64_t step = kGroup2 % ng;  // s0 mod ng advances by this per chunk
-  for (int ci = warp; ci < nchunks; ci += NWARP) {
-    const bool partial = ci >= cl.ntab_full;
-    const int64_t cidx = partial ? cl.nfull : ci;
-    const int n = (int)min64(kGroup2, cl.total - cidx * kGroup2);
-    float mn = 1e10f, mx = -1e10f;
-    if (n >= ng) {  // every group at least once
-      for (int g = lane; g < ng; g += 32) {
-        const float v = scale_of(g);
-        mn = fminf(mn, v);
-        mx = fmaxf(mx, v);
-      }
-    } else {
-      // (cidx * 256) mod ng, without a 64-bit division when the product fits
-      const int64_t prod = cidx * step;
-      const int g0 = prod < (int64_t)0xFFFFFFFF ? (int)((uint32_t)prod % (uint32_t)ng)
-                                                : (int)(prod % ng);
-      for (int k = lane; k < n; k += 32) {
-        int g = g0 + k;
-        if (g >= ng) g -= ng;
-        const float v = scale_of(g);
-        mn = fminf(mn, v);
-        mx = fmaxf(mx, v);
-      }
-    }
-    mn = warp_min(mn);
-    mx = warp_max(mx);
-    if (lane == 0) a.ws.chunk_tab[partial ? cl.ntab_full : ci] = make_float4(mn, mx, 0.f, 0.f);
-  }
-  sync_nt<NT>();
-  for (int ci = tid; ci < nchunks; ci += NT) {
-    float4* e = a.ws.chunk_tab + (ci < cl.ntab_full ? ci : cl.ntab_full);
-    const float4 r = __ldcg(e);
-    const float mn = r.x, mx = r.y;
-    float sc2 = __fdiv_rn(__fsub_rn(mx, mn), 15.0f);
-    if (sc2 < 1e-10f) sc2 = 1e-10f;
-    const int z2 = f2i_rz(roundf(__fdiv_rn(-mn, sc2)));
-    if (z2 < -128 || z2 > 127) atomicOr(&a.ws.hdr->status, kStatusZero2Wrap);
-    *e = make_float4(mn, sc2, __int_as_float((int)__half_as_ushort(__float2half_rn(sc2))),
-                     __int_as_float((int)(int8_t)z2));
-  }
-  if (tid == 0) {
-    a.ws.hdr->any_irregular = *s_irr;
-    if (rebuild_order) {
-      a.ws.hdr->n_dec = (uint32_t)ng;
-      a.ws.hdr->n_pend = 0;
-    }
-  }
-  enc_partition<NT>(a, cost_in_smem ? s_cost : nullptr, cost_in_smem ? s_pref : nullptr);
-}
-
 // Interval of a group's fp32 serial sum as sortable keys (lo rounded down,
 // hi rounded up) from its flags, prediction P and moment (M rows of 16
 // terms).  NaN / inf groups are exact.
