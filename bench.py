@@ -734,6 +734,10 @@ def sub_gptq(tokens=262144, reps=2, hessian_only=False):
                                      "peak": pk.get("bf16_tflops"), "unit": "TFLOP/s",
                                      "frac": round(tf / float(pk.get("bf16_tflops", 1590.0)), 4),
                                      "of": f"{kind} bf16_tflops (burst: kernels timed alone)",
+                                     "frac_sustained": round(
+                                         tf / float(pk.get("bf16_tflops_sustained", 1400.0)), 4),
+                                     "sustained_note": "the K = 11008 Hessian runs ~30 ms per "
+                                                       "call, long enough for the power cap",
                                      "flops": "N*K*(K+1) per Hessian (symmetric)"}}}
 
 
