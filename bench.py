@@ -79,8 +79,9 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-sub", action="store_true", help="skip the one-GPU sub-records")
     p.add_argument("--layers", type=int, default=32, help="model layers (32 = the config)")
-    p.add_argument("--per-launch", type=int, default=8,
-                   help="matrices sharing one launch of each quantize kernel (1-8)")
+    p.add_argument("--per-launch", type=int, default=None,
+                   help="matrices sharing one launch of each quantize kernel (1-8; default: 8, "
+                        "fewer when a rank's share would make fewer launch sets than branches)")
     p.add_argument("--branches", type=int, default=8, help="parallel CUDA-graph branches")
     p.add_argument("--only", default=None,
                    choices=("mlp_pair", "single_4096", "gptq_layer", "hessian", "qgemv",
@@ -361,6 +362,10 @@ def run_ours(args, ws, rank, local):
     clk = ClockSampler(local)
     shapes = model_shapes(args.layers, wl)
     mine = shard.lpt_partition([M * K for _, M, K, _ in shapes], ws)[rank]
+    if args.per_launch is None:
+        # 8 matrices per launch set, but at least one set per graph branch, so
+        # that a set's serial kernel chain overlaps others at 4-8 GPUs too
+        args.per_launch = max(1, min(8, len(mine) // max(1, args.branches)))
     cases = [wl.llama7b_matrix(shapes[i][0], shapes[i][1], shapes[i][2], shapes[i][3],
                                device=dev) for i in mine]
     batch = _C.QuantizeBatch([c.weights for c in cases], [c.ratio_4bit for c in cases],
